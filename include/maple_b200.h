@@ -1,0 +1,192 @@
+/*
+ * maple-b200: C ABI of the B200 (sm_100a) decode kernels for packed ternary
+ * MoE language models.
+ *
+ * Every entry point takes raw device pointers, element strides, dtype enums
+ * and a cudaStream_t passed as void*, launches asynchronously on that stream
+ * and returns a status code (0 = ok, see maple_status).  Nothing here
+ * allocates device memory: scratch space is passed in by the caller, sized by
+ * the matching *_workspace_bytes() query, and must be zero-filled once before
+ * its first use (kernels leave it zeroed again when they finish).
+ *
+ * Each declaration names the reference operator it replaces
+ * (cloud-000/maple-flash-dgx-spark, paths relative to src/maple_run/).
+ */
+#ifndef MAPLE_B200_H
+#define MAPLE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum maple_status {
+  MAPLE_OK = 0,
+  MAPLE_ERR_SHAPE = 1,     /* shape/size argument invalid        (ValueError)   */
+  MAPLE_ERR_DTYPE = 2,     /* dtype not supported                 (TypeError)    */
+  MAPLE_ERR_BOUNDS = 3,    /* index outside its buffer            (ValueError)   */
+  MAPLE_ERR_TIMEOUT = 4,   /* bounded device wait gave up         (RuntimeError) */
+  MAPLE_ERR_CUDA = 5,      /* CUDA launch/runtime error           (RuntimeError) */
+  MAPLE_ERR_WORKSPACE = 6, /* workspace missing or too small      (ValueError)   */
+  MAPLE_ERR_ALIGN = 7      /* pointer not 16-byte aligned         (ValueError)   */
+};
+
+enum maple_dtype { MAPLE_F32 = 0, MAPLE_BF16 = 1 };
+
+/* ------------------------------------------------------------------------
+ * Ternary GEMV / small-batch GEMM.
+ * Replaces kernels/ternary_gemv.py:261 ternary_gemv(x, packed_weight,
+ * row_alpha, *, rms_weight=None, rms_eps=1e-6) and linear.py:16-41
+ * PackedTernaryLinear.forward.
+ *
+ *   y[b, n] = alpha[n] * rstd_b * sum_k (code[n,k] - 1) * x[b,k] * rms_w[k]
+ *
+ * x: [batch, k] (row stride x_row_stride elements), dtype x_dtype.
+ * codes: uint32 [n, k/16] contiguous, 16-byte aligned, reference layout.
+ * alpha: [n]; rms_w: [k] or NULL (no fused RMSNorm, rstd = 1).
+ * y: [batch, n] in x_dtype (row stride y_row_stride).  k % 64 == 0, k <= 8192.
+ * ------------------------------------------------------------------------ */
+int64_t maple_ternary_gemv_workspace_bytes(int64_t batch, int64_t n, int64_t k);
+int maple_ternary_gemv(const void* x, int x_dtype, int64_t batch, int64_t k, int64_t x_row_stride,
+                       const uint32_t* codes, int64_t n, const void* alpha, int alpha_dtype,
+                       const void* rms_w, int rms_dtype, float eps, void* y, int64_t y_row_stride,
+                       void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Selected-expert GEMV.  Replaces kernels/ternary_expert.py:125
+ * ternary_expert_gemv and linear.py:51 PackedTernaryExperts.forward.
+ * Slot z uses expert expert_ids[z] (rows of codes [n_experts, n, k/16]) and
+ * activation row z / x_rows_per_token.  y: [slots, n].  An out-of-range
+ * expert id produces NaN rows. */
+int64_t maple_ternary_expert_gemv_workspace_bytes(int64_t slots, int64_t n, int64_t k);
+int maple_ternary_expert_gemv(const void* x, int x_dtype, int64_t x_row_stride, int64_t x_rows_per_token,
+                              const int32_t* expert_ids, int64_t slots, int64_t k, const uint32_t* codes,
+                              int64_t n_experts, int64_t n, const void* alpha, int alpha_dtype, void* y,
+                              int64_t y_row_stride, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Fused up|gate GEMV + clamp + SiLU.  Replaces kernels/ternary_expert.py:403
+ * ternary_expert_swiglu and linear.py:55 PackedTernaryExperts.swiglu.
+ * codes [n_experts, 2*inter, k/16] (rows [0, inter) up, [inter, 2*inter) gate),
+ * expert_ids [tokens, topk]; y [tokens*topk, inter]:
+ *   y = clamp(up, -7, 7) * min(gate, 7) * sigmoid(min(gate, 7)). */
+int64_t maple_ternary_expert_swiglu_workspace_bytes(int64_t slots, int64_t inter, int64_t k);
+int maple_ternary_expert_swiglu(const void* x, int x_dtype, int64_t x_row_stride, const int32_t* expert_ids,
+                                int64_t tokens, int64_t topk, int64_t k, const uint32_t* codes,
+                                int64_t n_experts, int64_t inter, const void* alpha, int alpha_dtype, void* y,
+                                int64_t y_row_stride, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Down projection of every top-k slot fused with the weighted combine and the
+ * residual add.  maple_ternary_expert_down_reduce has the reference model's
+ * rounding (kernels/ternary_expert.py:125 down GEMV with bf16 expert outputs,
+ * then kernels/fused_norm.py:164 moe_reduce_add, as called at model.py:471-473);
+ * maple_ternary_expert_down_sum replaces kernels/ternary_expert.py:471
+ * ternary_expert_down_sum and linear.py:59 PackedTernaryExperts.down_sum.
+ * h: [tokens, topk, k] (strides h_tok_stride, h_slot_stride); ids/wt
+ * [tokens, topk]; codes [n_experts, n, k/16]; residual [tokens, n] or NULL;
+ * out [tokens, n].  topk <= 8, k <= 2048. */
+int maple_ternary_expert_down_reduce(const void* h, int h_dtype, int64_t h_tok_stride, int64_t h_slot_stride,
+                                     const int32_t* ids, const float* wt, int64_t tokens, int64_t topk,
+                                     int64_t k, const uint32_t* codes, int64_t n_experts, int64_t n,
+                                     const void* alpha, int alpha_dtype, const void* residual,
+                                     int64_t res_stride, void* out, int64_t out_stride, void* stream);
+int maple_ternary_expert_down_sum(const void* h, int h_dtype, int64_t h_tok_stride, int64_t h_slot_stride,
+                                  const int32_t* ids, const float* wt, int64_t tokens, int64_t topk, int64_t k,
+                                  const uint32_t* codes, int64_t n_experts, int64_t n, const void* alpha,
+                                  int alpha_dtype, const void* residual, int64_t res_stride, void* out,
+                                  int64_t out_stride, void* stream);
+
+/* y = sum_s w[t,s] * x[t,s,:] (+ residual).  Replaces kernels/fused_norm.py:164
+ * moe_reduce_add. */
+int maple_moe_reduce_add(const void* x, int x_dtype, int64_t x_tok_stride, int64_t x_slot_stride,
+                         const float* wt, int64_t tokens, int64_t topk, int64_t n, const void* residual,
+                         int64_t res_stride, void* y, int64_t y_stride, void* stream);
+
+/* Router: logits = x . gate^T, softmax, top-k (ties -> lowest index),
+ * weights renormalised by 1/(sum + 1e-20).  Replaces kernels/router.py:141
+ * router_topk.  idx int32 / wt fp32 [tokens, topk].  n_experts <= 256. */
+int64_t maple_router_topk_workspace_bytes(int64_t tokens, int64_t n_experts);
+int maple_router_topk(const void* x, int x_dtype, int64_t x_row_stride, int64_t tokens, int64_t k,
+                      const void* gate, int gate_dtype, int64_t n_experts, int64_t topk, int32_t* idx,
+                      float* wt, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* RMSNorm and residual add + RMSNorm.  Replace kernels/fused_norm.py:105
+ * rms_norm and :128 add_rms_norm (residual = x + y, out = norm(residual)). */
+int maple_rms_norm(const void* x, int x_dtype, int64_t rows, int64_t n, int64_t x_row_stride, const void* w,
+                   int w_dtype, float eps, void* out, int64_t out_row_stride, void* stream);
+int maple_add_rms_norm(const void* x, const void* y, int x_dtype, int64_t rows, int64_t n, int64_t x_row_stride,
+                       int64_t y_row_stride, const void* w, int w_dtype, float eps, void* residual,
+                       int64_t residual_row_stride, void* out, int64_t out_row_stride, void* stream);
+
+/* Per-head QK RMSNorm + RoPE (rotate-half on the first rotary_dim dims) and
+ * K/V store at seqlen[b] of cache row row_map[b] (identity when NULL).
+ * Replaces kernels/decode_attn.py:362 apply_qkv_decode.  qkv [batch,
+ * (H + 2*Hkv)*D]; caches [cache_batch, Hkv, max_len, D] with D contiguous;
+ * q_out [batch, H, D].  An out-of-range position or cache row skips the
+ * store and sets bit 2 of *err. */
+int maple_apply_qkv_decode(const void* qkv, int x_dtype, int64_t batch, int64_t qkv_row_stride,
+                           const void* q_weight, const void* k_weight, int w_dtype, const void* cos,
+                           const void* sin, int cs_dtype, int64_t cs_row_stride, void* q_out, int64_t q_sb,
+                           int64_t q_sh, void* k_cache, void* v_cache, int64_t cache_batch, int64_t cache_sb,
+                           int64_t cache_sh, int64_t max_len, const int64_t* seqlen, const int32_t* row_map,
+                           int64_t num_heads, int64_t num_kv_heads, int64_t head_dim, int64_t rotary_dim,
+                           int use_rope, float eps, int* err, void* stream);
+
+/* GQA decode attention over [start, seqlen[b] + 1) split in chunks of
+ * split_len positions with an in-kernel log-sum-exp merge.  Replaces
+ * kernels/decode_attn.py:470 decode_gqa_attn.  head_dim in {64,128,256},
+ * H/Hkv <= 8, split_len in {32,64,128}.  A bounded wait that gives up sets
+ * bit 1 of *err. */
+int64_t maple_decode_gqa_workspace_bytes(int64_t batch, int64_t num_heads, int64_t head_dim, int64_t max_len,
+                                         int64_t split_len);
+int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, int64_t num_heads, int64_t q_sb,
+                          int64_t q_sh, const void* k_cache, const void* v_cache, int64_t cache_batch,
+                          int64_t num_kv_heads, int64_t cache_sb, int64_t cache_sh, int64_t max_len,
+                          int64_t head_dim, const int64_t* seqlen, const int32_t* row_map, float scale,
+                          int64_t window, int64_t split_len, void* out, int64_t o_sb, int64_t o_sh,
+                          void* workspace, int64_t workspace_bytes, int* err, void* stream);
+
+/* RTN-4 GEMV y = x . (scale*code + bias)^T per group.  Replaces
+ * kernels/rtn4.py:285 rtn4_gemv and linear.py:72 PackedRTN4Linear.  codes
+ * uint32 [n, k/8] (8 LSB-first 4-bit codes per word); scales/biases
+ * [n, k/group_size]; biases NULL means symmetric (bias = -8 * scale).
+ * group_size 64 or a multiple of 128. */
+int maple_rtn4_gemv(const void* x, int x_dtype, int64_t batch, int64_t k, int64_t x_row_stride,
+                    const uint32_t* codes, int64_t n, const void* scales, const void* biases, int s_dtype,
+                    int64_t group_size, void* y, int64_t y_row_stride, void* stream);
+
+/* RTN-4 GEMV over rows head[cluster_ids[r / C], r % C] (FlashHead probes).
+ * Replaces kernels/rtn4.py:514 rtn4_indexed_gemv. */
+int maple_rtn4_indexed_gemv(const void* x, int x_dtype, int64_t batch, int64_t k, int64_t x_row_stride,
+                            const uint32_t* codes, int64_t n_clusters, int64_t cluster_size,
+                            const void* scales, const void* biases, int s_dtype, int64_t group_size,
+                            const int32_t* cluster_ids, int64_t n_probes, void* y, int64_t y_row_stride,
+                            void* stream);
+
+/* Greedy next token (first index of the max).  Replaces the argmax of
+ * generate.py:147-148 / :806-808. */
+int64_t maple_argmax_workspace_bytes(int64_t batch, int64_t vocab);
+int maple_argmax(const void* logits, int x_dtype, int64_t batch, int64_t vocab, int64_t row_stride,
+                 int64_t* out, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Fused top-k / temperature / top-p sampler with a caller-supplied uniform
+ * per row.  Replaces kernels/sampler.py:106 fused_sample and :152
+ * fused_sample_batched.  top_k <= 64. */
+int64_t maple_fused_sample_workspace_bytes(int64_t batch, int64_t vocab, int64_t top_k);
+int maple_fused_sample(const void* logits, int x_dtype, int64_t batch, int64_t vocab, int64_t row_stride,
+                       const float* uniform, float temperature, float top_p, int64_t top_k, int64_t* out,
+                       void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Embedding gather (plain table) and RTN-4 gather + dequant.  Replace
+ * kernels/rtn4.py:27 rtn4_embedding / linear.py:95 PackedRTN4Embedding.  An
+ * out-of-range id writes zeros and sets bit 2 of *err. */
+int maple_embedding(const int64_t* ids, int64_t batch, const void* table, int t_dtype, int64_t vocab,
+                    int64_t hidden, void* out, int out_dtype, int64_t out_row_stride, int* err, void* stream);
+int maple_rtn4_embedding(const int64_t* ids, int64_t batch, const uint32_t* codes, const void* scales,
+                         const void* biases, int s_dtype, int64_t vocab, int64_t hidden, int64_t group_size,
+                         void* out, int out_dtype, int64_t out_row_stride, int* err, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAPLE_B200_H */

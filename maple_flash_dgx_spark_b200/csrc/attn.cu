@@ -1,0 +1,431 @@
+// Decode attention: per-head QK RMSNorm + RoPE + KV-cache store, and GQA
+// flash-decode split along the sequence with an in-kernel log-sum-exp merge.
+//
+// Reference: kernels/decode_attn.py:362-439 (apply_qkv_decode, kernel
+// :64-163) and :470-592 (decode_gqa_attn, kernels :166-359; split count
+// gqa_splits :446-467).
+//
+// Canonical arithmetic (mirrored by the CPU oracle):
+//   head RMS      sum of squares in R128 order, x_hat = (x * rstd) * w
+//   RoPE          lo' = x_lo*cos_lo + (-x_hi)*sin_lo,  hi' = x_hi*cos_hi + x_lo*sin_hi
+//   scores        s_gt = R128 dot(q_g, k_t) * scale
+//   split         positions [start + s*P, ...) in chunks of P (the caller's
+//                 split length); per split m = max_t s, p_t = exp(s_t - m),
+//                 l = R128 sum of p_t over the split's positions,
+//                 acc_d = sequential fmaf over t of bf16(p_t) * v_td
+//   merge         w_s = exp(m_s - max m), out = (fmaf-chain w_s*acc_s) /
+//                 (fmaf-chain w_s*l_s), sequential over splits
+// K/V tiles of a split are staged in shared memory with cp.async.bulk (TMA
+// bulk copy) completing on an mbarrier; the wait is bounded and a timeout is
+// reported through the error word instead of hanging.
+#include "common.cuh"
+
+namespace mb {
+
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned phase) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr int kWaitSpins = 1 << 22;
+constexpr int kErrFlagTimeout = 1;
+constexpr int kErrFlagBounds = 2;
+
+// ------------------------------------------------------ QK norm + RoPE ----
+struct QkvParams {
+  const void* qkv;        // [B, (Hq + 2*Hkv) * D]
+  const void* q_w;        // [D]
+  const void* k_w;        // [D]
+  const void* cos;        // [B, R]
+  const void* sin;        // [B, R]
+  void* q_out;            // [B, Hq, D]
+  void* kc;               // [Bc, Hkv, T, D]
+  void* vc;
+  const int64_t* seqlen;  // [B]
+  const int32_t* row_map; // [B] or nullptr
+  int* err;
+  int64_t qkv_sb, cs_sb, q_sb, q_sh, kc_sb, kc_sh, vc_sb, vc_sh;
+  int Hq, Hkv, D, R, Bc, T;
+  int use_rope;
+  float eps;
+};
+
+template <int XT, int WT, int CT>
+__global__ void __launch_bounds__(32) qk_norm_rope_store_kernel(QkvParams p) {
+  __shared__ float xh[256];
+  const int lane = threadIdx.x;
+  const int head = blockIdx.x, b = blockIdx.y;
+  const int D = p.D;
+  const char* row = static_cast<const char*>(p.qkv) + b * p.qkv_sb * (XT == kBF16 ? 2 : 4);
+  const int64_t pos = p.seqlen[b];
+  int cb = b;
+  if (p.row_map != nullptr) cb = p.row_map[b];
+  const bool store_ok = pos >= 0 && pos < p.T && cb >= 0 && cb < p.Bc;
+  if (head >= p.Hq && !store_ok) {
+    if (lane == 0) atomicOr(p.err, kErrFlagBounds);
+    return;
+  }
+  if (head >= p.Hq + p.Hkv) {  // V: raw copy into the cache
+    const int base = (p.Hq + p.Hkv) * D + (head - p.Hq - p.Hkv) * D;
+    char* dst = static_cast<char*>(p.vc) + (cb * p.vc_sb + (head - p.Hq - p.Hkv) * p.vc_sh + pos * D) * (XT == kBF16 ? 2 : 4);
+    for (int d = lane; d < D; d += 32) store_f<XT>(dst, d, load_f<XT>(row, base + d));
+    return;
+  }
+  const bool is_q = head < p.Hq;
+  const int base = is_q ? head * D : p.Hq * D + (head - p.Hq) * D;
+  const void* w = is_q ? p.q_w : p.k_w;
+  float part[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int u = 0; u * 32 < D; ++u) {
+    const int d = lane + 32 * u;
+    const float v = load_f<XT>(row, base + d);
+    xh[d] = v;
+    part[u & 3] = __fmaf_rn(v, v, part[u & 3]);
+  }
+  const float rstd = rstd_of(r128_lane_finish(part[0], part[1], part[2], part[3]), D, p.eps);
+  for (int u = 0; u * 32 < D; ++u) {
+    const int d = lane + 32 * u;
+    xh[d] = __fmul_rn(__fmul_rn(xh[d], rstd), load_f<WT>(w, d));
+  }
+  __syncwarp();
+  const char* cs = static_cast<const char*>(p.cos) + b * p.cs_sb * (CT == kBF16 ? 2 : 4);
+  const char* sn = static_cast<const char*>(p.sin) + b * p.cs_sb * (CT == kBF16 ? 2 : 4);
+  const int half = p.R / 2;
+  char* dst;
+  if (is_q)
+    dst = static_cast<char*>(p.q_out) + (b * p.q_sb + head * p.q_sh) * (XT == kBF16 ? 2 : 4);
+  else
+    dst = static_cast<char*>(p.kc) + (cb * p.kc_sb + (head - p.Hq) * p.kc_sh + pos * D) * (XT == kBF16 ? 2 : 4);
+  for (int d = lane; d < D; d += 32) {
+    float o = xh[d];
+    if (p.use_rope && d < p.R) {
+      if (d < half) {
+        o = __fadd_rn(__fmul_rn(xh[d], load_f<CT>(cs, d)), __fmul_rn(-xh[d + half], load_f<CT>(sn, d)));
+      } else {
+        o = __fadd_rn(__fmul_rn(xh[d], load_f<CT>(cs, d)), __fmul_rn(xh[d - half], load_f<CT>(sn, d)));
+      }
+    }
+    store_f<XT>(dst, d, o);
+  }
+}
+
+// ---------------------------------------------------------- GQA decode ----
+struct AttnParams {
+  const void* q;          // [B, Hq, D]
+  const void* kc;         // [Bc, Hkv, T, D]
+  const void* vc;
+  const int64_t* seqlen;  // [B]
+  const int32_t* row_map; // [B] or nullptr
+  void* out;              // [B, Hq, D]
+  float* ws_acc;          // [B, Hq, NS, D]
+  float* ws_ml;           // [B, Hq, NS, 2]
+  unsigned* tickets;      // [B * Hkv]
+  int* err;
+  int64_t q_sb, q_sh, kc_sb, kc_sh, vc_sb, vc_sh, o_sb, o_sh;
+  int Hq, Hkv, G, Bc, T, P, NS, window;
+  float scale;
+};
+
+template <int XT, int D>
+__global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
+  constexpr int U = D / 32;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t bar;
+  __shared__ float s_m[8], s_l[8];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int P = p.P, G = p.G;
+  const int es = XT == kBF16 ? 2 : 4;
+
+  const int64_t pos = p.seqlen[b];
+  const int kv_len = (int)min(pos + 1, (int64_t)p.T);
+  const int start = p.window > 0 ? max(0, kv_len - p.window) : 0;
+  const int ns = kv_len > start ? (kv_len - start + P - 1) / P : 0;
+  if (s >= ns) return;
+  const int t0 = start + s * P;
+  const int n = min(P, kv_len - t0);
+  int cb = b;
+  if (p.row_map != nullptr) cb = p.row_map[b];
+  if (cb < 0 || cb >= p.Bc) {
+    if (tid == 0) atomicOr(p.err, kErrFlagBounds);
+    cb = 0;
+  }
+
+  unsigned char* ktile = smem;
+  unsigned char* vtile = smem + (size_t)P * D * es;
+  float* scores = reinterpret_cast<float*>(smem + 2 * (size_t)P * D * es);  // [8][P]
+  float* pb = scores + 8 * P;                                                 // [8][P]
+
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    const unsigned bytes = (unsigned)(n * D * es);
+    mbar_expect_tx(&bar, 2 * bytes);
+    const char* ksrc = static_cast<const char*>(p.kc) + (cb * p.kc_sb + h * p.kc_sh + (int64_t)t0 * D) * es;
+    const char* vsrc = static_cast<const char*>(p.vc) + (cb * p.vc_sb + h * p.vc_sh + (int64_t)t0 * D) * es;
+    bulk_g2s(ktile, ksrc, bytes, &bar);
+    bulk_g2s(vtile, vsrc, bytes, &bar);
+  }
+  // q of the group's heads while the copies are in flight.
+  float qv[8][U];
+#pragma unroll
+  for (int g = 0; g < 8; ++g)
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      qv[g][u] = g < G ? load_f<XT>(static_cast<const char*>(p.q) + (b * p.q_sb + (h * G + g) * p.q_sh) * es,
+                                    lane + 32 * u)
+                       : 0.0f;
+  __syncthreads();  // barrier initialised before anyone waits on it
+  bool ready = false;
+  for (int i = 0; i < kWaitSpins && !ready; ++i) ready = mbar_try_wait(&bar, 0);
+  if (!ready) {
+    if (tid == 0) atomicOr(p.err, kErrFlagTimeout);
+    for (int i = 0; i < kWaitSpins && !ready; ++i) ready = mbar_try_wait(&bar, 0);
+    return;
+  }
+
+  // Scores: warp w takes position groups of 4; 32 (position, head) partials
+  // per lane reduced with a transposing butterfly (lane l ends with element l).
+  for (int grp = warp; grp * 4 < n; grp += 4) {
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = grp * 4 + i;
+      float kk[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) kk[u] = t < n ? load_f<XT>(ktile + (size_t)t * D * es, lane + 32 * u) : 0.0f;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        float pj[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int u = 0; u < U; ++u) pj[u & 3] = __fmaf_rn(qv[g][u], kk[u], pj[u & 3]);
+        v[i * 8 + g] = __fadd_rn(__fadd_rn(__fadd_rn(pj[0], pj[1]), pj[2]), pj[3]);
+      }
+    }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+      const bool upper = (lane & m) != 0;
+#pragma unroll
+      for (int i = 0; i < m; ++i) {
+        const float keep = upper ? v[i + m] : v[i];
+        const float send = upper ? v[i] : v[i + m];
+        v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
+      }
+    }
+    const int t = grp * 4 + (lane >> 3), g = lane & 7;
+    if (t < n && g < G) scores[g * P + t] = __fmul_rn(v[0], p.scale);
+  }
+  __syncthreads();
+
+  // Softmax statistics of this split, one warp per head.
+  const float ninf = __int_as_float(0xff800000);
+  for (int g = warp; g < G; g += 4) {
+    float sv[4];
+    float m = ninf;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = lane + 32 * u;
+      sv[u] = (t < n) ? scores[g * P + t] : ninf;
+      m = fmaxf(m, sv[u]);
+    }
+    m = warp_max(m);
+    float pp[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = lane + 32 * u;
+      pp[u] = (t < n) ? mexp(__fsub_rn(sv[u], m)) : 0.0f;
+      if (t < P) pb[g * P + t] = (t < n) ? bf16_to_f32(f32_to_bf16(pp[u])) : 0.0f;
+    }
+    const float l = r128_lane_finish(pp[0], pp[1], pp[2], pp[3]);
+    if (lane == 0) { s_m[g] = m; s_l[g] = l; }
+  }
+  __syncthreads();
+
+  // P.V with the bf16-rounded probabilities, sequential over positions.
+  for (int g = warp; g < G; g += 4) {
+    float acc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) acc[u] = 0.0f;
+    for (int t = 0; t < n; ++t) {
+      const float pt = pb[g * P + t];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        acc[u] = __fmaf_rn(pt, load_f<XT>(vtile + (size_t)t * D * es, lane + 32 * u), acc[u]);
+    }
+    const int hq = h * G + g;
+    if (ns == 1) {
+      char* o = static_cast<char*>(p.out) + (b * p.o_sb + hq * p.o_sh) * es;
+#pragma unroll
+      for (int u = 0; u < U; ++u) store_f<XT>(o, lane + 32 * u, __fdiv_rn(acc[u], s_l[g]));
+    } else {
+      float* wa = p.ws_acc + (((int64_t)b * p.Hq + hq) * p.NS + s) * D;
+#pragma unroll
+      for (int u = 0; u < U; ++u) wa[lane + 32 * u] = acc[u];
+      if (lane == 0) {
+        float* wml = p.ws_ml + (((int64_t)b * p.Hq + hq) * p.NS + s) * 2;
+        wml[0] = s_m[g];
+        wml[1] = s_l[g];
+      }
+    }
+  }
+  if (ns == 1) return;
+
+  // Last split of (b, h) merges all splits in split order.
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    unsigned* tk = p.tickets + (int64_t)b * p.Hkv + h;
+    const unsigned old = atomicAdd(tk, 1u);
+    s_last = (old == static_cast<unsigned>(ns - 1));
+    if (s_last) atomicExch(tk, 0u);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int idx = tid; idx < G * D; idx += 128) {
+    const int g = idx / D, d = idx - (idx / D) * D;
+    const int hq = h * G + g;
+    const float* ml = p.ws_ml + ((int64_t)b * p.Hq + hq) * p.NS * 2;
+    const float* ac = p.ws_acc + ((int64_t)b * p.Hq + hq) * p.NS * D;
+    float M = ninf;
+    for (int j = 0; j < ns; ++j) M = fmaxf(M, __ldcg(ml + 2 * j));
+    float num = 0.0f, den = 0.0f;
+    for (int j = 0; j < ns; ++j) {
+      const float w = mexp(__fsub_rn(__ldcg(ml + 2 * j), M));
+      num = __fmaf_rn(w, __ldcg(ac + (int64_t)j * D + d), num);
+      den = __fmaf_rn(w, __ldcg(ml + 2 * j + 1), den);
+    }
+    store_f<XT>(static_cast<char*>(p.out) + (b * p.o_sb + hq * p.o_sh) * es, d, __fdiv_rn(num, den));
+  }
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+constexpr int kAttnTicketBytes = 64 * 1024;
+
+extern "C" int maple_apply_qkv_decode(const void* qkv, int x_dtype, int64_t batch, int64_t qkv_row_stride,
+                                      const void* q_weight, const void* k_weight, int w_dtype,
+                                      const void* cos, const void* sin, int cs_dtype, int64_t cs_row_stride,
+                                      void* q_out, int64_t q_sb, int64_t q_sh, void* k_cache, void* v_cache,
+                                      int64_t cache_batch, int64_t cache_sb, int64_t cache_sh,
+                                      int64_t max_len, const int64_t* seqlen, const int32_t* row_map,
+                                      int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                                      int64_t rotary_dim, int use_rope, float eps, int* err, void* stream) {
+  if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0) return kErrShape;
+  if (batch == 0) return kOk;
+  if (head_dim % 32 != 0 || head_dim > 256 || rotary_dim < 0 || rotary_dim > head_dim || (rotary_dim & 1))
+    return kErrShape;
+  if (x_dtype != kF32 && x_dtype != kBF16) return kErrDtype;
+  if ((w_dtype != kF32 && w_dtype != kBF16) || (cs_dtype != kF32 && cs_dtype != kBF16)) return kErrDtype;
+  if (!qkv || !q_weight || !k_weight || !q_out || !k_cache || !v_cache || !seqlen || !err) return kErrShape;
+  if (use_rope && (!cos || !sin)) return kErrShape;
+  QkvParams p{};
+  p.qkv = qkv; p.q_w = q_weight; p.k_w = k_weight; p.cos = cos; p.sin = sin; p.q_out = q_out;
+  p.kc = k_cache; p.vc = v_cache; p.seqlen = seqlen; p.row_map = row_map; p.err = err;
+  p.qkv_sb = qkv_row_stride; p.cs_sb = cs_row_stride; p.q_sb = q_sb; p.q_sh = q_sh;
+  p.kc_sb = cache_sb; p.kc_sh = cache_sh; p.vc_sb = cache_sb; p.vc_sh = cache_sh;
+  p.Hq = (int)num_heads; p.Hkv = (int)num_kv_heads; p.D = (int)head_dim; p.R = (int)rotary_dim;
+  p.Bc = (int)cache_batch; p.T = (int)max_len; p.use_rope = use_rope; p.eps = eps;
+  dim3 grid((unsigned)(num_heads + 2 * num_kv_heads), (unsigned)batch);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define MB_QKV(XT, WT, CT) qk_norm_rope_store_kernel<XT, WT, CT><<<grid, 32, 0, st>>>(p)
+  if (x_dtype == kBF16) {
+    if (w_dtype == kBF16) { if (cs_dtype == kBF16) MB_QKV(kBF16, kBF16, kBF16); else MB_QKV(kBF16, kBF16, kF32); }
+    else { if (cs_dtype == kBF16) MB_QKV(kBF16, kF32, kBF16); else MB_QKV(kBF16, kF32, kF32); }
+  } else {
+    if (w_dtype == kBF16) { if (cs_dtype == kBF16) MB_QKV(kF32, kBF16, kBF16); else MB_QKV(kF32, kBF16, kF32); }
+    else { if (cs_dtype == kBF16) MB_QKV(kF32, kF32, kBF16); else MB_QKV(kF32, kF32, kF32); }
+  }
+#undef MB_QKV
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+extern "C" int64_t maple_decode_gqa_workspace_bytes(int64_t batch, int64_t num_heads, int64_t head_dim,
+                                                    int64_t max_len, int64_t split_len) {
+  if (split_len <= 0) return -1;
+  const int64_t ns = (max_len + split_len - 1) / split_len;
+  return kAttnTicketBytes + batch * num_heads * ns * (head_dim + 2) * (int64_t)sizeof(float);
+}
+
+extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, int64_t num_heads,
+                                     int64_t q_sb, int64_t q_sh, const void* k_cache, const void* v_cache,
+                                     int64_t cache_batch, int64_t num_kv_heads, int64_t cache_sb,
+                                     int64_t cache_sh, int64_t max_len, int64_t head_dim,
+                                     const int64_t* seqlen, const int32_t* row_map, float scale,
+                                     int64_t window, int64_t split_len, void* out, int64_t o_sb,
+                                     int64_t o_sh, void* workspace, int64_t workspace_bytes, int* err,
+                                     void* stream) {
+  if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_len <= 0) return kErrShape;
+  if (batch == 0) return kOk;
+  if (num_heads % num_kv_heads != 0 || num_heads / num_kv_heads > 8) return kErrShape;
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return kErrShape;
+  if (split_len != 32 && split_len != 64 && split_len != 128) return kErrShape;
+  if (x_dtype != kF32 && x_dtype != kBF16) return kErrDtype;
+  if (!q || !k_cache || !v_cache || !seqlen || !out || !err) return kErrShape;
+  const int es = x_dtype == kBF16 ? 2 : 4;
+  if ((reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15) ||
+      ((cache_sb * es) & 15) || ((cache_sh * es) & 15))
+    return kErrAlign;
+  const int64_t ns = (max_len + split_len - 1) / split_len;
+  if (batch * num_kv_heads * (int64_t)sizeof(unsigned) > kAttnTicketBytes || ns > 65535 || batch > 65535)
+    return kErrShape;
+  if (ns > 1 && (!workspace || workspace_bytes < maple_decode_gqa_workspace_bytes(batch, num_heads, head_dim,
+                                                                                  max_len, split_len)))
+    return kErrWorkspace;
+  AttnParams p{};
+  p.q = q; p.kc = k_cache; p.vc = v_cache; p.seqlen = seqlen; p.row_map = row_map; p.out = out; p.err = err;
+  p.tickets = static_cast<unsigned*>(workspace);
+  p.ws_acc = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kAttnTicketBytes) : nullptr;
+  p.ws_ml = p.ws_acc ? p.ws_acc + batch * num_heads * ns * head_dim : nullptr;
+  p.q_sb = q_sb; p.q_sh = q_sh; p.kc_sb = cache_sb; p.kc_sh = cache_sh; p.vc_sb = cache_sb; p.vc_sh = cache_sh;
+  p.o_sb = o_sb; p.o_sh = o_sh;
+  p.Hq = (int)num_heads; p.Hkv = (int)num_kv_heads; p.G = (int)(num_heads / num_kv_heads);
+  p.Bc = (int)cache_batch; p.T = (int)max_len; p.P = (int)split_len; p.NS = (int)ns;
+  p.window = (int)window; p.scale = scale;
+  const size_t smem = 2 * (size_t)split_len * head_dim * es + 2 * 8 * (size_t)split_len * sizeof(float);
+  dim3 grid((unsigned)ns, (unsigned)num_kv_heads, (unsigned)batch);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+#define MB_ATT(XT, DD)                                                                        \
+  do {                                                                                        \
+    auto kern = gqa_decode_kernel<XT, DD>;                                                    \
+    if (smem > 48 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (e == cudaSuccess) kern<<<grid, 128, smem, st>>>(p);                                   \
+  } while (0)
+  if (x_dtype == kBF16) {
+    if (head_dim == 64) MB_ATT(kBF16, 64); else if (head_dim == 128) MB_ATT(kBF16, 128); else MB_ATT(kBF16, 256);
+  } else {
+    if (head_dim == 64) MB_ATT(kF32, 64); else if (head_dim == 128) MB_ATT(kF32, 128); else MB_ATT(kF32, 256);
+  }
+#undef MB_ATT
+  if (e != cudaSuccess) return kErrCuda;
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}

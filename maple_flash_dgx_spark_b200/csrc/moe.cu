@@ -1,0 +1,368 @@
+// MoE router and expert combine.
+//
+// router_topk      reference kernels/router.py:141-217 (kernels :20-126)
+// expert down+sum  reference kernels/ternary_expert.py:125-234 (down GEMV) followed
+//                  by kernels/fused_norm.py:164-202 (moe_reduce_add), fused; and
+//                  ternary_expert_down_sum (ternary_expert.py:471-556)
+// moe_reduce_add   reference kernels/fused_norm.py:164-202
+#include "fxa.cuh"
+
+namespace mb {
+
+constexpr int kTicketBytesMoe = 64 * 1024;
+
+// ----------------------------------------------------------------- router --
+// Logits: one warp per (token, expert), R128 order over K (products x*g added
+// with fmaf).  The last CTA of a token (ticket) runs softmax, top-k by
+// repeated argmax (ties -> lowest index), and the 1/(sum+1e-20) renorm.
+struct RouterParams {
+  const void* x;       // [T, K]
+  const void* gate;    // [E, K]
+  int32_t* idx;        // [T, topk]
+  float* wt;           // [T, topk]
+  float* logits;       // [T, E] scratch
+  unsigned* tickets;   // [T]
+  int64_t x_stride;
+  int E, K, topk;
+};
+
+constexpr int kRouterWarps = 8;
+
+template <int XT, int GT>
+__global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
+  __shared__ float s_part[kRouterWarps][128];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tok = blockIdx.y;
+  const int e = blockIdx.x * kRouterWarps + warp;
+  const char* xr = static_cast<const char*>(p.x) + tok * p.x_stride * (XT == kBF16 ? 2 : 4);
+  if (e < p.E) {
+    const char* gr = static_cast<const char*>(p.gate) + (int64_t)e * p.K * (GT == kBF16 ? 2 : 4);
+    // Lane l owns partials j = 4l .. 4l+3 (elements j, j+128, ...).
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int c = 0; c < p.K; c += 128) {
+      const int k = c + 4 * lane;
+      if (k < p.K) {
+        a0 = __fmaf_rn(load_f<XT>(xr, k + 0), load_f<GT>(gr, k + 0), a0);
+        a1 = __fmaf_rn(load_f<XT>(xr, k + 1), load_f<GT>(gr, k + 1), a1);
+        a2 = __fmaf_rn(load_f<XT>(xr, k + 2), load_f<GT>(gr, k + 2), a2);
+        a3 = __fmaf_rn(load_f<XT>(xr, k + 3), load_f<GT>(gr, k + 3), a3);
+      }
+    }
+    float* pp = s_part[warp];
+    pp[4 * lane + 0] = a0; pp[4 * lane + 1] = a1; pp[4 * lane + 2] = a2; pp[4 * lane + 3] = a3;
+    __syncwarp();
+    const float logit = r128_smem_finish(pp, lane);
+    if (lane == 0) p.logits[(int64_t)tok * p.E + e] = logit;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned old = atomicAdd(&p.tickets[tok], 1u);
+    s_last = (old == gridDim.x - 1);
+    if (s_last) atomicExch(&p.tickets[tok], 0u);
+  }
+  __syncthreads();
+  if (!s_last || warp != 0) return;
+  __threadfence();
+  // Softmax + top-k on one warp; lane l holds experts l + 32i.
+  constexpr int kMaxE = 256;
+  float v[kMaxE / 32];
+  const float ninf = __int_as_float(0xff800000);
+  float m = ninf;
+#pragma unroll
+  for (int i = 0; i < kMaxE / 32; ++i) {
+    const int ee = lane + 32 * i;
+    v[i] = ee < p.E ? __ldcg(&p.logits[(int64_t)tok * p.E + ee]) : ninf;
+    m = fmaxf(m, v[i]);
+  }
+  m = warp_max(m);
+  // R128 sum of exp: partial j = expert j, j+128 (sequential).
+  float q0 = 0.f, q1 = 0.f, q2 = 0.f, q3 = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxE / 32; ++i) {
+    const int ee = lane + 32 * i;
+    v[i] = ee < p.E ? mexp(__fsub_rn(v[i], m)) : 0.0f;
+    const int j = (i & 3);
+    if (j == 0) q0 = __fadd_rn(q0, v[i]);
+    if (j == 1) q1 = __fadd_rn(q1, v[i]);
+    if (j == 2) q2 = __fadd_rn(q2, v[i]);
+    if (j == 3) q3 = __fadd_rn(q3, v[i]);
+  }
+  const float sum = r128_lane_finish(q0, q1, q2, q3);
+#pragma unroll
+  for (int i = 0; i < kMaxE / 32; ++i) v[i] = (lane + 32 * i < p.E) ? __fdiv_rn(v[i], sum) : ninf;
+  float total = 0.0f;
+  float sel_p = 0.0f;
+  int sel_i = 0;
+  for (int r = 0; r < p.topk; ++r) {
+    float bv = ninf;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kMaxE / 32; ++i) {
+      const int ee = lane + 32 * i;
+      if (v[i] > bv || (v[i] == bv && ee < bi)) { bv = v[i]; bi = ee; }
+    }
+#pragma unroll
+    for (int mm = 16; mm >= 1; mm >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, mm);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, mm);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    total = __fadd_rn(total, bv);
+    if (lane == r) { sel_p = bv; sel_i = bi; }
+#pragma unroll
+    for (int i = 0; i < kMaxE / 32; ++i)
+      if (lane + 32 * i == bi) v[i] = ninf;
+  }
+  const float inv = __fdiv_rn(1.0f, __fadd_rn(total, 1e-20f));
+  if (lane < p.topk) {
+    p.idx[(int64_t)tok * p.topk + lane] = sel_i;
+    p.wt[(int64_t)tok * p.topk + lane] = __fmul_rn(sel_p, inv);
+  }
+}
+
+// ------------------------------------------------------- expert down + sum --
+// One CTA per (16-row tile, token); warp s contracts top-k slot s's expert
+// rows against that slot's activation h[t, s, :].  MODE 0 (model path, same
+// rounding as ternary_expert_gemv + moe_reduce_add): y_s = bf16(alpha * S_s),
+// out = bf16(fmaf-chain_s(w_s, y_s) + residual).  MODE 1
+// (ternary_expert_down_sum): acc = fmaf(w_s * S_s, alpha, acc), no bf16 y_s.
+struct DownParams {
+  const void* h;          // [T, topk, K]
+  const int32_t* ids;     // [T, topk]
+  const float* wt;        // [T, topk]
+  const uint32_t* codes;  // [E, N, K/16]
+  const void* alpha;      // [E, N]
+  const void* residual;   // [T, N] or nullptr
+  void* out;              // [T, N]
+  int64_t h_tok_stride, h_slot_stride, res_stride, out_stride;
+  int E, N, K, nwords, topk, iters;
+};
+
+constexpr int kDownMaxIters = 8;
+constexpr int kDownMaxTopk = 8;
+
+template <int XT, int AT, int MODE>
+__global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ float s_y[kDownMaxTopk][16];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int tok = blockIdx.y;
+  const int row_g = blockIdx.x * 16 + g, row_h = row_g + 8;
+  const size_t per_warp = (size_t)p.iters * 256 * sizeof(uint2) + (size_t)p.K * sizeof(float);
+  uint2* frag = reinterpret_cast<uint2*>(smem + warp * per_warp);
+  float* xsm = reinterpret_cast<float*>(smem + warp * per_warp + (size_t)p.iters * 256 * sizeof(uint2));
+
+  if (warp < p.topk) {
+    int e = p.ids[(int64_t)tok * p.topk + warp];
+    const bool bad = (e < 0 || e >= p.E);
+    if (bad) e = 0;
+    const uint32_t* codes = p.codes + (int64_t)e * p.N * p.nwords;
+    uint4 wa[kDownMaxIters], wb[kDownMaxIters];
+#pragma unroll
+    for (int i = 0; i < kDownMaxIters; ++i) {
+      wa[i] = make_uint4(0, 0, 0, 0);
+      wb[i] = make_uint4(0, 0, 0, 0);
+      const int word = i * 16 + 4 * t;
+      if (i < p.iters && word < p.nwords) {
+        if (row_g < p.N) wa[i] = ld_stream_u4(codes + (int64_t)row_g * p.nwords + word);
+        if (row_h < p.N) wb[i] = ld_stream_u4(codes + (int64_t)row_h * p.nwords + word);
+      }
+    }
+    const void* hr = static_cast<const char*>(p.h) +
+                     (tok * p.h_tok_stride + warp * p.h_slot_stride) * (XT == kBF16 ? 2 : 4);
+    int tot[4];
+    const int s = fxa_warp_prologue<XT>(hr, p.K, p.iters, xsm, frag, tot);
+    int acc[4] = {0, 0, 0, 0};
+    contract_tile<kDownMaxIters>(wa, wb, p.iters, frag, lane, acc);
+    long long Sg, Sh;
+    combine_digits(acc, tot, t, Sg, Sh);
+    if (t == 0) {
+      const void* al = static_cast<const char*>(p.alpha) + (int64_t)e * p.N * (AT == kBF16 ? 2 : 4);
+      const bool nan_out = bad || s == kFxaNonFinite;
+      const float nanv = __int_as_float(0x7fc00000);
+      const float vg = nan_out ? nanv : fxa_value(Sg, s);
+      const float vh = nan_out ? nanv : fxa_value(Sh, s);
+      const float ag = row_g < p.N ? load_f<AT>(al, row_g) : 0.f;
+      const float ah = row_h < p.N ? load_f<AT>(al, row_h) : 0.f;
+      if constexpr (MODE == 0) {
+        // the expert output is stored in the activation dtype before the combine
+        float yg = __fmul_rn(vg, ag), yh = __fmul_rn(vh, ah);
+        if constexpr (XT == kBF16) {
+          yg = bf16_to_f32(f32_to_bf16(yg));
+          yh = bf16_to_f32(f32_to_bf16(yh));
+        }
+        s_y[warp][g] = yg;
+        s_y[warp][g + 8] = yh;
+      } else {
+        // alpha is applied in the combine below: acc = fmaf(w*S, alpha, acc)
+        const float w = p.wt[(int64_t)tok * p.topk + warp];
+        s_y[warp][g] = __fmul_rn(w, vg);
+        s_y[warp][g + 8] = __fmul_rn(w, vh);
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < 16) {
+    const int row = blockIdx.x * 16 + tid;
+    if (row < p.N) {
+      float acc = 0.0f;
+      for (int sl = 0; sl < p.topk; ++sl) {
+        if constexpr (MODE == 0) {
+          acc = __fmaf_rn(p.wt[(int64_t)tok * p.topk + sl], s_y[sl][tid], acc);
+        } else {
+          int e = p.ids[(int64_t)tok * p.topk + sl];
+          if (e < 0 || e >= p.E) e = 0;
+          const void* al = static_cast<const char*>(p.alpha) + (int64_t)e * p.N * (AT == kBF16 ? 2 : 4);
+          acc = __fmaf_rn(s_y[sl][tid], load_f<AT>(al, row), acc);
+        }
+      }
+      if (p.residual != nullptr)
+        acc = __fadd_rn(acc, load_f<XT>(static_cast<const char*>(p.residual) +
+                                            tok * p.res_stride * (XT == kBF16 ? 2 : 4), row));
+      store_f<XT>(static_cast<char*>(p.out) + tok * p.out_stride * (XT == kBF16 ? 2 : 4), row, acc);
+    }
+  }
+}
+
+// ------------------------------------------------------------ moe reduce --
+template <int XT>
+__global__ void moe_reduce_kernel(const void* x, const float* w, const void* residual, void* y,
+                                  int64_t x_tok_stride, int64_t x_slot_stride, int64_t res_stride,
+                                  int64_t y_stride, int N, int topk) {
+  const int tok = blockIdx.y;
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  const int es = XT == kBF16 ? 2 : 4;
+  float acc = 0.0f;
+  for (int s = 0; s < topk; ++s)
+    acc = __fmaf_rn(w[(int64_t)tok * topk + s],
+                    load_f<XT>(static_cast<const char*>(x) + (tok * x_tok_stride + s * x_slot_stride) * es, n),
+                    acc);
+  if (residual != nullptr)
+    acc = __fadd_rn(acc, load_f<XT>(static_cast<const char*>(residual) + tok * res_stride * es, n));
+  store_f<XT>(static_cast<char*>(y) + tok * y_stride * es, n, acc);
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" int64_t maple_router_topk_workspace_bytes(int64_t tokens, int64_t n_experts) {
+  return kTicketBytesMoe + tokens * n_experts * (int64_t)sizeof(float);
+}
+
+extern "C" int maple_router_topk(const void* x, int x_dtype, int64_t x_row_stride, int64_t tokens,
+                                 int64_t k, const void* gate, int gate_dtype, int64_t n_experts,
+                                 int64_t topk, int32_t* idx, float* wt, void* workspace,
+                                 int64_t workspace_bytes, void* stream) {
+  if (tokens < 0 || k <= 0 || n_experts <= 0 || topk <= 0) return kErrShape;
+  if (tokens == 0) return kOk;
+  if (topk > n_experts || topk > 32 || n_experts > 256) return kErrShape;
+  if ((x_dtype != kF32 && x_dtype != kBF16) || (gate_dtype != kF32 && gate_dtype != kBF16)) return kErrDtype;
+  if (!x || !gate || !idx || !wt) return kErrShape;
+  if (tokens * (int64_t)sizeof(unsigned) > kTicketBytesMoe || tokens > 65535) return kErrShape;
+  if (!workspace || workspace_bytes < maple_router_topk_workspace_bytes(tokens, n_experts)) return kErrWorkspace;
+  RouterParams p{};
+  p.x = x; p.gate = gate; p.idx = idx; p.wt = wt;
+  p.tickets = static_cast<unsigned*>(workspace);
+  p.logits = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytesMoe);
+  p.x_stride = x_row_stride; p.E = (int)n_experts; p.K = (int)k; p.topk = (int)topk;
+  dim3 grid((unsigned)((n_experts + kRouterWarps - 1) / kRouterWarps), (unsigned)tokens);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (x_dtype == kBF16) {
+    if (gate_dtype == kBF16) router_kernel<kBF16, kBF16><<<grid, 256, 0, st>>>(p);
+    else router_kernel<kBF16, kF32><<<grid, 256, 0, st>>>(p);
+  } else {
+    if (gate_dtype == kBF16) router_kernel<kF32, kBF16><<<grid, 256, 0, st>>>(p);
+    else router_kernel<kF32, kF32><<<grid, 256, 0, st>>>(p);
+  }
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+namespace {
+template <int XT, int AT, int MODE>
+cudaError_t launch_down(const DownParams& p, int T, cudaStream_t st) {
+  const size_t per_warp = (size_t)p.iters * 256 * sizeof(uint2) + (size_t)p.K * sizeof(float);
+  const size_t smem = per_warp * kDownMaxTopk;
+  auto kern = down_sum_kernel<XT, AT, MODE>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid((p.N + 15) / 16, T);
+  kern<<<grid, 256, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <int MODE>
+int down_entry(const void* h, int h_dtype, int64_t h_tok_stride, int64_t h_slot_stride,
+               const int32_t* ids, const float* wt, int64_t tokens, int64_t topk, int64_t k,
+               const uint32_t* codes, int64_t n_experts, int64_t n, const void* alpha,
+               int alpha_dtype, const void* residual, int64_t res_stride, void* out,
+               int64_t out_stride, void* stream) {
+  if (tokens < 0 || topk <= 0 || k <= 0 || n < 0 || n_experts <= 0) return kErrShape;
+  if (tokens == 0 || n == 0) return kOk;
+  if (topk > kDownMaxTopk || k % 64 != 0 || k > kDownMaxIters * 256 || tokens > 65535) return kErrShape;
+  if ((h_dtype != kF32 && h_dtype != kBF16) || (alpha_dtype != kF32 && alpha_dtype != kBF16)) return kErrDtype;
+  if (!h || !ids || !wt || !codes || !alpha || !out) return kErrShape;
+  if ((reinterpret_cast<uintptr_t>(codes) & 15) != 0) return kErrAlign;
+  DownParams p{};
+  p.h = h; p.ids = ids; p.wt = wt; p.codes = codes; p.alpha = alpha; p.residual = residual; p.out = out;
+  p.h_tok_stride = h_tok_stride; p.h_slot_stride = h_slot_stride; p.res_stride = res_stride;
+  p.out_stride = out_stride; p.E = (int)n_experts; p.N = (int)n; p.K = (int)k; p.nwords = (int)(k / 16);
+  p.topk = (int)topk; p.iters = (int)((k + 255) / 256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (h_dtype == kBF16)
+    e = alpha_dtype == kBF16 ? launch_down<kBF16, kBF16, MODE>(p, (int)tokens, st)
+                             : launch_down<kBF16, kF32, MODE>(p, (int)tokens, st);
+  else
+    e = alpha_dtype == kBF16 ? launch_down<kF32, kBF16, MODE>(p, (int)tokens, st)
+                             : launch_down<kF32, kF32, MODE>(p, (int)tokens, st);
+  return e == cudaSuccess ? kOk : kErrCuda;
+}
+}  // namespace
+
+extern "C" int maple_ternary_expert_down_reduce(const void* h, int h_dtype, int64_t h_tok_stride,
+                                                int64_t h_slot_stride, const int32_t* ids,
+                                                const float* wt, int64_t tokens, int64_t topk,
+                                                int64_t k, const uint32_t* codes, int64_t n_experts,
+                                                int64_t n, const void* alpha, int alpha_dtype,
+                                                const void* residual, int64_t res_stride, void* out,
+                                                int64_t out_stride, void* stream) {
+  return down_entry<0>(h, h_dtype, h_tok_stride, h_slot_stride, ids, wt, tokens, topk, k, codes,
+                       n_experts, n, alpha, alpha_dtype, residual, res_stride, out, out_stride, stream);
+}
+
+extern "C" int maple_ternary_expert_down_sum(const void* h, int h_dtype, int64_t h_tok_stride,
+                                             int64_t h_slot_stride, const int32_t* ids,
+                                             const float* wt, int64_t tokens, int64_t topk,
+                                             int64_t k, const uint32_t* codes, int64_t n_experts,
+                                             int64_t n, const void* alpha, int alpha_dtype,
+                                             const void* residual, int64_t res_stride, void* out,
+                                             int64_t out_stride, void* stream) {
+  return down_entry<1>(h, h_dtype, h_tok_stride, h_slot_stride, ids, wt, tokens, topk, k, codes,
+                       n_experts, n, alpha, alpha_dtype, residual, res_stride, out, out_stride, stream);
+}
+
+extern "C" int maple_moe_reduce_add(const void* x, int x_dtype, int64_t x_tok_stride,
+                                    int64_t x_slot_stride, const float* wt, int64_t tokens,
+                                    int64_t topk, int64_t n, const void* residual,
+                                    int64_t res_stride, void* y, int64_t y_stride, void* stream) {
+  if (tokens < 0 || topk <= 0 || n < 0) return kErrShape;
+  if (tokens == 0 || n == 0) return kOk;
+  if (x_dtype != kF32 && x_dtype != kBF16) return kErrDtype;
+  if (!x || !wt || !y || tokens > 65535) return kErrShape;
+  dim3 grid((unsigned)((n + 127) / 128), (unsigned)tokens);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (x_dtype == kBF16)
+    moe_reduce_kernel<kBF16><<<grid, 128, 0, st>>>(x, wt, residual, y, x_tok_stride, x_slot_stride,
+                                                   res_stride, y_stride, (int)n, (int)topk);
+  else
+    moe_reduce_kernel<kF32><<<grid, 128, 0, st>>>(x, wt, residual, y, x_tok_stride, x_slot_stride,
+                                                  res_stride, y_stride, (int)n, (int)topk);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}

@@ -1,0 +1,263 @@
+"""Every sm_100a decode operator vs the CPU oracle on identical inputs: bit-exact (GPU)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from tests.helpers import alpha_bf, bf, randn_bf, rng, tern_packed, to_dev, to_np
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+BF = None
+
+
+@pytest.fixture(scope="module")
+def K():
+    from maple_flash_dgx_spark_b200 import kernels
+
+    return kernels
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors(cuda):
+    from maple_flash_dgx_spark_b200 import _lib
+
+    _lib.take_device_errors(cuda)
+    yield
+
+
+@pytest.mark.parametrize("rows,n", [(1, 2048), (3, 2048), (2, 128), (1, 4096)])
+def test_norms(cuda, K, rows, n):
+    rs = rng(rows * 7 + n)
+    x, y = randn_bf(rs, rows, n), randn_bf(rs, rows, n)
+    w = (1 + 0.02 * rs.standard_normal(n)).astype(np.float32)
+    xt, yt, wt = to_dev(x, cuda, torch.bfloat16), to_dev(y, cuda, torch.bfloat16), to_dev(w, cuda)
+    np.testing.assert_array_equal(to_np(K.rms_norm(xt, wt, 1e-6)), oracle.rms_norm(x, w, 1e-6))
+    r, nrm = K.add_rms_norm(xt, yt, wt, 1e-6)
+    r_o, n_o = oracle.add_rms_norm(x, y, w, 1e-6)
+    np.testing.assert_array_equal(to_np(r), r_o)
+    np.testing.assert_array_equal(to_np(nrm), n_o)
+
+
+@pytest.mark.parametrize("T,E,topk,k", [(1, 64, 8, 2048), (5, 64, 8, 2048), (3, 4, 2, 128), (2, 256, 8, 1024)])
+def test_router_topk(cuda, K, T, E, topk, k):
+    rs = rng(T * 100 + E)
+    x = randn_bf(rs, T, k)
+    g = randn_bf(rs, E, k, scale=0.02)
+    idx, wt = K.router_topk(to_dev(x, cuda, torch.bfloat16), to_dev(g, cuda, torch.bfloat16), topk)
+    idx_o, wt_o = oracle.router_topk(x, g, topk)
+    np.testing.assert_array_equal(to_np(idx), idx_o)
+    np.testing.assert_array_equal(to_np(wt), wt_o)
+
+
+def test_router_ties_take_lowest_index(cuda, K):
+    x = np.ones((1, 128), np.float32)
+    g = np.zeros((8, 128), np.float32)  # all logits equal
+    idx, wt = K.router_topk(to_dev(x, cuda, torch.bfloat16), to_dev(g, cuda, torch.bfloat16), 3)
+    np.testing.assert_array_equal(to_np(idx), [[0, 1, 2]])
+
+
+@pytest.mark.parametrize("T,topk,E,inter,k", [(1, 8, 64, 1024, 2048), (3, 2, 4, 128, 128), (2, 8, 16, 96, 1024)])
+def test_expert_swiglu(cuda, K, T, topk, E, inter, k):
+    rs = rng(T + topk + inter)
+    x = randn_bf(rs, T, k)
+    packed = tern_packed(rs, E, 2 * inter, k)
+    alpha = bf(alpha_bf(rs, E, 2 * inter) * 40)  # larger scales exercise the clamp
+    ids = np.stack([rs.permutation(E)[:topk] for _ in range(T)]).astype(np.int32)
+    h = K.ternary_expert_swiglu(to_dev(x, cuda, torch.bfloat16), to_dev(packed, cuda),
+                                to_dev(alpha, cuda, torch.bfloat16), to_dev(ids, cuda))
+    h_o = oracle.expert_swiglu(x, packed, alpha, ids)
+    np.testing.assert_array_equal(to_np(h), h_o)
+
+
+@pytest.mark.parametrize("per_slot", [False, True])
+def test_expert_gemv(cuda, K, per_slot):
+    rs = rng(5 + per_slot)
+    T, topk, E, N, k = 3, 4, 8, 320, 1024
+    x = randn_bf(rs, T, topk, k) if per_slot else randn_bf(rs, T, k)
+    packed = tern_packed(rs, E, N, k)
+    alpha = alpha_bf(rs, E, N)
+    ids = rs.randint(0, E, size=(T, topk)).astype(np.int32)
+    y = K.ternary_expert_gemv(to_dev(x, cuda, torch.bfloat16), to_dev(packed, cuda), to_dev(alpha, cuda, torch.bfloat16),
+                              to_dev(ids, cuda))
+    y_o = oracle.expert_gemv(x.reshape(-1, k), packed, alpha, ids, x_rows_per_token=1 if per_slot else topk)
+    np.testing.assert_array_equal(to_np(y).reshape(-1, N), y_o)
+
+
+@pytest.mark.parametrize("mode", ["reduce", "sum"])
+@pytest.mark.parametrize("T,topk,E,N,k", [(1, 8, 64, 2048, 1024), (4, 2, 4, 128, 128), (2, 8, 8, 200, 512)])
+def test_expert_down(cuda, K, mode, T, topk, E, N, k):
+    rs = rng(T * topk + N)
+    h = randn_bf(rs, T, topk, k)
+    packed = tern_packed(rs, E, N, k)
+    alpha = alpha_bf(rs, E, N)
+    ids = np.stack([rs.permutation(E)[:topk] for _ in range(T)]).astype(np.int32)
+    w = rs.random_sample((T, topk)).astype(np.float32)
+    res = randn_bf(rs, T, N)
+    fn = K.ternary_expert_down_reduce if mode == "reduce" else K.ternary_expert_down_sum
+    out = fn(to_dev(h, cuda, torch.bfloat16), to_dev(packed, cuda), to_dev(alpha, cuda, torch.bfloat16), to_dev(ids, cuda),
+             to_dev(w, cuda), to_dev(res, cuda, torch.bfloat16))
+    out_o = oracle.expert_down_reduce(h, packed, alpha, ids, w, res, mode=0 if mode == "reduce" else 1)
+    np.testing.assert_array_equal(to_np(out), out_o)
+
+
+def test_moe_reduce_add(cuda, K):
+    rs = rng(9)
+    x = randn_bf(rs, 3, 8, 2048)
+    w = rs.random_sample((3, 8)).astype(np.float32)
+    r = randn_bf(rs, 3, 2048)
+    y = K.moe_reduce_add(to_dev(x, cuda, torch.bfloat16), to_dev(w, cuda), to_dev(r, cuda, torch.bfloat16))
+    np.testing.assert_array_equal(to_np(y), oracle.moe_reduce_add(x, w, r))
+
+
+def _attn_case(rs, B, Hq, Hkv, D, T, lens, Bc=None):
+    Bc = Bc or B
+    qkv = randn_bf(rs, B, (Hq + 2 * Hkv) * D)
+    qw = (1 + 0.02 * rs.standard_normal(D)).astype(np.float32)
+    kw = (1 + 0.02 * rs.standard_normal(D)).astype(np.float32)
+    kc = randn_bf(rs, Bc, Hkv, T, D)
+    vc = randn_bf(rs, Bc, Hkv, T, D)
+    pos = np.asarray(lens, np.int64) - 1
+    inv = 1.0 / (1e6 ** (np.arange(0, D, 2, dtype=np.float32) / D))
+    ang = np.outer(pos.astype(np.float32), inv)
+    emb = np.concatenate([ang, ang], -1).astype(np.float32)
+    cos, sin = bf(np.cos(emb)), bf(np.sin(emb))
+    return qkv, qw, kw, kc, vc, pos, cos, sin
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D,T,lens,split,window", [
+    (1, 32, 4, 128, 4096, [4096], 64, 0),
+    (1, 32, 4, 128, 768, [640], 32, 0),
+    (7, 32, 4, 128, 1024, [1, 63, 64, 65, 300, 511, 1000], 64, 0),
+    (2, 2, 2, 64, 64, [20, 64], 32, 0),
+    (3, 16, 2, 128, 600, [600, 17, 333], 128, 0),
+    (2, 8, 8, 128, 512, [512, 100], 64, 96),
+])
+def test_qkv_decode_and_attention(cuda, K, B, Hq, Hkv, D, T, lens, split, window):
+    rs = rng(B * 31 + T)
+    qkv, qw, kw, kc, vc, pos, cos, sin = _attn_case(rs, B, Hq, Hkv, D, T, lens)
+    kc_d, vc_d = to_dev(kc, cuda, torch.bfloat16), to_dev(vc, cuda, torch.bfloat16)
+    sl = to_dev(pos, cuda)
+    q = K.apply_qkv_decode(to_dev(qkv, cuda, torch.bfloat16), to_dev(qw, cuda), to_dev(kw, cuda),
+                           to_dev(cos, cuda, torch.bfloat16), to_dev(sin, cuda, torch.bfloat16), kc_d, vc_d, sl,
+                           num_heads=Hq, num_kv_heads=Hkv, head_dim=D, rotary_dim=D, use_rope=True,
+                           use_qk_norm=True, eps=1e-6)
+    kc_o, vc_o = kc.copy(), vc.copy()
+    q_o = oracle.apply_qkv_decode(qkv, qw, kw, cos, sin, kc_o, vc_o, pos, num_heads=Hq, num_kv_heads=Hkv,
+                                  head_dim=D)
+    np.testing.assert_array_equal(to_np(q)[:, :, 0], q_o)
+    np.testing.assert_array_equal(to_np(kc_d), kc_o)
+    np.testing.assert_array_equal(to_np(vc_d), vc_o)
+    out = K.decode_gqa_attn(q, kc_d, vc_d, sl, scale=D ** -0.5, window=window or None, split_len=split)
+    out_o = oracle.decode_gqa(q_o, kc_o, vc_o, pos, scale=np.float32(D ** -0.5), window=window, split_len=split)
+    np.testing.assert_array_equal(to_np(out)[:, :, 0], out_o)
+
+
+def test_attention_row_map_equals_gathered_cache(cuda, K):
+    """Reference tests/test_fused_decode.py:364-402: row_map reads the mapped cache rows."""
+    rs = rng(77)
+    B, Bc, Hq, Hkv, D, T = 3, 5, 8, 2, 128, 256
+    qkv, qw, kw, kc, vc, pos, cos, sin = _attn_case(rs, B, Hq, Hkv, D, T, [200, 31, 256], Bc=Bc)
+    rmap = np.array([4, 0, 2], np.int32)
+    kc_d, vc_d = to_dev(kc, cuda, torch.bfloat16), to_dev(vc, cuda, torch.bfloat16)
+    sl, rm = to_dev(pos, cuda), to_dev(rmap, cuda)
+    q = K.apply_qkv_decode(to_dev(qkv, cuda, torch.bfloat16), to_dev(qw, cuda), to_dev(kw, cuda),
+                           to_dev(cos, cuda, torch.bfloat16), to_dev(sin, cuda, torch.bfloat16), kc_d, vc_d, sl,
+                           row_map=rm, num_heads=Hq, num_kv_heads=Hkv, head_dim=D, rotary_dim=D, use_rope=True,
+                           use_qk_norm=True, eps=1e-6)
+    out = K.decode_gqa_attn(q, kc_d, vc_d, sl, row_map=rm, scale=D ** -0.5, window=None, split_len=64)
+    kc_o, vc_o = kc.copy(), vc.copy()
+    q_o = oracle.apply_qkv_decode(qkv, qw, kw, cos, sin, kc_o, vc_o, pos, rmap, num_heads=Hq, num_kv_heads=Hkv,
+                                  head_dim=D)
+    out_o = oracle.decode_gqa(q_o, kc_o, vc_o, pos, rmap, scale=np.float32(D ** -0.5), split_len=64)
+    np.testing.assert_array_equal(to_np(out)[:, :, 0], out_o)
+    untouched = [1, 3]
+    np.testing.assert_array_equal(to_np(kc_d)[untouched], kc[untouched])
+
+
+def test_attention_vs_sdpa(cuda, K):
+    """Within the reference's 1e-3 tolerance of torch SDPA (test_fused_decode.py:104-222)."""
+    rs = rng(3)
+    B, Hq, Hkv, D, T = 2, 32, 4, 128, 1000
+    q = to_dev(randn_bf(rs, B, Hq, 1, D), cuda, torch.bfloat16)
+    kc = to_dev(randn_bf(rs, B, Hkv, T, D), cuda, torch.bfloat16)
+    vc = to_dev(randn_bf(rs, B, Hkv, T, D), cuda, torch.bfloat16)
+    sl = torch.tensor([T - 1, 499], device=cuda)
+    out = K.decode_gqa_attn(q, kc, vc, sl, scale=D ** -0.5, window=None)
+    for b, n in enumerate([T, 500]):
+        ref = torch.nn.functional.scaled_dot_product_attention(
+            q[b:b + 1].float(), kc[b:b + 1, :, :n].float(), vc[b:b + 1, :, :n].float(), enable_gqa=True)
+        torch.testing.assert_close(out[b:b + 1].float(), ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("group,symmetric,B", [(128, True, 1), (64, False, 1), (128, False, 3), (256, True, 2)])
+def test_rtn4_gemv(cuda, K, group, symmetric, B):
+    rs = rng(group + B)
+    N, k = 1000, 2048
+    x = randn_bf(rs, B, k)
+    codes = rs.randint(0, 16, size=(N, k)).astype(np.uint32)
+    packed = oracle.pack_4bit(codes)
+    s = bf(np.abs(rs.standard_normal((N, k // group))) * 0.003 + 1e-4)
+    b = None if symmetric else bf(rs.standard_normal((N, k // group)) * 0.01)
+    y = K.rtn4_gemv(to_dev(x, cuda, torch.bfloat16), to_dev(packed, cuda), to_dev(s, cuda, torch.bfloat16),
+                    None if b is None else to_dev(b, cuda, torch.bfloat16), group_size=group)
+    np.testing.assert_array_equal(to_np(y), oracle.rtn4_gemv(x, packed, s, b, group))
+
+
+def test_rtn4_indexed_gemv(cuda, K):
+    rs = rng(44)
+    nc, C, k, P = 50, 32, 2048, 7
+    x = randn_bf(rs, 1, k)
+    packed = oracle.pack_4bit(rs.randint(0, 16, size=(nc * C, k)).astype(np.uint32))
+    s = bf(np.abs(rs.standard_normal((nc * C, k // 64))) * 0.003)
+    b = bf(rs.standard_normal((nc * C, k // 64)) * 0.01)
+    cids = rs.permutation(nc)[:P].astype(np.int32)
+    y = K.rtn4_indexed_gemv(to_dev(x, cuda, torch.bfloat16), to_dev(packed.reshape(nc, C, -1), cuda),
+                            to_dev(s.reshape(nc, C, -1), cuda, torch.bfloat16),
+                            to_dev(b.reshape(nc, C, -1), cuda, torch.bfloat16), to_dev(cids, cuda), group_size=64)
+    rows = (cids[:, None].astype(np.int64) * C + np.arange(C)).reshape(-1)
+    np.testing.assert_array_equal(to_np(y), oracle.rtn4_gemv(x, packed, s, b, 64, row_index=rows))
+
+
+@pytest.mark.parametrize("V", [151936, 1000, 8192])
+def test_argmax(cuda, K, V):
+    rs = rng(V)
+    logits = randn_bf(rs, 3, V)
+    logits[1, 17] = logits[1].max()   # a tie: the first index wins
+    logits[1, 5] = logits[1].max()
+    got = K.argmax(to_dev(logits, cuda, torch.bfloat16))
+    np.testing.assert_array_equal(to_np(got), oracle.argmax(logits))
+
+
+@pytest.mark.parametrize("top_k,top_p,temp", [(20, 0.95, 1.0), (2, 1.0, 0.8), (64, 0.5, 1.3)])
+def test_fused_sampler(cuda, K, top_k, top_p, temp):
+    rs = rng(top_k)
+    V = 151936
+    logits = (rs.standard_normal((4, V)) * 3).astype(np.float32)
+    for u in (0.0, 0.25, 0.5, 0.75, 0.999):
+        uu = np.full(4, u, np.float32)
+        got = K.fused_sample_batched(to_dev(logits, cuda), to_dev(uu, cuda), temperature=temp, top_p=top_p,
+                                     top_k=top_k)
+        np.testing.assert_array_equal(to_np(got), oracle.fused_sample(logits, uu, temperature=temp, top_p=top_p,
+                                                                      top_k=top_k))
+    one = K.fused_sample(to_dev(logits[2], cuda), to_dev(np.float32(0.5), cuda), temperature=temp, top_p=top_p,
+                         top_k=top_k)
+    assert int(one) == int(oracle.fused_sample(logits[2:3], np.float32([0.5]), temperature=temp, top_p=top_p,
+                                               top_k=top_k)[0])
+
+
+def test_embeddings(cuda, K):
+    rs = rng(12)
+    V, H = 1000, 2048
+    table = randn_bf(rs, V, H, scale=0.02)
+    ids = np.array([0, 999, 17], np.int64)
+    e = K.embedding(to_dev(ids, cuda), to_dev(table, cuda, torch.bfloat16))
+    np.testing.assert_array_equal(to_np(e), table[ids])
+    packed = oracle.pack_4bit(rs.randint(0, 16, size=(V, H)).astype(np.uint32))
+    s = bf(np.abs(rs.standard_normal((V, H // 64))) * 0.003)
+    b = bf(rs.standard_normal((V, H // 64)) * 0.01)
+    r = K.rtn4_embedding(to_dev(ids, cuda), to_dev(packed, cuda), to_dev(s, cuda, torch.bfloat16),
+                         to_dev(b, cuda, torch.bfloat16), group_size=64)
+    np.testing.assert_array_equal(to_np(r), oracle.rtn4_embedding(ids, packed, s, b, 64, out_bf16=False))
