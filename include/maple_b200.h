@@ -7,7 +7,10 @@
  * and returns a status code (0 = ok, see maple_status).  Nothing here
  * allocates device memory: scratch space is passed in by the caller, sized by
  * the matching *_workspace_bytes() query, and must be zero-filled once before
- * its first use (kernels leave it zeroed again when they finish).
+ * its first use.  Its first MiB holds completion tickets that every kernel
+ * leaves at zero when it finishes, so one workspace can serve all entry
+ * points one after another on a stream; launches that may overlap on the GPU
+ * need separate workspaces.
  *
  * Each declaration names the reference operator it replaces
  * (cloud-000/maple-flash-dgx-spark, paths relative to src/maple_run/).
@@ -121,11 +124,14 @@ int maple_add_rms_norm(const void* x, const void* y, int x_dtype, int64_t rows, 
  * K/V store at seqlen[b] of cache row row_map[b] (identity when NULL).
  * Replaces kernels/decode_attn.py:362 apply_qkv_decode.  qkv [batch,
  * (H + 2*Hkv)*D]; caches [cache_batch, Hkv, max_len, D] with D contiguous;
- * q_out [batch, H, D].  An out-of-range position or cache row skips the
- * store and sets bit 2 of *err. */
+ * q_out [batch, H, D].  cos/sin: one row per batch row (cs_table_len = 0)
+ * or a table [cs_table_len, rotary_dim] read at row clamp(seqlen[b]), the
+ * out-of-place clamp of model.py:94-109.  An out-of-range position or cache
+ * row skips the store and sets bit 2 of *err. */
 int maple_apply_qkv_decode(const void* qkv, int x_dtype, int64_t batch, int64_t qkv_row_stride,
                            const void* q_weight, const void* k_weight, int w_dtype, const void* cos,
-                           const void* sin, int cs_dtype, int64_t cs_row_stride, void* q_out, int64_t q_sb,
+                           const void* sin, int cs_dtype, int64_t cs_row_stride, int64_t cs_table_len,
+                           void* q_out, int64_t q_sb,
                            int64_t q_sh, void* k_cache, void* v_cache, int64_t cache_batch, int64_t cache_sb,
                            int64_t cache_sh, int64_t max_len, const int64_t* seqlen, const int32_t* row_map,
                            int64_t num_heads, int64_t num_kv_heads, int64_t head_dim, int64_t rotary_dim,

@@ -73,6 +73,7 @@ struct QkvParams {
   int* err;
   int64_t qkv_sb, cs_sb, q_sb, q_sh, kc_sb, kc_sh, vc_sb, vc_sh;
   int Hq, Hkv, D, R, Bc, T;
+  int64_t cs_table_len;   // > 0: cos/sin are tables indexed by clamp(pos); 0: one row per batch row
   int use_rope;
   float eps;
 };
@@ -114,8 +115,10 @@ __global__ void __launch_bounds__(32) qk_norm_rope_store_kernel(QkvParams p) {
     xh[d] = __fmul_rn(__fmul_rn(xh[d], rstd), load_f<WT>(w, d));
   }
   __syncwarp();
-  const char* cs = static_cast<const char*>(p.cos) + b * p.cs_sb * (CT == kBF16 ? 2 : 4);
-  const char* sn = static_cast<const char*>(p.sin) + b * p.cs_sb * (CT == kBF16 ? 2 : 4);
+  int64_t cs_row = b;
+  if (p.cs_table_len > 0) cs_row = pos < 0 ? 0 : (pos >= p.cs_table_len ? p.cs_table_len - 1 : pos);
+  const char* cs = static_cast<const char*>(p.cos) + cs_row * p.cs_sb * (CT == kBF16 ? 2 : 4);
+  const char* sn = static_cast<const char*>(p.sin) + cs_row * p.cs_sb * (CT == kBF16 ? 2 : 4);
   const int half = p.R / 2;
   char* dst;
   if (is_q)
@@ -329,12 +332,12 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
 
 using namespace mb;
 
-constexpr int kAttnTicketBytes = 64 * 1024;
+constexpr int kAttnTicketBytes = 1 << 20;
 
 extern "C" int maple_apply_qkv_decode(const void* qkv, int x_dtype, int64_t batch, int64_t qkv_row_stride,
                                       const void* q_weight, const void* k_weight, int w_dtype,
                                       const void* cos, const void* sin, int cs_dtype, int64_t cs_row_stride,
-                                      void* q_out, int64_t q_sb, int64_t q_sh, void* k_cache, void* v_cache,
+                                      int64_t cs_table_len, void* q_out, int64_t q_sb, int64_t q_sh, void* k_cache, void* v_cache,
                                       int64_t cache_batch, int64_t cache_sb, int64_t cache_sh,
                                       int64_t max_len, const int64_t* seqlen, const int32_t* row_map,
                                       int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
@@ -350,7 +353,7 @@ extern "C" int maple_apply_qkv_decode(const void* qkv, int x_dtype, int64_t batc
   QkvParams p{};
   p.qkv = qkv; p.q_w = q_weight; p.k_w = k_weight; p.cos = cos; p.sin = sin; p.q_out = q_out;
   p.kc = k_cache; p.vc = v_cache; p.seqlen = seqlen; p.row_map = row_map; p.err = err;
-  p.qkv_sb = qkv_row_stride; p.cs_sb = cs_row_stride; p.q_sb = q_sb; p.q_sh = q_sh;
+  p.qkv_sb = qkv_row_stride; p.cs_sb = cs_row_stride; p.cs_table_len = cs_table_len; p.q_sb = q_sb; p.q_sh = q_sh;
   p.kc_sb = cache_sb; p.kc_sh = cache_sh; p.vc_sb = cache_sb; p.vc_sh = cache_sh;
   p.Hq = (int)num_heads; p.Hkv = (int)num_kv_heads; p.D = (int)head_dim; p.R = (int)rotary_dim;
   p.Bc = (int)cache_batch; p.T = (int)max_len; p.use_rope = use_rope; p.eps = eps;

@@ -17,7 +17,7 @@
 
 namespace mb {
 
-constexpr int kHeadTicketBytes = 64 * 1024;
+constexpr int kHeadTicketBytes = 1 << 20;
 constexpr int kHeadPrefetch = 4;  // iterations in flight per warp
 
 struct Rtn4Params {

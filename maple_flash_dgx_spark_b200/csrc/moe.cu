@@ -9,7 +9,7 @@
 
 namespace mb {
 
-constexpr int kTicketBytesMoe = 64 * 1024;
+constexpr int kTicketBytesMoe = 1 << 20;
 
 // ----------------------------------------------------------------- router --
 // Logits: one warp per (token, expert), R128 order over K (products x*g added

@@ -26,7 +26,7 @@
 namespace mb {
 
 constexpr int kMaxIters = 8;                 // K iterations held in registers (K <= 2048)
-constexpr int kTicketBytes = 64 * 1024;      // ticket header at the start of a workspace
+constexpr int kTicketBytes = 1 << 20;          // ticket header at the start of a workspace
 
 enum GemvMode : int { kPlain = 0, kSwiglu = 1 };
 

@@ -307,9 +307,12 @@ def add_rms_norm(x, y, weight, eps: float = 1e-6):
 
 
 def apply_qkv_decode(qkv, q_weight, k_weight, cos, sin, k_cache, v_cache, seqlen, *, row_map=None, num_heads,
-                     num_kv_heads, head_dim, rotary_dim, use_rope, use_qk_norm, eps):
+                     num_kv_heads, head_dim, rotary_dim, use_rope, use_qk_norm, eps, rope_table: bool = False,
+                     q_out=None):
     """QK RMSNorm + RoPE + K/V store at ``seqlen``.  Reference kernels/decode_attn.py:362-439.
-    Returns Q ``[B, H, 1, D]``."""
+    Returns Q ``[B, H, 1, D]``.  With ``rope_table`` the ``cos``/``sin``
+    arguments are whole ``[T, rotary_dim]`` tables read at ``clamp(seqlen[b])``
+    inside the kernel (no per-step gather)."""
     op = "apply_qkv_decode"
     if qkv.ndim != 2:
         raise ValueError(f"apply_qkv_decode expects [B, qkv], got {tuple(qkv.shape)}.")
@@ -327,10 +330,12 @@ def apply_qkv_decode(qkv, q_weight, k_weight, cos, sin, k_cache, v_cache, seqlen
         raise ValueError("KV caches must be [B, n_kv, T, D] with contiguous (T, D).")
     if k_cache.dtype != qkv.dtype or v_cache.dtype != qkv.dtype:
         raise TypeError("KV cache dtype must match qkv dtype.")
-    q_out = torch.empty(bsz, num_heads, 1, head_dim, device=qkv.device, dtype=qkv.dtype)
+    if q_out is None:
+        q_out = torch.empty(bsz, num_heads, 1, head_dim, device=qkv.device, dtype=qkv.dtype)
     rot = max(int(rotary_dim), 0) if use_rope else 0
-    cos2 = cos.reshape(bsz, -1) if use_rope else None
-    sin2 = sin.reshape(bsz, -1) if use_rope else None
+    table_len = int(cos.shape[0]) if (use_rope and rope_table) else 0
+    cos2 = (cos if rope_table else cos.reshape(bsz, -1)) if use_rope else None
+    sin2 = (sin if rope_table else sin.reshape(bsz, -1)) if use_rope else None
     if use_rope and (cos2.stride(1) != 1 or sin2.stride(1) != 1 or cos2.stride(0) != sin2.stride(0)):
         cos2, sin2 = cos2.contiguous(), sin2.contiguous()
     sl = seqlen.reshape(-1).to(torch.int64)
@@ -339,7 +344,8 @@ def apply_qkv_decode(qkv, q_weight, k_weight, cos, sin, k_cache, v_cache, seqlen
     kw = k_weight.reshape(-1).contiguous().to(qw.dtype)
     check(lib().maple_apply_qkv_decode(
         ptr(qkv), dtype_code(qkv, op), bsz, qkv.stride(0), ptr(qw), ptr(kw), dtype_code(qw, op), ptr(cos2), ptr(sin2),
-        dtype_code(cos2, op) if cos2 is not None else 0, cos2.stride(0) if cos2 is not None else 0, ptr(q_out),
+        dtype_code(cos2, op) if cos2 is not None else 0, cos2.stride(0) if cos2 is not None else 0, table_len,
+        ptr(q_out),
         q_out.stride(0), q_out.stride(1), ptr(k_cache), ptr(v_cache), k_cache.shape[0], k_cache.stride(0),
         k_cache.stride(1), k_cache.shape[2], ptr(sl), ptr(rm), num_heads, num_kv_heads, head_dim, rot,
         int(bool(use_rope)), float(eps), ptr(_err(qkv.device)), stream_ptr(qkv.device)), op)

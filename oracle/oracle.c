@@ -115,6 +115,31 @@ static inline int64_t fxa_encode(float v, int s) { return (int64_t)rint((double)
 
 static inline float fxa_value(int64_t S, int s) { return (float)((double)S * pow2d(-s)); }
 
+/* Byte lookup table of an FXA vector for 2-bit codes: entry [q][b] =
+ * sum_{i<4} (((b >> 2i) & 3) - 1) * X[4q + i], so a code byte costs one
+ * lookup.  The sums are exact integers, identical to the direct loop. */
+static int64_t* tern_lut(const int64_t* X, int64_t k) {
+  int64_t* lut = (int64_t*)malloc(sizeof(int64_t) * (k / 4) * 256);
+  for (int64_t q = 0; q < k / 4; ++q)
+    for (int b = 0; b < 256; ++b) {
+      int64_t v = 0;
+      for (int i = 0; i < 4; ++i) v += ((int64_t)((b >> (2 * i)) & 3) - 1) * X[4 * q + i];
+      lut[q * 256 + b] = v;
+    }
+  return lut;
+}
+
+/* Exact sum_k (c_k - 1) * X_k over a ternary code row. */
+static int64_t tern_dot(const uint32_t* row, int64_t nwords, const int64_t* lut) {
+  int64_t S = 0;
+  for (int64_t w = 0; w < nwords; ++w) {
+    const uint32_t word = row[w];
+    const int64_t* l = lut + w * 4 * 256;
+    S += l[word & 0xff] + l[256 + ((word >> 8) & 0xff)] + l[512 + ((word >> 16) & 0xff)] + l[768 + (word >> 24)];
+  }
+  return S;
+}
+
 /* ------------------------------------------------------ ternary GEMV ---- */
 /* Reference: kernels/ternary_gemv.py:76-153.  y[b,n] = alpha[n] * rstd *
  * sum_k (c-1) * x[b,k]*w[k].  The sum is the exact integer contraction of the
@@ -131,19 +156,16 @@ void orc_ternary_gemv(const float* x, int64_t batch, int64_t k, const uint32_t* 
     if (rms_w) rstd = rstd_of(orc_r128_sumsq(xr, k), (int)k, eps);
     const int s = orc_fxa_shift(xh, k);
     for (int64_t i = 0; i < k; ++i) X[i] = (s == FXA_NONFINITE) ? 0 : fxa_encode(xh[i], s);
+    int64_t* lut = tern_lut(X, k);
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < n; ++r) {
-      const uint32_t* row = codes + r * nwords;
-      int64_t S = 0;
-      for (int64_t w = 0; w < nwords; ++w) {
-        const uint32_t word = row[w];
-        for (int i = 0; i < 16; ++i) S += ((int64_t)((word >> (2 * i)) & 3u) - 1) * X[w * 16 + i];
-      }
+      const int64_t S = tern_dot(codes + r * nwords, nwords, lut);
       float v = (s == FXA_NONFINITE) ? f_of(0x7fc00000u) : fxa_value(S, s);
       if (rms_w) v = v * rstd;
       v = v * alpha[r];
       y[b * n + r] = out_bf16 ? bf(v) : v;
     }
+    free(lut);
   }
   free(xh);
   free(X);
@@ -155,16 +177,6 @@ static int fxa_row(const float* v, int64_t k, int64_t* X) {
   const int s = orc_fxa_shift(v, k);
   for (int64_t i = 0; i < k; ++i) X[i] = (s == FXA_NONFINITE) ? 0 : fxa_encode(v[i], s);
   return s;
-}
-
-/* Exact sum_k (c_k - 1) * X_k over a ternary code row. */
-static int64_t tern_dot(const uint32_t* row, int64_t nwords, const int64_t* X) {
-  int64_t S = 0;
-  for (int64_t w = 0; w < nwords; ++w) {
-    const uint32_t word = row[w];
-    for (int i = 0; i < 16; ++i) S += ((int64_t)((word >> (2 * i)) & 3u) - 1) * X[w * 16 + i];
-  }
-  return S;
 }
 
 static inline float fxa_val_or_nan(int64_t S, int s) {
@@ -245,14 +257,16 @@ void orc_expert_gemv(const float* x, int64_t x_div, const int32_t* ids, int64_t 
   int64_t* X = (int64_t*)malloc(sizeof(int64_t) * K);
   for (int64_t z = 0; z < slots; ++z) {
     const int s = fxa_row(x + (z / x_div) * K, K, X);
+    int64_t* lut = tern_lut(X, K);
     const int32_t e = ids[z];
     const int ok = e >= 0 && e < E;
 #pragma omp parallel for schedule(static)
     for (int64_t n = 0; n < N; ++n) {
       float v = f_of(0x7fc00000u);
-      if (ok) v = fxa_val_or_nan(tern_dot(codes + ((int64_t)e * N + n) * nwords, nwords, X), s) * alpha[e * N + n];
+      if (ok) v = fxa_val_or_nan(tern_dot(codes + ((int64_t)e * N + n) * nwords, nwords, lut), s) * alpha[e * N + n];
       y[z * N + n] = out_bf16 ? bf(v) : v;
     }
+    free(lut);
   }
   free(X);
 }
@@ -265,6 +279,7 @@ void orc_expert_swiglu(const float* x, int64_t T, int64_t topk, int64_t K, const
   int64_t* X = (int64_t*)malloc(sizeof(int64_t) * K);
   for (int64_t t = 0; t < T; ++t) {
     const int s = fxa_row(x + t * K, K, X);
+    int64_t* lut = tern_lut(X, K);
     for (int64_t j = 0; j < topk; ++j) {
       const int32_t e = ids[t * topk + j];
       const int ok = e >= 0 && e < E;
@@ -273,8 +288,8 @@ void orc_expert_swiglu(const float* x, int64_t T, int64_t topk, int64_t K, const
         float out = f_of(0x7fc00000u);
         if (ok) {
           const uint32_t* base = codes + (int64_t)e * 2 * I * nwords;
-          float up = fxa_val_or_nan(tern_dot(base + n * nwords, nwords, X), s) * alpha[e * 2 * I + n];
-          float gate = fxa_val_or_nan(tern_dot(base + (I + n) * nwords, nwords, X), s) * alpha[e * 2 * I + I + n];
+          float up = fxa_val_or_nan(tern_dot(base + n * nwords, nwords, lut), s) * alpha[e * 2 * I + n];
+          float gate = fxa_val_or_nan(tern_dot(base + (I + n) * nwords, nwords, lut), s) * alpha[e * 2 * I + I + n];
           up = fminf(fmaxf(up, -7.0f), 7.0f);
           gate = fminf(gate, 7.0f);
           out = (up * gate) * sigmoid_(gate);
@@ -282,6 +297,7 @@ void orc_expert_swiglu(const float* x, int64_t T, int64_t topk, int64_t K, const
         h[(t * topk + j) * I + n] = out_bf16 ? bf(out) : out;
       }
     }
+    free(lut);
   }
   free(X);
 }
@@ -297,9 +313,13 @@ void orc_expert_down_reduce(const float* h, int64_t T, int64_t topk, int64_t K, 
                             const float* residual, int mode, int out_bf16, float* out) {
   const int64_t nwords = K / 16;
   int64_t* X = (int64_t*)malloc(sizeof(int64_t) * K * topk);
+  int64_t** luts = (int64_t**)malloc(sizeof(int64_t*) * topk);
   int* sh = (int*)malloc(sizeof(int) * topk);
   for (int64_t t = 0; t < T; ++t) {
-    for (int64_t j = 0; j < topk; ++j) sh[j] = fxa_row(h + (t * topk + j) * K, K, X + j * K);
+    for (int64_t j = 0; j < topk; ++j) {
+      sh[j] = fxa_row(h + (t * topk + j) * K, K, X + j * K);
+      luts[j] = tern_lut(X + j * K, K);
+    }
 #pragma omp parallel for schedule(static)
     for (int64_t n = 0; n < N; ++n) {
       float acc = 0.0f;
@@ -307,7 +327,7 @@ void orc_expert_down_reduce(const float* h, int64_t T, int64_t topk, int64_t K, 
         int32_t e = ids[t * topk + j];
         const int ok = e >= 0 && e < E;
         if (!ok) e = 0;
-        float v = ok ? fxa_val_or_nan(tern_dot(codes + ((int64_t)e * N + n) * nwords, nwords, X + j * K), sh[j])
+        float v = ok ? fxa_val_or_nan(tern_dot(codes + ((int64_t)e * N + n) * nwords, nwords, luts[j]), sh[j])
                      : f_of(0x7fc00000u);
         const float w = wt[t * topk + j];
         if (mode == 0) {
@@ -321,9 +341,11 @@ void orc_expert_down_reduce(const float* h, int64_t T, int64_t topk, int64_t K, 
       if (residual) acc = acc + residual[t * N + n];
       out[t * N + n] = out_bf16 ? bf(acc) : acc;
     }
+    for (int64_t j = 0; j < topk; ++j) free(luts[j]);
   }
   free(X);
   free(sh);
+  free(luts);
 }
 
 /* Reference: kernels/fused_norm.py:60-97. */
@@ -461,6 +483,10 @@ void orc_rtn4_gemv(const float* x, int64_t B, int64_t K, const uint32_t* codes, 
       Xg[g] = 0;
       for (int64_t k = g * G; k < (g + 1) * G; ++k) Xg[g] += X[k];
     }
+    /* byte LUT: entry [q][b] = (b & 15) * X[2q] + (b >> 4) * X[2q + 1] */
+    int64_t* lut = (int64_t*)malloc(sizeof(int64_t) * (K / 2) * 256);
+    for (int64_t q = 0; q < K / 2; ++q)
+      for (int bb = 0; bb < 256; ++bb) lut[q * 256 + bb] = (int64_t)(bb & 15) * X[2 * q] + (int64_t)(bb >> 4) * X[2 * q + 1];
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < N; ++r) {
       const int64_t pr = row_index ? row_index[r] : r;
@@ -468,7 +494,11 @@ void orc_rtn4_gemv(const float* x, int64_t B, int64_t K, const uint32_t* codes, 
       double acc = 0.0;
       for (int64_t g = 0; g < ng; ++g) {
         int64_t C = 0;
-        for (int64_t k = g * G; k < (g + 1) * G; ++k) C += (int64_t)((row[k >> 3] >> (4 * (k & 7))) & 15u) * X[k];
+        for (int64_t w = g * G / 8; w < (g + 1) * G / 8; ++w) {
+          const uint32_t word = row[w];
+          const int64_t* l = lut + w * 4 * 256;
+          C += l[word & 0xff] + l[256 + ((word >> 8) & 0xff)] + l[512 + ((word >> 16) & 0xff)] + l[768 + (word >> 24)];
+        }
         const float sg = scales[pr * ng + g];
         const float bg = biases ? biases[pr * ng + g] : -8.0f * sg;
         acc = (acc + (double)sg * (double)C) + (double)bg * (double)Xg[g];
@@ -476,6 +506,7 @@ void orc_rtn4_gemv(const float* x, int64_t B, int64_t K, const uint32_t* codes, 
       const float v = (s == FXA_NONFINITE) ? f_of(0x7fc00000u) : (float)(acc * pow2d(-s));
       y[b * N + r] = out_bf16 ? bf(v) : v;
     }
+    free(lut);
   }
   free(X);
   free(Xg);
@@ -555,4 +586,83 @@ void orc_rtn4_embedding(const int64_t* ids, int64_t B, const uint32_t* codes, co
       out[b * H + k] = out_bf16 ? bf(v) : v;
     }
   }
+}
+
+/* ------------------------------------------------------- synthetic ---- */
+/* Same generator as the CUDA library's maple_synth_* (integer hashing, one
+ * fp32 multiply-add, one rounding), written independently. */
+static inline uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ULL;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+static inline uint64_t skey(uint64_t seed, uint64_t stream) { return mix64(mix64(seed) ^ (stream * 0x9E3779B97F4A7C15ULL)); }
+static inline uint64_t hat(uint64_t key, uint64_t i) { return mix64(key ^ (i * 0xD1B54A32D192ED03ULL)); }
+static inline float ncst(double scale) { return (float)(scale / sqrt(4.0 * (65536.0 * 65536.0 - 1.0) / 12.0)); }
+static inline float nat(uint64_t key, uint64_t i, float c) {
+  const uint64_t h = hat(key, i);
+  const int s = (int)(h & 0xffff) + (int)((h >> 16) & 0xffff) + (int)((h >> 32) & 0xffff) + (int)(h >> 48);
+  return (float)(s - 131070) * c;
+}
+
+void orc_synth_ternary(uint64_t seed, uint64_t stream, int64_t n_words, uint32_t* out) {
+  const uint64_t key = skey(seed, stream);
+#pragma omp parallel for schedule(static)
+  for (int64_t w = 0; w < n_words; ++w) {
+    uint32_t word = 0;
+    for (int q = 0; q < 4; ++q) {
+      const uint64_t h = hat(key, 4 * (uint64_t)w + q);
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t u = (uint32_t)((h >> (16 * j)) & 0xffffu);
+        const uint32_t code = u < 26214u ? 1u : (u < 45875u ? 0u : 2u);
+        word |= code << (2 * (4 * q + j));
+      }
+    }
+    out[w] = word;
+  }
+}
+
+/* out_bf16: round each value to bf16 (stored as fp32). */
+void orc_synth_normal(uint64_t seed, uint64_t stream, int64_t n, double scale, float offset, int use_abs,
+                      int out_bf16, float* out) {
+  const uint64_t key = skey(seed, stream);
+  const float c = ncst(scale);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    float v = nat(key, (uint64_t)i, c);
+    if (use_abs) v = fabsf(v);
+    v = v + offset;
+    out[i] = out_bf16 ? bf(v) : v;
+  }
+}
+
+void orc_synth_rtn4_sym(uint64_t seed, uint64_t stream, int64_t rows, int64_t k, int64_t group, double scale,
+                        uint32_t* codes, float* scales) {
+  const uint64_t key = skey(seed, stream);
+  const float c = ncst(scale);
+  const int64_t ng = k / group;
+#pragma omp parallel for schedule(static)
+  for (int64_t rg = 0; rg < rows * ng; ++rg) {
+    const int64_t r = rg / ng, g = rg % ng;
+    const int64_t base = r * k + g * group;
+    float amax = 0.0f;
+    for (int64_t i = 0; i < group; ++i) amax = fmaxf(amax, fabsf(nat(key, (uint64_t)(base + i), c)));
+    const float sc = amax / 7.0f;
+    for (int64_t w = 0; w < group / 8; ++w) {
+      uint32_t word = 0;
+      for (int j = 0; j < 8; ++j) {
+        float q = 0.0f;
+        if (sc > 0.0f) q = fminf(fmaxf(rintf(nat(key, (uint64_t)(base + 8 * w + j), c) / sc), -8.0f), 7.0f);
+        word |= (uint32_t)((int)q + 8) << (4 * j);
+      }
+      codes[(base >> 3) + w] = word;
+    }
+    scales[rg] = bf(sc);
+  }
+}
+
+void orc_synth_tokens(uint64_t seed, uint64_t stream, int64_t n, int64_t vocab, int64_t* out) {
+  const uint64_t key = skey(seed, stream);
+  for (int64_t i = 0; i < n; ++i) out[i] = (int64_t)(hat(key, (uint64_t)i) % (uint64_t)vocab);
 }

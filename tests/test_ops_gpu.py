@@ -261,3 +261,26 @@ def test_embeddings(cuda, K):
     r = K.rtn4_embedding(to_dev(ids, cuda), to_dev(packed, cuda), to_dev(s, cuda, torch.bfloat16),
                          to_dev(b, cuda, torch.bfloat16), group_size=64)
     np.testing.assert_array_equal(to_np(r), oracle.rtn4_embedding(ids, packed, s, b, 64, out_bf16=False))
+
+
+def test_synthetic_generator_matches_oracle(cuda):
+    """The device generator and the oracle's independent one agree bit for bit."""
+    from maple_flash_dgx_spark_b200 import synth as S
+    from oracle import model as om
+
+    t = S._ternary(5, 77, (64, 128), cuda)
+    np.testing.assert_array_equal(to_np(t.view(torch.int32)).view(np.uint32), om.synth_ternary(5, 77, (64, 128)))
+    n = S._normal(5, 78, (3000,), cuda, 0.02, 1e-3, True)
+    np.testing.assert_array_equal(to_np(n), om.synth_normal(5, 78, (3000,), 0.02, 1e-3, True))
+    f = S._normal(5, 79, (3000,), cuda, 0.02, 1.0, dtype=torch.float32)
+    np.testing.assert_array_equal(to_np(f), om.synth_normal(5, 79, (3000,), 0.02, 1.0, bf16=False))
+    codes = torch.empty(40, 2048 // 8, dtype=torch.int32, device=cuda).view(torch.uint32)
+    scales = torch.empty(40, 16, dtype=torch.bfloat16, device=cuda)
+    from maple_flash_dgx_spark_b200._lib import lib, ptr, stream_ptr
+
+    assert lib().maple_synth_rtn4_sym(5, 80, 40, 2048, 128, 0.02, ptr(codes), ptr(scales), stream_ptr(cuda)) == 0
+    c_o, s_o = om.synth_rtn4_sym(5, 80, 40, 2048, 128, 0.02)
+    np.testing.assert_array_equal(to_np(codes.view(torch.int32)).view(np.uint32), c_o)
+    np.testing.assert_array_equal(to_np(scales), s_o)
+    tok = S.synthetic_tokens(5, 100, 151936, cuda)
+    np.testing.assert_array_equal(to_np(tok), om.synth_tokens(5, 100, 151936))
