@@ -202,12 +202,14 @@ def main():
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ctx0 = int(cache.seen[0])
         with ClockSampler(local) as clocks:
+            torch.cuda.nvtx.range_push("maple_decode")
             start.record()
             for _ in range(Kst):
                 graph.graph.replay()
                 graph.token_ids.copy_(nxt.reshape(1, 1))
             end.record()
             torch.cuda.synchronize(dev)
+            torch.cuda.nvtx.range_pop()
         ms = start.elapsed_time(end)
         if world > 1:
             t = torch.tensor([ms], device=dev)
