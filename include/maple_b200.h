@@ -32,7 +32,8 @@ enum maple_status {
   MAPLE_ERR_TIMEOUT = 4,   /* bounded device wait gave up         (RuntimeError) */
   MAPLE_ERR_CUDA = 5,      /* CUDA launch/runtime error           (RuntimeError) */
   MAPLE_ERR_WORKSPACE = 6, /* workspace missing or too small      (ValueError)   */
-  MAPLE_ERR_ALIGN = 7      /* pointer not 16-byte aligned         (ValueError)   */
+  MAPLE_ERR_ALIGN = 7,     /* pointer not 16-byte aligned         (ValueError)   */
+  MAPLE_ERR_SCRATCH_LIMIT = 8 /* request exceeds a fixed scratch  (ValueError)   */
 };
 
 enum maple_dtype { MAPLE_F32 = 0, MAPLE_BF16 = 1 };
@@ -55,6 +56,22 @@ int maple_ternary_gemv(const void* x, int x_dtype, int64_t batch, int64_t k, int
                        const uint32_t* codes, int64_t n, const void* alpha, int alpha_dtype,
                        const void* rms_w, int rms_dtype, float eps, void* y, int64_t y_row_stride,
                        void* workspace, int64_t workspace_bytes, void* stream);
+
+/* maple_ternary_gemv for callers that cannot allocate device memory (a host
+ * that reaches the library through a thin FFI and holds only its input and
+ * output buffers, or a serving loop whose device memory is all reserved).  No
+ * counterpart in the reference.  Same arguments and result as
+ * maple_ternary_gemv, without the workspace: split-K scratch comes from a
+ * fixed 2 MiB __device__ array inside the library (held on every GPU that
+ * loads it), so it needs batch * splits * n * 16 bytes <= 2 MiB - 16 KiB
+ * (splits = 2 for k = 4096; k <= 2048 uses none) or it returns
+ * MAPLE_ERR_SCRATCH_LIMIT.  The first call on each device looks up the
+ * array's address; make it before any stream capture.  Calls share the
+ * array: calls that can overlap on the GPU race and must be serialised. */
+int maple_ternary_gemv_noalloc(const void* x, int x_dtype, int64_t batch, int64_t k, int64_t x_row_stride,
+                               const uint32_t* codes, int64_t n, const void* alpha, int alpha_dtype,
+                               const void* rms_w, int rms_dtype, float eps, void* y, int64_t y_row_stride,
+                               void* stream);
 
 /* Selected-expert GEMV.  Replaces kernels/ternary_expert.py:125
  * ternary_expert_gemv and linear.py:51 PackedTernaryExperts.forward.

@@ -28,6 +28,7 @@ _ERRORS = {
     5: (RuntimeError, "CUDA launch failed"),
     6: (ValueError, "workspace missing or too small"),
     7: (ValueError, "pointer or stride not 16-byte aligned"),
+    8: (ValueError, "request exceeds the library's fixed scratch"),
 }
 
 _lib = None
@@ -39,6 +40,7 @@ i32, i64, f32, vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_
 _SIGS: dict[str, tuple] = {
     "maple_ternary_gemv_workspace_bytes": (i64, [i64, i64, i64]),
     "maple_ternary_gemv": (i32, [vp, i32, i64, i64, i64, vp, i64, vp, i32, vp, i32, f32, vp, i64, vp, i64, vp]),
+    "maple_ternary_gemv_noalloc": (i32, [vp, i32, i64, i64, i64, vp, i64, vp, i32, vp, i32, f32, vp, i64, vp]),
     "maple_ternary_expert_gemv_workspace_bytes": (i64, [i64, i64, i64]),
     "maple_ternary_expert_gemv": (i32, [vp, i32, i64, i64, vp, i64, i64, vp, i64, i64, vp, i32, vp, i64, vp,
                                         i64, vp]),

@@ -33,6 +33,7 @@ enum Status : int {
   kErrCuda = 5,       // CUDA launch / runtime error (Python: RuntimeError)
   kErrWorkspace = 6,  // caller workspace too small (Python: ValueError)
   kErrAlign = 7,      // pointer or stride misaligned for vector loads (Python: ValueError)
+  kErrScratchLimit = 8,  // request exceeds a fixed internal scratch (Python: ValueError)
 };
 
 enum DType : int { kF32 = 0, kBF16 = 1 };

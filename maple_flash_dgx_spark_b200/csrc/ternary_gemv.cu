@@ -362,3 +362,94 @@ extern "C" int maple_ternary_expert_swiglu(const void* x, int x_dtype, int64_t x
                                           static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? kOk : kErrCuda;
 }
+
+// ---------------------------------------------------------------------------
+// Ternary GEMV for callers that cannot allocate device memory.
+//
+// Some callers of this library own no CUDA allocator: a host that binds the
+// library through a thin foreign-function layer (cgo, JNI, ctypes) and is
+// handed only the input and output buffers, or a serving loop whose device
+// memory is fully reserved up front by its KV-cache pool.  They cannot size,
+// allocate and zero the workspace that maple_ternary_gemv wants for its
+// split-K partials.  This entry point takes no workspace: its scratch is the
+// file-scope array below, a fixed 2 MiB on every GPU that loads the library,
+// held until the process exits.  It never calls cudaMalloc or cudaFree.
+//
+// * The first call on a device looks up the array's device address there
+//   (cudaGetSymbolAddress) and remembers it; make that first call before any
+//   stream capture.
+// * All calls share the one array, which keeps the last call's contents.
+//   The completion tickets are cleared at the start of every call; the split
+//   partials are fully rewritten before they are read.  Two calls that can
+//   run at the same time on the GPU (different streams, no ordering) race on
+//   the array and give wrong results: serialise them.
+// * Requests whose split-K scratch does not fit (see kNoAllocPartialBytes)
+//   return MAPLE_ERR_SCRATCH_LIMIT without launching anything.
+#include <mutex>
+
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = 2 * 1024 * 1024;
+constexpr int64_t kNoAllocTicketBytes = 16 * 1024;  // 4096 completion tickets
+constexpr int64_t kNoAllocPartialBytes = kNoAllocScratchBytes - kNoAllocTicketBytes;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_address[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up once.
+cudaError_t noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_address[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_address[dev] = p;
+  }
+  *out = g_noalloc_address[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" int maple_ternary_gemv_noalloc(const void* x, int x_dtype, int64_t batch, int64_t k,
+                                          int64_t x_row_stride, const uint32_t* codes, int64_t n,
+                                          const void* alpha, int alpha_dtype, const void* rms_w,
+                                          int rms_dtype, float eps, void* y, int64_t y_row_stride,
+                                          void* stream) {
+  if (batch < 0 || n < 0 || k < 0) return kErrShape;
+  if (batch == 0 || n == 0) return kOk;
+  if (int rc = common_checks(x_dtype, alpha_dtype, rms_w, rms_dtype, k)) return rc;
+  if (!x || !codes || !alpha || !y) return kErrShape;
+  if ((reinterpret_cast<uintptr_t>(codes) & 15) != 0) return kErrAlign;
+  if (batch > 65535 || n > (1LL << 30)) return kErrShape;
+  TGemvParams p{};
+  p.x = x; p.codes = codes; p.alpha = alpha; p.rms_w = rms_w; p.y = y;
+  p.x_stride = x_row_stride; p.y_stride = y_row_stride; p.x_div = 1;
+  p.rows = (int)n; p.n_out = (int)n; p.n_experts = 1;
+  p.K = (int)k; p.nwords = (int)(k / 16); p.eps = eps;
+  p.ks = gemv_splits(p.nwords);
+  const int iters_total = (p.nwords + 15) / 16;
+  p.iters = (iters_total + p.ks - 1) / p.ks;
+  p.ks = (iters_total + p.iters - 1) / p.iters;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p.ks > 1) {
+    const int64_t tickets = batch * ((n + 63) / 64);
+    const int64_t partials = batch * p.ks * n * 4 * (int64_t)sizeof(int);
+    if (tickets * (int64_t)sizeof(unsigned) > kNoAllocTicketBytes || partials > kNoAllocPartialBytes)
+      return kErrScratchLimit;
+    void* base = nullptr;
+    if (noalloc_scratch(&base) != cudaSuccess) return kErrCuda;
+    if (cudaMemsetAsync(base, 0, tickets * sizeof(unsigned), st) != cudaSuccess) return kErrCuda;
+    p.tickets = static_cast<unsigned*>(base);
+    p.ws = reinterpret_cast<int*>(static_cast<char*>(base) + kNoAllocTicketBytes);
+  }
+  const cudaError_t e = dispatch<kPlain>(p, x_dtype, alpha_dtype, rms_dtype, (int)batch, st);
+  return e == cudaSuccess ? kOk : kErrCuda;
+}
