@@ -103,11 +103,15 @@ __global__ void __launch_bounds__(32) qk_norm_rope_store_kernel(QkvParams p) {
   const int base = is_q ? head * D : p.Hq * D + (head - p.Hq) * D;
   const void* w = is_q ? p.q_w : p.k_w;
   float part[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int u = 0; u * 32 < D; ++u) {
-    const int d = lane + 32 * u;
-    const float v = load_f<XT>(row, base + d);
-    xh[d] = v;
-    part[u & 3] = __fmaf_rn(v, v, part[u & 3]);
+  float xv[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) xv[u] = (u * 32 < D) ? load_f<XT>(row, base + lane + 32 * u) : 0.0f;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    if (u * 32 < D) {
+      xh[lane + 32 * u] = xv[u];
+      part[u & 3] = __fmaf_rn(xv[u], xv[u], part[u & 3]);
+    }
   }
   const float rstd = rstd_of(r128_lane_finish(part[0], part[1], part[2], part[3]), D, p.eps);
   for (int u = 0; u * 32 < D; ++u) {
@@ -311,20 +315,44 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  for (int idx = tid; idx < G * D; idx += 128) {
-    const int g = idx / D, d = idx - (idx / D) * D;
+  // One warp per query head: lanes own dims lane + 32u; splits in order, their
+  // partials fetched four at a time.
+  for (int g = warp; g < G; g += 4) {
     const int hq = h * G + g;
     const float* ml = p.ws_ml + ((int64_t)b * p.Hq + hq) * p.NS * 2;
     const float* ac = p.ws_acc + ((int64_t)b * p.Hq + hq) * p.NS * D;
     float M = ninf;
-    for (int j = 0; j < ns; ++j) M = fmaxf(M, __ldcg(ml + 2 * j));
-    float num = 0.0f, den = 0.0f;
-    for (int j = 0; j < ns; ++j) {
-      const float w = mexp(__fsub_rn(__ldcg(ml + 2 * j), M));
-      num = __fmaf_rn(w, __ldcg(ac + (int64_t)j * D + d), num);
-      den = __fmaf_rn(w, __ldcg(ml + 2 * j + 1), den);
+    for (int j = lane; j < ns; j += 32) M = fmaxf(M, __ldcg(ml + 2 * j));
+    M = warp_max(M);
+    float num[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) num[u] = 0.0f;
+    float den = 0.0f;
+    for (int j0 = 0; j0 < ns; j0 += 4) {
+      float mj[4], lj[4], aj[4][U];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int j = j0 + i;
+        if (j < ns) {
+          mj[i] = __ldcg(ml + 2 * j);
+          lj[i] = __ldcg(ml + 2 * j + 1);
+#pragma unroll
+          for (int u = 0; u < U; ++u) aj[i][u] = __ldcg(ac + (int64_t)j * D + lane + 32 * u);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (j0 + i < ns) {
+          const float w = mexp(__fsub_rn(mj[i], M));
+          den = __fmaf_rn(w, lj[i], den);
+#pragma unroll
+          for (int u = 0; u < U; ++u) num[u] = __fmaf_rn(w, aj[i][u], num[u]);
+        }
+      }
     }
-    store_f<XT>(static_cast<char*>(p.out) + (b * p.o_sb + hq * p.o_sh) * es, d, __fdiv_rn(num, den));
+    char* o = static_cast<char*>(p.out) + (b * p.o_sb + hq * p.o_sh) * es;
+#pragma unroll
+    for (int u = 0; u < U; ++u) store_f<XT>(o, lane + 32 * u, __fdiv_rn(num[u], den));
   }
 }
 
@@ -420,7 +448,7 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
 #define MB_ATT(XT, DD)                                                                        \
   do {                                                                                        \
     auto kern = gqa_decode_kernel<XT, DD>;                                                    \
-    if (smem > 48 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (smem > 32 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
     if (e == cudaSuccess) kern<<<grid, 128, smem, st>>>(p);                                   \
   } while (0)
   if (x_dtype == kBF16) {

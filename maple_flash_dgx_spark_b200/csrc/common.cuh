@@ -189,4 +189,53 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
   return r;
 }
 
+// Plain 16-byte load (activations written by the previous kernel).
+__device__ __forceinline__ uint4 ld_u4(const void* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+
+// Widen the 16 bytes of a vector load to fp32 values (8 bf16 or 4 fp32).
+template <int XT>
+__device__ __forceinline__ void widen_u4(const uint4& r, float* out) {
+  if constexpr (XT == kBF16) {
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      out[2 * i] = __uint_as_float(w[i] << 16);
+      out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  } else {
+    out[0] = __uint_as_float(r.x); out[1] = __uint_as_float(r.y);
+    out[2] = __uint_as_float(r.z); out[3] = __uint_as_float(r.w);
+  }
+}
+
+// Copy src[0:n) (dtype XT) into dst[0:n) as fp32 with 16-byte loads that
+// are all issued before any is used (one memory round trip for rows of up to
+// NT * MAXC vectors).  Threads 0..NT-1 of the block take part (the caller
+// synchronises).  Falls back to element loads when src is not 16-byte
+// aligned or n is not a whole number of vectors.
+template <int XT, int NT, int MAXC>
+__device__ __forceinline__ void stage_row(const void* src, int n, float* dst, int tid) {
+  constexpr int EPC = XT == kBF16 ? 8 : 4;
+  if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && n % EPC == 0) {
+    const int nch = n / EPC;
+    const char* s8 = static_cast<const char*>(src);
+    uint4 r[MAXC];
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * NT;
+      if (c < nch) r[i] = ld_u4(s8 + (size_t)c * 16);
+    }
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * NT;
+      if (c < nch) widen_u4<XT>(r[i], dst + (size_t)c * EPC);
+    }
+    for (int c = tid + MAXC * NT; c < nch; c += NT) widen_u4<XT>(ld_u4(s8 + (size_t)c * 16), dst + (size_t)c * EPC);
+  } else {
+    for (int k = tid; k < n; k += NT) dst[k] = load_f<XT>(src, k);
+  }
+}
+
 }  // namespace mb

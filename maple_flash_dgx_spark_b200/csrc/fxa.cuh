@@ -55,25 +55,29 @@ struct FxaShared {
 
 // Block prologue (blockDim.x == 128).  Reads x[0:K) once (times rms_w when
 // RMS), computes the FXA shift over all K, the R128 rstd of the raw x (RMS),
-// and the digit fragments for local codes [0, iters*256) starting at k_lo.
-// xsm must hold K floats.  Ends with __syncthreads().
+// and the digit fragments for local codes [0, iters*Pack::kIter) starting at
+// k_lo.  xsm must hold K floats and wsm (RMS only) K floats.  Ends with
+// __syncthreads().
 template <int XT, int RT, bool RMS, int BITS = 2>
 __device__ __forceinline__ void fxa_block_prologue(const void* xr, const void* rms_w, int K, float eps,
                                                    int k_lo, int iters, float* xsm, uint2* frag,
-                                                   FxaShared& sh) {
+                                                   FxaShared& sh, float* wsm = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  stage_row<XT, 128, 4>(xr, K, xsm, tid);
+  if constexpr (RMS) stage_row<RT, 128, 4>(rms_w, K, wsm, tid);
+  for (int e = tid; e < iters * Pack<BITS>::kMmas * 32; e += 128) frag[e] = make_uint2(0u, 0u);
+  __syncthreads();
   float ss = 0.0f;
   unsigned amax = 0;
   for (int k = tid; k < K; k += 128) {
-    float v = load_f<XT>(xr, k);
+    float v = xsm[k];
     if constexpr (RMS) {
       ss = __fmaf_rn(v, v, ss);
-      v = __fmul_rn(v, load_f<RT>(rms_w, k));
+      v = __fmul_rn(v, wsm[k]);
+      xsm[k] = v;
     }
-    xsm[k] = v;
     amax = max(amax, __float_as_uint(v) & 0x7fffffffu);
   }
-  for (int e = tid; e < iters * Pack<BITS>::kMmas * 32; e += 128) frag[e] = make_uint2(0u, 0u);
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, m));
   if (lane == 0) sh.amax[warp] = amax;
@@ -122,13 +126,11 @@ template <int XT>
 __device__ __forceinline__ int fxa_warp_prologue(const void* xr, int K, int iters, float* xsm,
                                                  uint2* frag, int (&tot)[4]) {
   const int lane = threadIdx.x & 31;
-  unsigned amax = 0;
-  for (int k = lane; k < K; k += 32) {
-    const float v = load_f<XT>(xr, k);
-    xsm[k] = v;
-    amax = max(amax, __float_as_uint(v) & 0x7fffffffu);
-  }
+  stage_row<XT, 32, 4>(xr, K, xsm, lane);
   for (int e = lane; e < iters * 256; e += 32) frag[e] = make_uint2(0u, 0u);
+  __syncwarp();
+  unsigned amax = 0;
+  for (int k = lane; k < K; k += 32) amax = max(amax, __float_as_uint(xsm[k]) & 0x7fffffffu);
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, m));
   const int s = fxa_shift(amax);

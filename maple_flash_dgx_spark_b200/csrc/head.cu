@@ -180,7 +180,27 @@ __global__ void __launch_bounds__(256) argmax_kernel(const void* logits, int64_t
   float bv = __int_as_float(0xff800000);
   int bi = 0x7fffffff;
   const int lo = blockIdx.x * 8192, hi = min(V, lo + 8192);
-  for (int k = lo + tid; k < hi; k += 256) {
+  constexpr int EPC = XT == kBF16 ? 8 : 4;   // elements per 16-byte vector
+  constexpr int CPT = 8192 / EPC / 256;     // vectors per thread
+  const int nvec = ((reinterpret_cast<uintptr_t>(row) & 15) == 0) ? (hi - lo) / EPC : 0;
+  uint4 r[CPT];
+#pragma unroll
+  for (int i = 0; i < CPT; ++i) {
+    const int c = tid + 256 * i;
+    if (c < nvec) r[i] = ld_u4(row + (size_t)(lo + c * EPC) * (XT == kBF16 ? 2 : 4));
+  }
+#pragma unroll
+  for (int i = 0; i < CPT; ++i) {
+    const int c = tid + 256 * i;
+    if (c < nvec) {
+      float f[EPC];
+      widen_u4<XT>(r[i], f);
+#pragma unroll
+      for (int e = 0; e < EPC; ++e)
+        if (better(f[e], lo + c * EPC + e, bv, bi)) { bv = f[e]; bi = lo + c * EPC + e; }
+    }
+  }
+  for (int k = lo + nvec * EPC + tid; k < hi; k += 256) {
     const float v = load_f<XT>(row, k);
     if (better(v, k, bv, bi)) { bv = v; bi = k; }
   }
@@ -422,7 +442,7 @@ int rtn4_launch(Rtn4Params& p, int x_dtype, int s_dtype, int64_t batch, void* st
 #define MB_R4(XT, ST)                                                                        \
   do {                                                                                       \
     auto kern = rtn4_gemv_kernel<XT, ST>;                                                    \
-    if (smem > 48 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (smem > 32 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
     if (e == cudaSuccess) kern<<<grid, 128, smem, st>>>(p);                                  \
   } while (0)
   if (x_dtype == kBF16) { if (s_dtype == kBF16) MB_R4(kBF16, kBF16); else MB_R4(kBF16, kF32); }

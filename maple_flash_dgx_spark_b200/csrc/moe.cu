@@ -30,30 +30,48 @@ constexpr int kRouterWarps = 8;
 
 template <int XT, int GT>
 __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
-  __shared__ float s_part[kRouterWarps][128];
+  extern __shared__ __align__(16) unsigned char rsm[];  // x as fp32 [K] | gate rows raw [8][K]
   __shared__ int s_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tok = blockIdx.y;
-  const int e = blockIdx.x * kRouterWarps + warp;
+  const int e0 = blockIdx.x * kRouterWarps;
+  const int ne = min(kRouterWarps, p.E - e0);
+  const int ges = GT == kBF16 ? 2 : 4;
+  float* xs = reinterpret_cast<float*>(rsm);
+  unsigned char* gs = rsm + (size_t)p.K * sizeof(float);
+  // Gate rows of this CTA's experts (contiguous), 16-byte loads issued together.
+  {
+    const char* gsrc = static_cast<const char*>(p.gate) + (int64_t)e0 * p.K * ges;
+    const int nbytes = ne * p.K * ges;
+    const bool vec = ((reinterpret_cast<uintptr_t>(gsrc) & 15) == 0) && (nbytes % 16 == 0);
+    if (vec) {
+      const int nch = nbytes / 16;
+      uint4 r[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) if (tid + 256 * i < nch) r[i] = ld_stream_u4(gsrc + (size_t)(tid + 256 * i) * 16);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) if (tid + 256 * i < nch) *reinterpret_cast<uint4*>(gs + (size_t)(tid + 256 * i) * 16) = r[i];
+      for (int c = tid + 2048; c < nch; c += 256) *reinterpret_cast<uint4*>(gs + (size_t)c * 16) = ld_stream_u4(gsrc + (size_t)c * 16);
+    } else {
+      for (int b = tid; b < nbytes; b += 256) gs[b] = gsrc[b];
+    }
+  }
   const char* xr = static_cast<const char*>(p.x) + tok * p.x_stride * (XT == kBF16 ? 2 : 4);
-  if (e < p.E) {
-    const char* gr = static_cast<const char*>(p.gate) + (int64_t)e * p.K * (GT == kBF16 ? 2 : 4);
-    // Lane l owns partials j = 4l .. 4l+3 (elements j, j+128, ...).
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  stage_row<XT, 256, 2>(xr, p.K, xs, tid);
+  __syncthreads();
+  if (warp < ne) {
+    const unsigned char* gr = gs + (size_t)warp * p.K * ges;
+    // Lane l owns R128 partials j = l + 32u (elements j, j+128, ...).
+    float pj[4] = {0.f, 0.f, 0.f, 0.f};
     for (int c = 0; c < p.K; c += 128) {
-      const int k = c + 4 * lane;
-      if (k < p.K) {
-        a0 = __fmaf_rn(load_f<XT>(xr, k + 0), load_f<GT>(gr, k + 0), a0);
-        a1 = __fmaf_rn(load_f<XT>(xr, k + 1), load_f<GT>(gr, k + 1), a1);
-        a2 = __fmaf_rn(load_f<XT>(xr, k + 2), load_f<GT>(gr, k + 2), a2);
-        a3 = __fmaf_rn(load_f<XT>(xr, k + 3), load_f<GT>(gr, k + 3), a3);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int k = c + lane + 32 * u;
+        if (k < p.K) pj[u] = __fmaf_rn(xs[k], load_f<GT>(gr, k), pj[u]);
       }
     }
-    float* pp = s_part[warp];
-    pp[4 * lane + 0] = a0; pp[4 * lane + 1] = a1; pp[4 * lane + 2] = a2; pp[4 * lane + 3] = a3;
-    __syncwarp();
-    const float logit = r128_smem_finish(pp, lane);
-    if (lane == 0) p.logits[(int64_t)tok * p.E + e] = logit;
+    const float logit = r128_lane_finish(pj[0], pj[1], pj[2], pj[3]);
+    if (lane == 0) p.logits[(int64_t)tok * p.E + e0 + warp] = logit;
   }
   __threadfence();
   __syncthreads();
@@ -272,13 +290,20 @@ extern "C" int maple_router_topk(const void* x, int x_dtype, int64_t x_row_strid
   p.x_stride = x_row_stride; p.E = (int)n_experts; p.K = (int)k; p.topk = (int)topk;
   dim3 grid((unsigned)((n_experts + kRouterWarps - 1) / kRouterWarps), (unsigned)tokens);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t smem = (size_t)k * sizeof(float) + (size_t)kRouterWarps * k * (gate_dtype == kBF16 ? 2 : 4);
+  if (smem > 200 * 1024) return kErrShape;
+#define MB_ROUTER(XT, GT)                                                                                 \
+  do {                                                                                                    \
+    if (smem > 32 * 1024)                                                                                 \
+      cudaFuncSetAttribute(router_kernel<XT, GT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    router_kernel<XT, GT><<<grid, 256, smem, st>>>(p);                                                    \
+  } while (0)
   if (x_dtype == kBF16) {
-    if (gate_dtype == kBF16) router_kernel<kBF16, kBF16><<<grid, 256, 0, st>>>(p);
-    else router_kernel<kBF16, kF32><<<grid, 256, 0, st>>>(p);
+    if (gate_dtype == kBF16) MB_ROUTER(kBF16, kBF16); else MB_ROUTER(kBF16, kF32);
   } else {
-    if (gate_dtype == kBF16) router_kernel<kF32, kBF16><<<grid, 256, 0, st>>>(p);
-    else router_kernel<kF32, kF32><<<grid, 256, 0, st>>>(p);
+    if (gate_dtype == kBF16) MB_ROUTER(kF32, kBF16); else MB_ROUTER(kF32, kF32);
   }
+#undef MB_ROUTER
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
@@ -288,7 +313,7 @@ cudaError_t launch_down(const DownParams& p, int T, cudaStream_t st) {
   const size_t per_warp = (size_t)p.iters * 256 * sizeof(uint2) + (size_t)p.K * sizeof(float);
   const size_t smem = per_warp * kDownMaxTopk;
   auto kern = down_sum_kernel<XT, AT, MODE>;
-  if (smem > 48 * 1024) {
+  if (smem > 32 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }

@@ -11,21 +11,27 @@ __global__ void __launch_bounds__(128) rms_norm_kernel(const void* x, const void
                                                        void* residual, void* out, int64_t x_stride,
                                                        int64_t y_stride, int64_t r_stride,
                                                        int64_t o_stride, int N, float eps) {
-  extern __shared__ float srow[];
+  extern __shared__ float srow[];  // x | y | w, N floats each
   __shared__ float part[128];
   __shared__ float s_rstd;
   const int tid = threadIdx.x;
   const int row = blockIdx.x;
   const int es = XT == kBF16 ? 2 : 4;
-  const char* xr = static_cast<const char*>(x) + row * x_stride * es;
+  float* xs = srow;
+  float* ys = srow + N;
+  float* wsm = srow + 2 * N;
+  stage_row<XT, 128, 4>(static_cast<const char*>(x) + row * x_stride * es, N, xs, tid);
+  if constexpr (ADD) stage_row<XT, 128, 4>(static_cast<const char*>(y) + row * y_stride * es, N, ys, tid);
+  stage_row<WT, 128, 4>(w, N, wsm, tid);
+  __syncthreads();
   float ss = 0.0f;
   for (int k = tid; k < N; k += 128) {
-    float v = load_f<XT>(xr, k);
+    float v = xs[k];
     if constexpr (ADD) {
-      v = __fadd_rn(v, load_f<XT>(static_cast<const char*>(y) + row * y_stride * es, k));
+      v = __fadd_rn(v, ys[k]);
       store_f<XT>(static_cast<char*>(residual) + row * r_stride * es, k, v);
+      xs[k] = v;
     }
-    srow[k] = v;
     ss = __fmaf_rn(v, v, ss);
   }
   part[tid] = ss;
@@ -37,8 +43,7 @@ __global__ void __launch_bounds__(128) rms_norm_kernel(const void* x, const void
   __syncthreads();
   const float rstd = s_rstd;
   char* orow = static_cast<char*>(out) + row * o_stride * es;
-  for (int k = tid; k < N; k += 128)
-    store_f<XT>(orow, k, __fmul_rn(__fmul_rn(srow[k], rstd), load_f<WT>(w, k)));
+  for (int k = tid; k < N; k += 128) store_f<XT>(orow, k, __fmul_rn(__fmul_rn(xs[k], rstd), wsm[k]));
 }
 
 template <bool ADD>
@@ -49,9 +54,15 @@ int launch_norm(const void* x, const void* y, int x_dtype, int64_t rows, int64_t
   if (rows == 0) return kOk;
   if ((x_dtype != kF32 && x_dtype != kBF16) || (w_dtype != kF32 && w_dtype != kBF16)) return kErrDtype;
   if (!x || !w || !out || (ADD && (!y || !residual))) return kErrShape;
-  if (n > 48 * 1024 / 4 || rows > (1LL << 31) - 1) return kErrShape;
+  if (n > 16384 || rows > (1LL << 31) - 1) return kErrShape;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const size_t smem = (size_t)n * sizeof(float);
+  const size_t smem = 3 * (size_t)n * sizeof(float);
+  if (smem > 32 * 1024) {
+    cudaFuncSetAttribute(rms_norm_kernel<kBF16, kBF16, ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(rms_norm_kernel<kBF16, kF32, ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(rms_norm_kernel<kF32, kBF16, ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(rms_norm_kernel<kF32, kF32, ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  }
   const dim3 grid((unsigned)rows);
   if (x_dtype == kBF16) {
     if (w_dtype == kBF16)

@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(128) ternary_gemv_kernel(TGemvParams p) {
   // 2) Activation prologue (shift over all K, fragments for this split).
   const int xrow = z / p.x_div;
   const void* xr = static_cast<const char*>(p.x) + xrow * p.x_stride * (XT == kBF16 ? 2 : 4);
-  fxa_block_prologue<XT, RT, RMS>(xr, p.rms_w, p.K, p.eps, it0 * kIterK, p.iters, xsm, frag, sh);
+  fxa_block_prologue<XT, RT, RMS>(xr, p.rms_w, p.K, p.eps, it0 * kIterK, p.iters, xsm, frag, sh, xsm + p.K);
   const int s = sh.s;
   const bool nan_out = (s == kFxaNonFinite) || bad_id;
 
@@ -214,7 +214,7 @@ int gemv_splits(int64_t nwords) {
 }
 
 size_t gemv_smem(int iters, int K) {
-  return (size_t)iters * 256 * sizeof(uint2) + (size_t)K * sizeof(float);
+  return (size_t)iters * 256 * sizeof(uint2) + 2 * (size_t)K * sizeof(float);
 }
 
 template <int XT, int AT, int RT, bool RMS, int MODE>
@@ -223,7 +223,7 @@ cudaError_t launch_tgemv(const TGemvParams& p, int Z, cudaStream_t st) {
   dim3 grid((p.n_out + per_cta - 1) / per_cta, p.ks, Z);
   const size_t smem = gemv_smem(p.iters, p.K);
   auto kern = ternary_gemv_kernel<XT, AT, RT, RMS, MODE>;
-  if (smem > 48 * 1024) {
+  if (smem > 32 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }

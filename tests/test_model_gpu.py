@@ -91,3 +91,22 @@ def test_model_generate_api(cuda):
     model = build(cfg, 17, cuda)
     out = model.generate(torch.from_numpy(synth_tokens(17, 5, cfg["vocab_size"])), max_tokens=6)
     assert out.shape == (1, 11)
+
+
+def test_cfg2_first_64_greedy_ids_equal_oracle(cuda):
+    """configs[2] (48 layers, V=151936, 512-token prompt): the first 64 greedy
+    ids equal the CPU oracle's (tests/golden/cfg2_greedy.json, made by
+    tests/golden/make_cfg2_greedy.py)."""
+    import json
+    from pathlib import Path
+
+    from maple_flash_dgx_spark_b200.generate import run_generate
+    from maple_flash_dgx_spark_b200.synth import synthetic_config
+
+    gold = json.loads((Path(__file__).parent / "golden" / "cfg2_greedy.json").read_text())
+    cfg = synthetic_config()
+    model = build(cfg, gold["seed"], cuda)
+    assert model.make_cache(max_len=gold["max_len"]).split_len == gold["split_len"]
+    prompt = synth_tokens(gold["seed"], gold["prompt_len"], cfg["vocab_size"])
+    res = run_generate(model, torch.from_numpy(prompt), max_tokens=gold["n_new"], temperature=0.0, log=None)
+    assert res.token_ids == gold["ids"]
