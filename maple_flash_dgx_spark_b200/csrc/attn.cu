@@ -19,6 +19,7 @@
 // bulk copy) completing on an mbarrier; the wait is bounded and a timeout is
 // reported through the error word instead of hanging.
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace mb {
 
@@ -81,6 +82,8 @@ struct QkvParams {
 template <int XT, int WT, int CT>
 __global__ void __launch_bounds__(32) qk_norm_rope_store_kernel(QkvParams p) {
   __shared__ float xh[256];
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x;
   const int head = blockIdx.x, b = blockIdx.y;
   const int D = p.D;
@@ -170,6 +173,8 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
   const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int P = p.P, G = p.G;
   const int es = XT == kBF16 ? 2 : 4;
+  pdl_wait();
+  pdl_trigger();
 
   const int64_t pos = p.seqlen[b];
   const int kv_len = (int)min(pos + 1, (int64_t)p.T);
@@ -387,7 +392,7 @@ extern "C" int maple_apply_qkv_decode(const void* qkv, int x_dtype, int64_t batc
   p.Bc = (int)cache_batch; p.T = (int)max_len; p.use_rope = use_rope; p.eps = eps;
   dim3 grid((unsigned)(num_heads + 2 * num_kv_heads), (unsigned)batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-#define MB_QKV(XT, WT, CT) qk_norm_rope_store_kernel<XT, WT, CT><<<grid, 32, 0, st>>>(p)
+#define MB_QKV(XT, WT, CT) launch_k(qk_norm_rope_store_kernel<XT, WT, CT>, dim3(grid), dim3(32), 0, st, p)
   if (x_dtype == kBF16) {
     if (w_dtype == kBF16) { if (cs_dtype == kBF16) MB_QKV(kBF16, kBF16, kBF16); else MB_QKV(kBF16, kBF16, kF32); }
     else { if (cs_dtype == kBF16) MB_QKV(kBF16, kF32, kBF16); else MB_QKV(kBF16, kF32, kF32); }
@@ -449,7 +454,7 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
   do {                                                                                        \
     auto kern = gqa_decode_kernel<XT, DD>;                                                    \
     if (smem > 32 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    if (e == cudaSuccess) kern<<<grid, 128, smem, st>>>(p);                                   \
+    if (e == cudaSuccess) launch_k(kern, dim3(grid), dim3(128), smem, st, p);                                   \
   } while (0)
   if (x_dtype == kBF16) {
     if (head_dim == 64) MB_ATT(kBF16, 64); else if (head_dim == 128) MB_ATT(kBF16, 128); else MB_ATT(kBF16, 256);

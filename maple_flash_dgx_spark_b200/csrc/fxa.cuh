@@ -158,6 +158,209 @@ __device__ __forceinline__ int fxa_warp_prologue(const void* xr, int K, int iter
   return s;
 }
 
+// ------------------------------------------------------------------ fast --
+// Offset that turns the balanced base-128 digits of X (|X| < 2^26) into the
+// plain digits of u = X + kFxaOffset: d_j = ((u >> 7j) & 127) - 64.
+constexpr int kFxaOffset = 135274560;  // 64 * (1 + 128 + 128^2 + 128^3)
+
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
+
+// X = rint(v * 2^s) in fp32: the scaling by a power of two is exact and
+// |v * 2^s| < 2^26, so this equals the double-precision definition.
+__device__ __forceinline__ int fxa_enc(float v, int s) {
+  const float f = (s <= 127) ? __fmul_rn(v, pow2f(s)) : __fmul_rn(__fmul_rn(v, pow2f(s - 76)), pow2f(76));
+  return __float2int_rn(f);
+}
+
+// Four 7-bit plain digits (digit j of u0..u3) packed in bytes, and the same
+// as signed balanced digits (raw - 64 per byte, two's complement).
+__device__ __forceinline__ uint32_t raw_digits(uint32_t u0, uint32_t u1, uint32_t u2, uint32_t u3, int j) {
+  const int sh = 7 * j;
+  return ((u0 >> sh) & 127u) | (((u1 >> sh) & 127u) << 8) | (((u2 >> sh) & 127u) << 16) |
+         (((u3 >> sh) & 127u) << 24);
+}
+__device__ __forceinline__ uint32_t signed_digits(uint32_t raw) {
+  return ((raw | 0x80808080u) - 0x40404040u) ^ 0x80808080u;
+}
+
+// Shift, rstd and digit totals shared by a block.
+struct FxaBlock {
+  unsigned amax[8];
+  int rawsum[8][4];
+  int s;
+  float rstd;
+  int tot[4];  // sum over the fragment's codes of digit j (balanced)
+};
+
+// Fragment builder for codes [0, iters*Pack::kIter) of the activation xs
+// (fp32 values in shared memory, zero beyond n): each thread owns whole
+// fragment entries ("combos": 8 codes x 4 digits), writes them with 64-bit
+// stores (digits 4..7 as zeros) and accumulates the raw digit sums.  For
+// RTN-4 (BITS=4) it also adds each combo's sum of X into xg[group]
+// (64-bit shared atomics) when xg != nullptr.
+template <int BITS>
+__device__ __forceinline__ void fxa_build(const float* xs, int n, int s, bool bad, int iters, uint2* frag,
+                                          int tid, int nt, int (&raws)[4], long long* xg = nullptr,
+                                          int group = 0) {
+  constexpr int kCombosPerIter = Pack<BITS>::kMmas * 4;
+  for (int c = tid; c < iters * kCombosPerIter; c += nt) {
+    const int it = c / kCombosPerIter, r = c - it * kCombosPerIter;
+    int m, t, k0;
+    int off[8];
+    if constexpr (BITS == 2) {
+      m = r >> 2; t = r & 3;
+      k0 = it * 256 + 16 * (4 * t + (m >> 1)) + 2 * (m & 1);
+      off[0] = 0; off[1] = 4; off[2] = 8; off[3] = 12; off[4] = 1; off[5] = 5; off[6] = 9; off[7] = 13;
+    } else {
+      m = r >> 2; t = r & 3;
+      k0 = it * 128 + 8 * (4 * t + m);
+      off[0] = 0; off[1] = 2; off[2] = 4; off[3] = 6; off[4] = 1; off[5] = 3; off[6] = 5; off[7] = 7;
+    }
+    uint32_t u[8];
+    long long xsum = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int k = k0 + off[e];
+      const int X = (k < n && !bad) ? fxa_enc(xs[k], s) : 0;
+      xsum += X;
+      u[e] = static_cast<uint32_t>(X + kFxaOffset);
+    }
+    uint2* dst = frag + (it * Pack<BITS>::kMmas + m) * 32 + t;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t w0 = raw_digits(u[0], u[1], u[2], u[3], j);
+      const uint32_t w1 = raw_digits(u[4], u[5], u[6], u[7], j);
+      raws[j] = static_cast<int>(__dp4a(w0, 0x01010101u, static_cast<unsigned>(raws[j])));
+      raws[j] = static_cast<int>(__dp4a(w1, 0x01010101u, static_cast<unsigned>(raws[j])));
+      dst[4 * j] = make_uint2(signed_digits(w0), signed_digits(w1));
+      dst[4 * j + 16] = make_uint2(0u, 0u);
+    }
+    if constexpr (BITS == 4) {
+      if (xg != nullptr) atomicAdd(reinterpret_cast<unsigned long long*>(&xg[k0 / group]),
+                                   static_cast<unsigned long long>(xsum));
+    }
+  }
+}
+
+// Block prologue for NT threads: stage x (and the RMS weights), FXA shift over
+// all K, R128 rstd of the raw x (RMS), fragments of codes [k_lo, k_lo +
+// iters*Pack::kIter).  xsm and wsm hold K floats each.  Ends synchronised.
+template <int XT, int RT, bool RMS, int BITS, int NT>
+__device__ __forceinline__ void fxa_prologue(const void* xr, const void* rms_w, int K, float eps, int k_lo,
+                                             int iters, float* xsm, float* wsm, uint2* frag, FxaBlock& fb,
+                                             long long* xg = nullptr, int group = 0) {
+  constexpr int NW = NT / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  stage_row<XT, NT, (8192 * 2 / 16 + NT - 1) / NT>(xr, K, xsm, tid);
+  if constexpr (RMS) stage_row<RT, NT, (8192 * 4 / 16 + NT - 1) / NT>(rms_w, K, wsm, tid);
+  if (xg != nullptr)
+    for (int g = tid; g < K / group; g += NT) xg[g] = 0;
+  __syncthreads();
+  unsigned amax = 0;
+  for (int k = tid; k < K; k += NT) {
+    float v = xsm[k];
+    if constexpr (RMS) {
+      v = __fmul_rn(v, wsm[k]);
+      wsm[k] = v;
+    }
+    amax = max(amax, __float_as_uint(v) & 0x7fffffffu);
+  }
+  float ss = 0.0f;
+  if constexpr (RMS) {
+    if (tid < 128)
+      for (int k = tid; k < K; k += 128) ss = __fmaf_rn(xsm[k], xsm[k], ss);
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+  __shared__ float part[128];
+  if (lane == 0) fb.amax[warp] = amax;
+  if constexpr (RMS) {
+    if (tid < 128) part[tid] = ss;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    unsigned a = 0;
+    for (int w = 0; w < NW; ++w) a = max(a, fb.amax[w]);
+    float rs = 1.0f;
+    if constexpr (RMS) rs = rstd_of(r128_smem_finish(part, lane), K, eps);
+    if (lane == 0) {
+      fb.s = fxa_shift(a);
+      fb.rstd = rs;
+    }
+  }
+  __syncthreads();
+  const int s = fb.s;
+  const bool bad = (s == kFxaNonFinite);
+  int raws[4] = {0, 0, 0, 0};
+  const float* xh = RMS ? wsm : xsm;
+  fxa_build<BITS>(xh + k_lo, K - k_lo, s, bad, iters, frag, tid, NT, raws, xg, group);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) raws[j] += __shfl_xor_sync(0xffffffffu, raws[j], m);
+    if (lane == 0) fb.rawsum[warp][j] = raws[j];
+  }
+  __syncthreads();
+  if (tid < 4) {
+    int t = 0;
+    for (int w = 0; w < NW; ++w) t += fb.rawsum[w][tid];
+    fb.tot[tid] = t - 64 * iters * Pack<BITS>::kIter;  // balanced digit sums (padding digits are 0)
+  }
+  __syncthreads();
+}
+
+// Warp version (one activation row per warp, no RMS, 2-bit layout).
+template <int XT>
+__device__ __forceinline__ int fxa_warp_prologue2(const void* xr, int K, int iters, float* xsm, uint2* frag,
+                                                  int (&tot)[4]) {
+  const int lane = threadIdx.x & 31;
+  stage_row<XT, 32, 8>(xr, K, xsm, lane);
+  __syncwarp();
+  unsigned amax = 0;
+  for (int k = lane; k < K; k += 32) amax = max(amax, __float_as_uint(xsm[k]) & 0x7fffffffu);
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+  const int s = fxa_shift(amax);
+  int raws[4] = {0, 0, 0, 0};
+  fxa_build<2>(xsm, K, s, s == kFxaNonFinite, iters, frag, lane, 32, raws);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) raws[j] += __shfl_xor_sync(0xffffffffu, raws[j], m);
+    tot[j] = raws[j] - 64 * iters * 256;
+  }
+  __syncwarp();
+  return s;
+}
+
+// Contraction with two independent accumulator chains (even / odd MMAs),
+// summed at the end (exact integers).  Same tile semantics as contract_tile.
+template <int NI>
+__device__ __forceinline__ void contract_tile2(const uint4 (&wa)[NI], const uint4 (&wb)[NI], int iters,
+                                               const uint2* frag, int lane, int (&acc)[4]) {
+  int a2[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int i = 0; i < NI; ++i) {
+    if (i < iters) {
+      const uint32_t ga[4] = {wa[i].x, wa[i].y, wa[i].z, wa[i].w};
+      const uint32_t gb[4] = {wb[i].x, wb[i].y, wb[i].z, wb[i].w};
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int q = m >> 1, sh = 4 * (m & 1);
+        const uint32_t a0 = (ga[q] >> sh) & 0x03030303u;
+        const uint32_t a2r = (ga[q] >> (sh + 2)) & 0x03030303u;
+        const uint32_t a1 = (gb[q] >> sh) & 0x03030303u;
+        const uint32_t a3 = (gb[q] >> (sh + 2)) & 0x03030303u;
+        const uint2 bf = frag[(i * 8 + m) * 32 + lane];
+        if (m & 1) mma_u8s8(a2, a0, a1, a2r, a3, bf.x, bf.y);
+        else mma_u8s8(acc, a0, a1, a2r, a3, bf.x, bf.y);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) acc[j] += a2[j];
+}
+
 // Contract one warp's 16-row tile: rows g and g+8 supply words via wa/wb
 // (already loaded), frag holds the digit fragments of the matching K range.
 // acc: lanes t<2 end with digits 2t, 2t+1 for rows g (acc0,1) and g+8 (acc2,3).

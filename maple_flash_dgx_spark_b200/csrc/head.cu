@@ -14,6 +14,7 @@
 //   group order as acc = (acc + s_g*C_g) + b_g*X_g, rounded once to fp32.
 // Symmetric heads (biases == NULL) use b_g = -8 * s_g.
 #include "fxa.cuh"
+#include "launch.cuh"
 
 namespace mb {
 
@@ -34,17 +35,23 @@ struct Rtn4Params {
 template <int XT, int ST>
 __global__ void __launch_bounds__(128) rtn4_gemv_kernel(Rtn4Params p) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ FxaShared sh;
-  __shared__ long long s_xg[64];  // per-group sums of X (ngroups <= 64 for K <= 8192 at G >= 128; G=64 -> K <= 4096)
+  __shared__ FxaBlock fb;
+  __shared__ long long s_xg[64];  // per-group sums of X (K / G <= 64)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int b = blockIdx.y;
   const int ngroups = p.K / p.G;
+  const int iters = p.iters;
   uint2* frag = reinterpret_cast<uint2*>(smem);
-  float* xsm = reinterpret_cast<float*>(smem + (size_t)p.iters * 128 * sizeof(uint2));
+  float* xsm = reinterpret_cast<float*>(smem + (size_t)iters * 128 * sizeof(uint2));
 
-  // Output rows of this warp, mapped to physical head rows.
-  const int out_g = blockIdx.x * 64 + 16 * warp + g, out_h = out_g + 8;
+  // Persistent: this CTA streams 64-row blocks blockIdx.x, +gridDim.x, ...;
+  // flattened (block, iteration) steps q keep kHeadPrefetch loads in flight
+  // per lane across block boundaries.
+  const int nblk = (p.n_out + 63) / 64;
+  const int nb_my = blockIdx.x < nblk ? (nblk - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int total = nb_my * iters;
+  if (p.cluster_ids != nullptr) pdl_wait();  // probe ids come from the previous launch
   auto phys = [&](int r) -> int64_t {
     if (p.cluster_ids == nullptr) return r;
     const int probe = r / p.cluster_size, member = r - probe * p.cluster_size;
@@ -52,49 +59,40 @@ __global__ void __launch_bounds__(128) rtn4_gemv_kernel(Rtn4Params p) {
     if (c < 0 || c >= p.n_clusters) c = 0;
     return (int64_t)c * p.cluster_size + member;
   };
-  const bool ok_g = out_g < p.n_out, ok_h = out_h < p.n_out;
-  const int64_t pr_g = ok_g ? phys(out_g) : 0, pr_h = ok_h ? phys(out_h) : 0;
-  const uint32_t* row_g = p.codes + pr_g * p.nwords;
-  const uint32_t* row_h = p.codes + pr_h * p.nwords;
-
+  auto issue = [&](int q, uint4& ra, uint4& rb) {
+    ra = make_uint4(0, 0, 0, 0);
+    rb = make_uint4(0, 0, 0, 0);
+    if (q >= total) return;
+    const int blk = blockIdx.x + (q / iters) * gridDim.x, i = q - (q / iters) * iters;
+    const int og = blk * 64 + 16 * warp + g, oh = og + 8;
+    const int word = i * 16 + 4 * t;
+    if (og < p.n_out) ra = ld_stream_u4(p.codes + phys(og) * p.nwords + word);
+    if (oh < p.n_out) rb = ld_stream_u4(p.codes + phys(oh) * p.nwords + word);
+  };
   uint4 wa[kHeadPrefetch], wb[kHeadPrefetch];
 #pragma unroll
-  for (int i = 0; i < kHeadPrefetch; ++i) {
-    wa[i] = make_uint4(0, 0, 0, 0);
-    wb[i] = make_uint4(0, 0, 0, 0);
-    if (i < p.iters) {
-      const int word = i * 16 + 4 * t;
-      if (ok_g) wa[i] = ld_stream_u4(row_g + word);
-      if (ok_h) wb[i] = ld_stream_u4(row_h + word);
-    }
-  }
+  for (int ii = 0; ii < kHeadPrefetch; ++ii) issue(ii, wa[ii], wb[ii]);
 
+  pdl_wait();
+  pdl_trigger();
   const void* xr = static_cast<const char*>(p.x) + b * p.x_stride * (XT == kBF16 ? 2 : 4);
-  fxa_block_prologue<XT, kF32, false, 4>(xr, nullptr, p.K, 0.0f, 0, p.iters, xsm, frag, sh);
-  const int s = sh.s;
+  fxa_prologue<XT, kF32, false, 4, 128>(xr, nullptr, p.K, 0.0f, 0, iters, xsm, nullptr, frag, fb, s_xg, p.G);
+  const int s = fb.s;
   const bool bad = (s == kFxaNonFinite);
-  // Per-group sums of the FXA values.
-  for (int gi = warp; gi < ngroups; gi += 4) {
-    long long a = 0;
-    for (int k = gi * p.G + lane; k < (gi + 1) * p.G; k += 32) a += bad ? 0 : fxa_encode(xsm[k], s);
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) a += __shfl_xor_sync(0xffffffffu, a, m);
-    if (lane == 0) s_xg[gi] = a;
-  }
-  __syncthreads();
-
+  const float nanv = __int_as_float(0x7fc00000);
   const int es_s = ST == kBF16 ? 2 : 4;
-  const char* sc_g = static_cast<const char*>(p.scales) + pr_g * ngroups * es_s;
-  const char* sc_h = static_cast<const char*>(p.scales) + pr_h * ngroups * es_s;
-  const char* bi_g = p.biases ? static_cast<const char*>(p.biases) + pr_g * ngroups * es_s : nullptr;
-  const char* bi_h = p.biases ? static_cast<const char*>(p.biases) + pr_h * ngroups * es_s : nullptr;
-  double acc_g = 0.0, acc_h = 0.0;
   const int its_per_group = p.G >= 128 ? p.G / 128 : 1;
   const bool split_iter = p.G == 64;
+  char* yr = static_cast<char*>(p.y) + b * p.y_stride * (XT == kBF16 ? 2 : 4);
+
+  double acc_g = 0.0, acc_h = 0.0;
   int ca[4] = {0, 0, 0, 0}, cb[4] = {0, 0, 0, 0};
+  int cur_blk = -1;
+  bool ok_g = false, ok_h = false;
+  const char *sc_g = nullptr, *sc_h = nullptr, *bi_g = nullptr, *bi_h = nullptr;
+  int out_g = 0, out_h = 0;
 
   auto finish_group = [&](int (&c)[4], int gi) {
-    // lanes t = 0, 1 hold digits 2t, 2t+1 of rows g (c0, c1) and g+8 (c2, c3)
     const long long pg = (long long)c[0] + 128LL * c[1];
     const long long ph = (long long)c[2] + 128LL * c[3];
     const long long ug = __shfl_down_sync(0xffffffffu, pg, 1);
@@ -112,20 +110,29 @@ __global__ void __launch_bounds__(128) rtn4_gemv_kernel(Rtn4Params p) {
     for (int j = 0; j < 4; ++j) c[j] = 0;
   };
 
-  for (int i0 = 0; i0 < p.iters; i0 += kHeadPrefetch) {
+  for (int q0 = 0; q0 < total; q0 += kHeadPrefetch) {
 #pragma unroll
     for (int ii = 0; ii < kHeadPrefetch; ++ii) {
-      const int i = i0 + ii;
-      if (i < p.iters) {
+      const int q = q0 + ii;
+      if (q < total) {
+        const int blk = blockIdx.x + (q / iters) * gridDim.x, i = q - (q / iters) * iters;
+        if (blk != cur_blk) {
+          cur_blk = blk;
+          out_g = blk * 64 + 16 * warp + g;
+          out_h = out_g + 8;
+          ok_g = out_g < p.n_out;
+          ok_h = out_h < p.n_out;
+          const int64_t pg = ok_g ? phys(out_g) : 0, ph = ok_h ? phys(out_h) : 0;
+          sc_g = static_cast<const char*>(p.scales) + pg * ngroups * es_s;
+          sc_h = static_cast<const char*>(p.scales) + ph * ngroups * es_s;
+          bi_g = p.biases ? static_cast<const char*>(p.biases) + pg * ngroups * es_s : nullptr;
+          bi_h = p.biases ? static_cast<const char*>(p.biases) + ph * ngroups * es_s : nullptr;
+          acc_g = 0.0;
+          acc_h = 0.0;
+        }
         const uint32_t ga[4] = {wa[ii].x, wa[ii].y, wa[ii].z, wa[ii].w};
         const uint32_t gb[4] = {wb[ii].x, wb[ii].y, wb[ii].z, wb[ii].w};
-        // refill this slot with iteration i + kHeadPrefetch
-        const int inext = i + kHeadPrefetch;
-        if (inext < p.iters) {
-          const int word = inext * 16 + 4 * t;
-          if (ok_g) wa[ii] = ld_stream_u4(row_g + word);
-          if (ok_h) wb[ii] = ld_stream_u4(row_h + word);
-        }
+        issue(q + kHeadPrefetch, wa[ii], wb[ii]);
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
           const uint32_t a0 = ga[m] & 0x0f0f0f0fu, a2 = (ga[m] >> 4) & 0x0f0f0f0fu;
@@ -146,14 +153,12 @@ __global__ void __launch_bounds__(128) rtn4_gemv_kernel(Rtn4Params p) {
         } else if ((i + 1) % its_per_group == 0) {
           finish_group(ca, i / its_per_group);
         }
+        if (i == iters - 1 && t == 0) {
+          if (ok_g) store_f<XT>(yr, out_g, bad ? nanv : __double2float_rn(acc_g * pow2d(-s)));
+          if (ok_h) store_f<XT>(yr, out_h, bad ? nanv : __double2float_rn(acc_h * pow2d(-s)));
+        }
       }
     }
-  }
-  if (t == 0) {
-    char* yr = static_cast<char*>(p.y) + b * p.y_stride * (XT == kBF16 ? 2 : 4);
-    const float nanv = __int_as_float(0x7fc00000);
-    if (ok_g) store_f<XT>(yr, out_g, bad ? nanv : __double2float_rn(acc_g * pow2d(-s)));
-    if (ok_h) store_f<XT>(yr, out_h, bad ? nanv : __double2float_rn(acc_h * pow2d(-s)));
   }
 }
 
@@ -174,6 +179,8 @@ __global__ void __launch_bounds__(256) argmax_kernel(const void* logits, int64_t
   __shared__ float sv[8];
   __shared__ int si[8];
   __shared__ int s_last;
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = blockIdx.y, nblk = gridDim.x;
   const char* row = static_cast<const char*>(logits) + b * row_stride * (XT == kBF16 ? 2 : 4);
@@ -266,6 +273,8 @@ __global__ void __launch_bounds__(256) sample_kernel(const void* logits, int64_t
   __shared__ int s_last;
   __shared__ float kv[kSampMaxK];
   __shared__ int ki[kSampMaxK];
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = blockIdx.y, nblk = gridDim.x;
   const char* row = static_cast<const char*>(logits) + b * row_stride * (XT == kBF16 ? 2 : 4);
@@ -397,6 +406,8 @@ __global__ void __launch_bounds__(256) sample_kernel(const void* logits, int64_t
 template <int OT, int TT>
 __global__ void embed_bf16_kernel(const int64_t* ids, const void* table, int64_t V, int64_t H, void* out,
                                   int64_t out_stride, int* err) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.y;
   const int64_t id = ids[b];
   const bool ok = id >= 0 && id < V;
@@ -411,6 +422,8 @@ template <int OT, int ST>
 __global__ void embed_rtn4_kernel(const int64_t* ids, const uint32_t* codes, const void* scales,
                                   const void* biases, int64_t V, int64_t H, int G, void* out,
                                   int64_t out_stride, int* err) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.y;
   const int64_t id = ids[b];
   const bool ok = id >= 0 && id < V;
@@ -436,14 +449,15 @@ using namespace mb;
 namespace {
 int rtn4_launch(Rtn4Params& p, int x_dtype, int s_dtype, int64_t batch, void* stream) {
   const size_t smem = (size_t)p.iters * 128 * sizeof(uint2) + (size_t)p.K * sizeof(float);
-  dim3 grid((unsigned)((p.n_out + 63) / 64), (unsigned)batch);
+  const int nblk = (p.n_out + 63) / 64;
+  dim3 grid((unsigned)(nblk < 148 * 4 ? nblk : 148 * 4), (unsigned)batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
 #define MB_R4(XT, ST)                                                                        \
   do {                                                                                       \
     auto kern = rtn4_gemv_kernel<XT, ST>;                                                    \
     if (smem > 32 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    if (e == cudaSuccess) kern<<<grid, 128, smem, st>>>(p);                                  \
+    if (e == cudaSuccess) launch_k(kern, dim3(grid), dim3(128), smem, st, p);                                  \
   } while (0)
   if (x_dtype == kBF16) { if (s_dtype == kBF16) MB_R4(kBF16, kBF16); else MB_R4(kBF16, kF32); }
   else { if (s_dtype == kBF16) MB_R4(kF32, kBF16); else MB_R4(kF32, kF32); }
@@ -514,8 +528,8 @@ extern "C" int maple_argmax(const void* logits, int x_dtype, int64_t batch, int6
   int* wi = wv ? reinterpret_cast<int*>(wv + batch * nblk) : nullptr;
   dim3 grid((unsigned)nblk, (unsigned)batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (x_dtype == kBF16) argmax_kernel<kBF16><<<grid, 256, 0, st>>>(logits, row_stride, (int)vocab, wv, wi, tickets, out);
-  else argmax_kernel<kF32><<<grid, 256, 0, st>>>(logits, row_stride, (int)vocab, wv, wi, tickets, out);
+  if (x_dtype == kBF16) launch_k(argmax_kernel<kBF16>, dim3(grid), dim3(256), 0, st, logits, row_stride, (int)vocab, wv, wi, tickets, out);
+  else launch_k(argmax_kernel<kF32>, dim3(grid), dim3(256), 0, st, logits, row_stride, (int)vocab, wv, wi, tickets, out);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
@@ -543,10 +557,10 @@ extern "C" int maple_fused_sample(const void* logits, int x_dtype, int64_t batch
   dim3 grid((unsigned)nblk, (unsigned)batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (x_dtype == kBF16)
-    sample_kernel<kBF16><<<grid, 256, 0, st>>>(logits, row_stride, (int)vocab, (int)top_k, inv_t, top_p, uniform,
+    launch_k(sample_kernel<kBF16>, dim3(grid), dim3(256), 0, st, logits, row_stride, (int)vocab, (int)top_k, inv_t, top_p, uniform,
                                                cv, ci, tickets, out);
   else
-    sample_kernel<kF32><<<grid, 256, 0, st>>>(logits, row_stride, (int)vocab, (int)top_k, inv_t, top_p, uniform,
+    launch_k(sample_kernel<kF32>, dim3(grid), dim3(256), 0, st, logits, row_stride, (int)vocab, (int)top_k, inv_t, top_p, uniform,
                                               cv, ci, tickets, out);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
@@ -561,11 +575,11 @@ extern "C" int maple_embedding(const int64_t* ids, int64_t batch, const void* ta
   dim3 grid((unsigned)((hidden + 255) / 256), (unsigned)batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (out_dtype == kBF16) {
-    if (t_dtype == kBF16) embed_bf16_kernel<kBF16, kBF16><<<grid, 256, 0, st>>>(ids, table, vocab, hidden, out, out_row_stride, err);
-    else embed_bf16_kernel<kBF16, kF32><<<grid, 256, 0, st>>>(ids, table, vocab, hidden, out, out_row_stride, err);
+    if (t_dtype == kBF16) launch_k(embed_bf16_kernel<kBF16, kBF16>, dim3(grid), dim3(256), 0, st, ids, table, vocab, hidden, out, out_row_stride, err);
+    else launch_k(embed_bf16_kernel<kBF16, kF32>, dim3(grid), dim3(256), 0, st, ids, table, vocab, hidden, out, out_row_stride, err);
   } else {
-    if (t_dtype == kBF16) embed_bf16_kernel<kF32, kBF16><<<grid, 256, 0, st>>>(ids, table, vocab, hidden, out, out_row_stride, err);
-    else embed_bf16_kernel<kF32, kF32><<<grid, 256, 0, st>>>(ids, table, vocab, hidden, out, out_row_stride, err);
+    if (t_dtype == kBF16) launch_k(embed_bf16_kernel<kF32, kBF16>, dim3(grid), dim3(256), 0, st, ids, table, vocab, hidden, out, out_row_stride, err);
+    else launch_k(embed_bf16_kernel<kF32, kF32>, dim3(grid), dim3(256), 0, st, ids, table, vocab, hidden, out, out_row_stride, err);
   }
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
@@ -582,11 +596,11 @@ extern "C" int maple_rtn4_embedding(const int64_t* ids, int64_t batch, const uin
   dim3 grid((unsigned)((hidden + 255) / 256), (unsigned)batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (out_dtype == kBF16) {
-    if (s_dtype == kBF16) embed_rtn4_kernel<kBF16, kBF16><<<grid, 256, 0, st>>>(ids, codes, scales, biases, vocab, hidden, (int)group_size, out, out_row_stride, err);
-    else embed_rtn4_kernel<kBF16, kF32><<<grid, 256, 0, st>>>(ids, codes, scales, biases, vocab, hidden, (int)group_size, out, out_row_stride, err);
+    if (s_dtype == kBF16) launch_k(embed_rtn4_kernel<kBF16, kBF16>, dim3(grid), dim3(256), 0, st, ids, codes, scales, biases, vocab, hidden, (int)group_size, out, out_row_stride, err);
+    else launch_k(embed_rtn4_kernel<kBF16, kF32>, dim3(grid), dim3(256), 0, st, ids, codes, scales, biases, vocab, hidden, (int)group_size, out, out_row_stride, err);
   } else {
-    if (s_dtype == kBF16) embed_rtn4_kernel<kF32, kBF16><<<grid, 256, 0, st>>>(ids, codes, scales, biases, vocab, hidden, (int)group_size, out, out_row_stride, err);
-    else embed_rtn4_kernel<kF32, kF32><<<grid, 256, 0, st>>>(ids, codes, scales, biases, vocab, hidden, (int)group_size, out, out_row_stride, err);
+    if (s_dtype == kBF16) launch_k(embed_rtn4_kernel<kF32, kBF16>, dim3(grid), dim3(256), 0, st, ids, codes, scales, biases, vocab, hidden, (int)group_size, out, out_row_stride, err);
+    else launch_k(embed_rtn4_kernel<kF32, kF32>, dim3(grid), dim3(256), 0, st, ids, codes, scales, biases, vocab, hidden, (int)group_size, out, out_row_stride, err);
   }
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }

@@ -6,6 +6,7 @@
 //                  ternary_expert_down_sum (ternary_expert.py:471-556)
 // moe_reduce_add   reference kernels/fused_norm.py:164-202
 #include "fxa.cuh"
+#include "launch.cuh"
 
 namespace mb {
 
@@ -35,6 +36,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tok = blockIdx.y;
   const int e0 = blockIdx.x * kRouterWarps;
+  // gate rows are weights: loaded before waiting for the activation
   const int ne = min(kRouterWarps, p.E - e0);
   const int ges = GT == kBF16 ? 2 : 4;
   float* xs = reinterpret_cast<float*>(rsm);
@@ -56,6 +58,8 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
       for (int b = tid; b < nbytes; b += 256) gs[b] = gsrc[b];
     }
   }
+  pdl_wait();
+  pdl_trigger();
   const char* xr = static_cast<const char*>(p.x) + tok * p.x_stride * (XT == kBF16 ? 2 : 4);
   stage_row<XT, 256, 2>(xr, p.K, xs, tid);
   __syncthreads();
@@ -173,8 +177,10 @@ __global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
   uint2* frag = reinterpret_cast<uint2*>(smem + warp * per_warp);
   float* xsm = reinterpret_cast<float*>(smem + warp * per_warp + (size_t)p.iters * 256 * sizeof(uint2));
 
+  // Routing ids come from two launches back (complete once the previous
+  // launch has passed its own wait), so the expert rows load before waiting.
   if (warp < p.topk) {
-    int e = p.ids[(int64_t)tok * p.topk + warp];
+    int e = __ldcg(&p.ids[(int64_t)tok * p.topk + warp]);
     const bool bad = (e < 0 || e >= p.E);
     if (bad) e = 0;
     const uint32_t* codes = p.codes + (int64_t)e * p.N * p.nwords;
@@ -189,12 +195,13 @@ __global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
         if (row_h < p.N) wb[i] = ld_stream_u4(codes + (int64_t)row_h * p.nwords + word);
       }
     }
+    pdl_wait();
     const void* hr = static_cast<const char*>(p.h) +
                      (tok * p.h_tok_stride + warp * p.h_slot_stride) * (XT == kBF16 ? 2 : 4);
     int tot[4];
-    const int s = fxa_warp_prologue<XT>(hr, p.K, p.iters, xsm, frag, tot);
+    const int s = fxa_warp_prologue2<XT>(hr, p.K, p.iters, xsm, frag, tot);
     int acc[4] = {0, 0, 0, 0};
-    contract_tile<kDownMaxIters>(wa, wb, p.iters, frag, lane, acc);
+    contract_tile2<kDownMaxIters>(wa, wb, p.iters, frag, lane, acc);
     long long Sg, Sh;
     combine_digits(acc, tot, t, Sg, Sh);
     if (t == 0) {
@@ -222,6 +229,8 @@ __global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
       }
     }
   }
+  pdl_wait();
+  pdl_trigger();
   __syncthreads();
   if (tid < 16) {
     const int row = blockIdx.x * 16 + tid;
@@ -250,6 +259,8 @@ template <int XT>
 __global__ void moe_reduce_kernel(const void* x, const float* w, const void* residual, void* y,
                                   int64_t x_tok_stride, int64_t x_slot_stride, int64_t res_stride,
                                   int64_t y_stride, int N, int topk) {
+  pdl_wait();
+  pdl_trigger();
   const int tok = blockIdx.y;
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
@@ -296,7 +307,7 @@ extern "C" int maple_router_topk(const void* x, int x_dtype, int64_t x_row_strid
   do {                                                                                                    \
     if (smem > 32 * 1024)                                                                                 \
       cudaFuncSetAttribute(router_kernel<XT, GT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    router_kernel<XT, GT><<<grid, 256, smem, st>>>(p);                                                    \
+    launch_k(router_kernel<XT, GT>, dim3(grid), dim3(256), smem, st, p);                                                    \
   } while (0)
   if (x_dtype == kBF16) {
     if (gate_dtype == kBF16) MB_ROUTER(kBF16, kBF16); else MB_ROUTER(kBF16, kF32);
@@ -318,7 +329,7 @@ cudaError_t launch_down(const DownParams& p, int T, cudaStream_t st) {
     if (e != cudaSuccess) return e;
   }
   dim3 grid((p.N + 15) / 16, T);
-  kern<<<grid, 256, smem, st>>>(p);
+  launch_k(kern, dim3(grid), dim3(256), smem, st, p);
   return cudaGetLastError();
 }
 
@@ -384,10 +395,10 @@ extern "C" int maple_moe_reduce_add(const void* x, int x_dtype, int64_t x_tok_st
   dim3 grid((unsigned)((n + 127) / 128), (unsigned)tokens);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (x_dtype == kBF16)
-    moe_reduce_kernel<kBF16><<<grid, 128, 0, st>>>(x, wt, residual, y, x_tok_stride, x_slot_stride,
+    launch_k(moe_reduce_kernel<kBF16>, dim3(grid), dim3(128), 0, st, x, wt, residual, y, x_tok_stride, x_slot_stride,
                                                    res_stride, y_stride, (int)n, (int)topk);
   else
-    moe_reduce_kernel<kF32><<<grid, 128, 0, st>>>(x, wt, residual, y, x_tok_stride, x_slot_stride,
+    launch_k(moe_reduce_kernel<kF32>, dim3(grid), dim3(128), 0, st, x, wt, residual, y, x_tok_stride, x_slot_stride,
                                                   res_stride, y_stride, (int)n, (int)topk);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }

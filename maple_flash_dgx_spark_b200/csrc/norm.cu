@@ -3,6 +3,7 @@
 // :128-161 (add_rms_norm, kernel :32-57).  One CTA (128 threads) per row;
 // the sum of squares is R128 order (thread j owns elements j, j+128, ...).
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace mb {
 
@@ -20,9 +21,11 @@ __global__ void __launch_bounds__(128) rms_norm_kernel(const void* x, const void
   float* xs = srow;
   float* ys = srow + N;
   float* wsm = srow + 2 * N;
+  stage_row<WT, 128, 4>(w, N, wsm, tid);  // weights: before waiting
+  pdl_wait();
+  pdl_trigger();
   stage_row<XT, 128, 4>(static_cast<const char*>(x) + row * x_stride * es, N, xs, tid);
   if constexpr (ADD) stage_row<XT, 128, 4>(static_cast<const char*>(y) + row * y_stride * es, N, ys, tid);
-  stage_row<WT, 128, 4>(w, N, wsm, tid);
   __syncthreads();
   float ss = 0.0f;
   for (int k = tid; k < N; k += 128) {
@@ -66,14 +69,14 @@ int launch_norm(const void* x, const void* y, int x_dtype, int64_t rows, int64_t
   const dim3 grid((unsigned)rows);
   if (x_dtype == kBF16) {
     if (w_dtype == kBF16)
-      rms_norm_kernel<kBF16, kBF16, ADD><<<grid, 128, smem, st>>>(x, y, w, residual, out, xs, ys, rs, os, (int)n, eps);
+      launch_k(rms_norm_kernel<kBF16, kBF16, ADD>, dim3(grid), dim3(128), smem, st, x, y, w, residual, out, xs, ys, rs, os, (int)n, eps);
     else
-      rms_norm_kernel<kBF16, kF32, ADD><<<grid, 128, smem, st>>>(x, y, w, residual, out, xs, ys, rs, os, (int)n, eps);
+      launch_k(rms_norm_kernel<kBF16, kF32, ADD>, dim3(grid), dim3(128), smem, st, x, y, w, residual, out, xs, ys, rs, os, (int)n, eps);
   } else {
     if (w_dtype == kBF16)
-      rms_norm_kernel<kF32, kBF16, ADD><<<grid, 128, smem, st>>>(x, y, w, residual, out, xs, ys, rs, os, (int)n, eps);
+      launch_k(rms_norm_kernel<kF32, kBF16, ADD>, dim3(grid), dim3(128), smem, st, x, y, w, residual, out, xs, ys, rs, os, (int)n, eps);
     else
-      rms_norm_kernel<kF32, kF32, ADD><<<grid, 128, smem, st>>>(x, y, w, residual, out, xs, ys, rs, os, (int)n, eps);
+      launch_k(rms_norm_kernel<kF32, kF32, ADD>, dim3(grid), dim3(128), smem, st, x, y, w, residual, out, xs, ys, rs, os, (int)n, eps);
   }
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }

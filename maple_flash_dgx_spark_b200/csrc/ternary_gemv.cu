@@ -22,11 +22,11 @@
 // partials are exact int32 and the last CTA of a row group (atomic ticket)
 // finishes the rows.  grid.z = activation row (token, or token x top-k slot).
 #include "fxa.cuh"
+#include "launch.cuh"
 
 namespace mb {
 
 constexpr int kMaxIters = 8;                 // K iterations held in registers (K <= 2048)
-constexpr int kTicketBytes = 1 << 20;          // ticket header at the start of a workspace
 
 enum GemvMode : int { kPlain = 0, kSwiglu = 1 };
 
@@ -66,9 +66,16 @@ __global__ void __launch_bounds__(128) ternary_gemv_kernel(TGemvParams p) {
   float* xsm = reinterpret_cast<float*>(smem + (size_t)p.iters * 256 * sizeof(uint2));
 
   // Expert selection (out-of-range ids produce NaN rows rather than a fault).
+  // The ids come from the previous launch, so expert GEMVs wait first; dense
+  // GEMVs load their weights before waiting.
+  const bool dense = p.ids == nullptr;
+  if (!dense) {
+    pdl_wait();
+    pdl_trigger();
+  }
   int e = 0;
   bool bad_id = false;
-  if (p.ids != nullptr) {
+  if (!dense) {
     e = p.ids[z];
     if (e < 0 || e >= p.n_experts) { bad_id = true; e = 0; }
   }
@@ -102,6 +109,10 @@ __global__ void __launch_bounds__(128) ternary_gemv_kernel(TGemvParams p) {
     }
   }
 
+  if (dense) {
+    pdl_wait();
+    pdl_trigger();
+  }
   // 2) Activation prologue (shift over all K, fragments for this split).
   const int xrow = z / p.x_div;
   const void* xr = static_cast<const char*>(p.x) + xrow * p.x_stride * (XT == kBF16 ? 2 : 4);
@@ -200,6 +211,122 @@ __global__ void __launch_bounds__(128) ternary_gemv_kernel(TGemvParams p) {
   if constexpr (MODE == kSwiglu) swiglu_finish();
 }
 
+
+// ---------------------------------------------------------------------------
+// v2: one CTA covers all of K.  8 warps = WM row tiles x WK K-slices; the
+// K-slices' exact int32 partials are summed in shared memory, so no
+// workspace is needed.  The FXA prologue is the fast one (fxa_prologue).
+template <int XT, int AT, int RT, bool RMS, int MODE, int WM, int WK, int NI>
+__global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
+  constexpr int NT = 32 * WM * WK;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ FxaBlock fb;
+  __shared__ int red[WK > 1 ? WK - 1 : 1][WM][32][4];
+  __shared__ float s_val[16 * WM];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int wm = warp % WM, wk = warp / WM;
+  const int g = lane >> 2, t = lane & 3;
+  const int z = blockIdx.z;
+  const int iters_total = (p.nwords + 15) / 16;
+  const int ipw = (iters_total + WK - 1) / WK;
+  const int it0 = wk * ipw;
+  const int my_iters = max(0, min(ipw, iters_total - it0));
+  uint2* frag = reinterpret_cast<uint2*>(smem);
+  float* xsm = reinterpret_cast<float*>(smem + (size_t)iters_total * 256 * sizeof(uint2));
+  float* wsm = xsm + p.K;
+
+  const bool dense = p.ids == nullptr;
+  if (!dense) {
+    pdl_wait();
+    pdl_trigger();
+  }
+  int e = 0;
+  bool bad_id = false;
+  if (!dense) {
+    e = p.ids[z];
+    if (e < 0 || e >= p.n_experts) { bad_id = true; e = 0; }
+  }
+  const uint32_t* codes = p.codes + (int64_t)e * p.expert_words;
+  int tile0;
+  if constexpr (MODE == kSwiglu) {
+    const int n0 = blockIdx.x * (8 * WM);
+    tile0 = (wm < WM / 2) ? n0 + 16 * wm : (p.rows >> 1) + n0 + 16 * (wm - WM / 2);
+  } else {
+    tile0 = blockIdx.x * (16 * WM) + 16 * wm;
+  }
+  const int row_g = tile0 + g, row_h = tile0 + g + 8;
+  const int base = (MODE == kSwiglu && wm >= WM / 2) ? (p.rows >> 1) : 0;
+  const int lim = (MODE == kSwiglu) ? base + p.n_out : p.rows;
+  const bool ok_g = row_g < lim, ok_h = row_h < lim;
+
+  uint4 wa[NI], wb[NI];
+#pragma unroll
+  for (int i = 0; i < NI; ++i) {
+    wa[i] = make_uint4(0, 0, 0, 0);
+    wb[i] = make_uint4(0, 0, 0, 0);
+    if (i < my_iters) {
+      const int word = (it0 + i) * 16 + 4 * t;
+      if (word < p.nwords) {
+        if (ok_g) wa[i] = ld_stream_u4(codes + (int64_t)row_g * p.nwords + word);
+        if (ok_h) wb[i] = ld_stream_u4(codes + (int64_t)row_h * p.nwords + word);
+      }
+    }
+  }
+  if (dense) {
+    pdl_wait();
+    pdl_trigger();
+  }
+  const void* xr = static_cast<const char*>(p.x) + (z / p.x_div) * p.x_stride * (XT == kBF16 ? 2 : 4);
+  fxa_prologue<XT, RT, RMS, 2, NT>(xr, p.rms_w, p.K, p.eps, 0, iters_total, xsm, wsm, frag, fb);
+  const int s = fb.s;
+  const bool nan_out = (s == kFxaNonFinite) || bad_id;
+
+  int acc[4] = {0, 0, 0, 0};
+  contract_tile2<NI>(wa, wb, my_iters, frag + (size_t)it0 * 256, lane, acc);
+  if (wk > 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) red[wk - 1][wm][lane][j] = acc[j];
+  }
+  __syncthreads();
+  const void* alpha = static_cast<const char*>(p.alpha) + (int64_t)e * p.alpha_estride * (AT == kBF16 ? 2 : 4);
+  char* yz = static_cast<char*>(p.y) + (int64_t)z * p.y_stride * (XT == kBF16 ? 2 : 4);
+  if (wk == 0) {
+#pragma unroll
+    for (int w2 = 0; w2 < WK - 1; ++w2)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] += red[w2][wm][lane][j];
+    long long Sg, Sh;
+    combine_digits(acc, fb.tot, t, Sg, Sh);
+    if (t == 0) {
+      auto value = [&](int row, long long S) -> float {
+        float v = nan_out ? __int_as_float(0x7fc00000) : fxa_value(S, s);
+        if constexpr (RMS) v = __fmul_rn(v, fb.rstd);
+        return __fmul_rn(v, load_f<AT>(alpha, row));
+      };
+      if constexpr (MODE == kSwiglu) {
+        s_val[16 * wm + g] = ok_g ? value(row_g, Sg) : 0.0f;
+        s_val[16 * wm + g + 8] = ok_h ? value(row_h, Sh) : 0.0f;
+      } else {
+        if (ok_g) store_f<XT>(yz, row_g, value(row_g, Sg));
+        if (ok_h) store_f<XT>(yz, row_h, value(row_h, Sh));
+      }
+    }
+  }
+  if constexpr (MODE == kSwiglu) {
+    __syncthreads();
+    constexpr int H = 8 * WM;  // outputs per CTA
+    if (tid < H) {
+      const int n = blockIdx.x * H + tid;
+      if (n < p.n_out) {
+        float up = s_val[tid], gate = s_val[H + tid];
+        up = fminf(fmaxf(up, -7.0f), 7.0f);
+        gate = fminf(gate, 7.0f);
+        store_f<XT>(yz, n, __fmul_rn(__fmul_rn(up, gate), msigmoid(gate)));
+      }
+    }
+  }
+}
+
 }  // namespace mb
 
 using namespace mb;
@@ -227,7 +354,7 @@ cudaError_t launch_tgemv(const TGemvParams& p, int Z, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  kern<<<grid, 128, smem, st>>>(p);
+  launch_k(kern, dim3(grid), dim3(128), smem, st, p);
   return cudaGetLastError();
 }
 
@@ -248,11 +375,44 @@ cudaError_t dispatch(const TGemvParams& p, int x_dtype, int alpha_dtype, int rms
                               : dispatch_rms<kF32, kF32, MODE>(p, rms_dtype, Z, st);
 }
 
-int64_t ws_bytes(int64_t Z, int64_t rows, int64_t nwords) {
-  const int ks = gemv_splits(nwords);
-  if (ks <= 1) return 0;
-  return kTicketBytes + Z * ks * rows * 4 * (int64_t)sizeof(int);
+template <int XT, int AT, int RT, bool RMS, int MODE, int WM, int WK, int NI>
+cudaError_t launch_v2(const TGemvParams& p, int Z, cudaStream_t st) {
+  const int iters_total = (p.nwords + 15) / 16;
+  const size_t smem = (size_t)iters_total * 256 * sizeof(uint2) + 2 * (size_t)p.K * sizeof(float);
+  const int per_cta = (MODE == kSwiglu) ? 8 * WM : 16 * WM;
+  dim3 grid((p.n_out + per_cta - 1) / per_cta, 1, Z);
+  auto kern = tgemv2_kernel<XT, AT, RT, RMS, MODE, WM, WK, NI>;
+  if (smem > 32 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_k(kern, grid, dim3(32 * WM * WK), smem, st, p);
 }
+
+template <int XT, int AT, int RT, bool RMS, int MODE>
+cudaError_t pick_v2(const TGemvParams& p, int Z, cudaStream_t st) {
+  const int iters_total = (p.nwords + 15) / 16;
+  if (iters_total <= 8) return launch_v2<XT, AT, RT, RMS, MODE, 4, 2, 4>(p, Z, st);
+  if (iters_total <= 16) return launch_v2<XT, AT, RT, RMS, MODE, 2, 4, 4>(p, Z, st);
+  return launch_v2<XT, AT, RT, RMS, MODE, 2, 4, 8>(p, Z, st);
+}
+
+template <int XT, int AT, int MODE>
+cudaError_t dispatch_v2(const TGemvParams& p, int rms_dtype, int Z, cudaStream_t st) {
+  if (p.rms_w == nullptr) return pick_v2<XT, AT, kF32, false, MODE>(p, Z, st);
+  if (rms_dtype == kF32) return pick_v2<XT, AT, kF32, true, MODE>(p, Z, st);
+  return pick_v2<XT, AT, kBF16, true, MODE>(p, Z, st);
+}
+
+template <int MODE>
+cudaError_t dispatch2(const TGemvParams& p, int x_dtype, int alpha_dtype, int rms_dtype, int Z, cudaStream_t st) {
+  if (x_dtype == kBF16)
+    return alpha_dtype == kBF16 ? dispatch_v2<kBF16, kBF16, MODE>(p, rms_dtype, Z, st)
+                                : dispatch_v2<kBF16, kF32, MODE>(p, rms_dtype, Z, st);
+  return alpha_dtype == kBF16 ? dispatch_v2<kF32, kBF16, MODE>(p, rms_dtype, Z, st)
+                              : dispatch_v2<kF32, kF32, MODE>(p, rms_dtype, Z, st);
+}
+
 
 int common_checks(int x_dtype, int alpha_dtype, const void* rms_w, int rms_dtype, int64_t k) {
   if ((x_dtype != kF32 && x_dtype != kBF16) || (alpha_dtype != kF32 && alpha_dtype != kBF16) ||
@@ -262,25 +422,12 @@ int common_checks(int x_dtype, int alpha_dtype, const void* rms_w, int rms_dtype
   return kOk;
 }
 
-int setup_ws(TGemvParams& p, int64_t Z, void* workspace, int64_t workspace_bytes, int per_cta = 64) {
-  p.ks = gemv_splits(p.nwords);
-  const int iters_total = (p.nwords + 15) / 16;
-  p.iters = (iters_total + p.ks - 1) / p.ks;
-  p.ks = (iters_total + p.iters - 1) / p.iters;
-  if (p.ks > 1) {
-    const int64_t tickets = Z * ((p.n_out + per_cta - 1) / per_cta + 1);
-    if (!workspace || workspace_bytes < ws_bytes(Z, p.rows, p.nwords)) return kErrWorkspace;
-    if (tickets * (int64_t)sizeof(unsigned) > kTicketBytes) return kErrWorkspace;
-    p.tickets = static_cast<unsigned*>(workspace);
-    p.ws = reinterpret_cast<int*>(static_cast<char*>(workspace) + kTicketBytes);
-  }
-  return kOk;
-}
 
 }  // namespace
 
 extern "C" int64_t maple_ternary_gemv_workspace_bytes(int64_t batch, int64_t n, int64_t k) {
-  return ws_bytes(batch, n, k / 16);
+  (void)batch; (void)n; (void)k;
+  return 0;  // one CTA covers all of K (k <= 8192): no split-K scratch
 }
 
 extern "C" int maple_ternary_gemv(const void* x, int x_dtype, int64_t batch, int64_t k,
@@ -299,14 +446,15 @@ extern "C" int maple_ternary_gemv(const void* x, int x_dtype, int64_t batch, int
   p.x_stride = x_row_stride; p.y_stride = y_row_stride; p.x_div = 1;
   p.rows = (int)n; p.n_out = (int)n; p.n_experts = 1;
   p.K = (int)k; p.nwords = (int)(k / 16); p.eps = eps;
-  if (int rc = setup_ws(p, batch, workspace, workspace_bytes)) return rc;
-  const cudaError_t e = dispatch<kPlain>(p, x_dtype, alpha_dtype, rms_dtype, (int)batch,
-                                         static_cast<cudaStream_t>(stream));
+  (void)workspace; (void)workspace_bytes;
+  const cudaError_t e = dispatch2<kPlain>(p, x_dtype, alpha_dtype, rms_dtype, (int)batch,
+                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? kOk : kErrCuda;
 }
 
 extern "C" int64_t maple_ternary_expert_gemv_workspace_bytes(int64_t slots, int64_t n, int64_t k) {
-  return ws_bytes(slots, n, k / 16);
+  (void)slots; (void)n; (void)k;
+  return 0;
 }
 
 extern "C" int maple_ternary_expert_gemv(const void* x, int x_dtype, int64_t x_row_stride,
@@ -327,15 +475,16 @@ extern "C" int maple_ternary_expert_gemv(const void* x, int x_dtype, int64_t x_r
   p.rows = (int)n; p.n_out = (int)n; p.n_experts = (int)n_experts;
   p.expert_words = n * (k / 16); p.alpha_estride = n;
   p.K = (int)k; p.nwords = (int)(k / 16);
-  if (int rc = setup_ws(p, slots, workspace, workspace_bytes)) return rc;
-  const cudaError_t e = dispatch<kPlain>(p, x_dtype, alpha_dtype, 0, (int)slots,
-                                         static_cast<cudaStream_t>(stream));
+  (void)workspace; (void)workspace_bytes;
+  const cudaError_t e = dispatch2<kPlain>(p, x_dtype, alpha_dtype, 0, (int)slots,
+                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? kOk : kErrCuda;
 }
 
 extern "C" int64_t maple_ternary_expert_swiglu_workspace_bytes(int64_t slots, int64_t inter,
                                                                 int64_t k) {
-  return ws_bytes(slots, 2 * inter, k / 16);
+  (void)slots; (void)inter; (void)k;
+  return 0;
 }
 
 extern "C" int maple_ternary_expert_swiglu(const void* x, int x_dtype, int64_t x_row_stride,
@@ -357,9 +506,9 @@ extern "C" int maple_ternary_expert_swiglu(const void* x, int x_dtype, int64_t x
   p.rows = (int)(2 * inter); p.n_out = (int)inter; p.n_experts = (int)n_experts;
   p.expert_words = 2 * inter * (k / 16); p.alpha_estride = 2 * inter;
   p.K = (int)k; p.nwords = (int)(k / 16);
-  if (int rc = setup_ws(p, slots, workspace, workspace_bytes, 32)) return rc;
-  const cudaError_t e = dispatch<kSwiglu>(p, x_dtype, alpha_dtype, 0, (int)slots,
-                                          static_cast<cudaStream_t>(stream));
+  (void)workspace; (void)workspace_bytes;
+  const cudaError_t e = dispatch2<kSwiglu>(p, x_dtype, alpha_dtype, 0, (int)slots,
+                                           static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? kOk : kErrCuda;
 }
 
