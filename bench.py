@@ -33,6 +33,8 @@ def _args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="also time each operator of the decode step in its own CUDA graph (48 layers)")
     return ap.parse_args()
 
 
@@ -282,6 +284,8 @@ def main():
         "gpu_launches": Kst * (8 * cfg["num_hidden_layers"] + 4),
         "clocks": clocks.summary(),
     }
+    if args.breakdown:
+        line["breakdown_us_per_launch"] = op_breakdown(model, cache, dev)
     if rank == 0 and not args.no_cpu_baseline:
         v, cores, sample = cpu_baseline(cfg)
         line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
@@ -327,6 +331,77 @@ def swiglu_roofline(model, prompt, dev):
     k, inter = model.top_k, model.moe_intermediate
     nbytes = k * (2 * inter * H // 4 + 2 * inter * 2) + H * 2 + k * inter * 2
     return us, nbytes
+
+
+def op_breakdown(model, cache, dev):
+    """Warm in-graph time of each decode operator: run one decode step layer by
+    layer keeping every intermediate, then replay each operator over the 48
+    layers in its own CUDA graph (launched like the decode step, with PDL)."""
+    import torch
+
+    from maple_flash_dgx_spark_b200 import kernels as K
+
+    pos = torch.full((1,), int(cache.seen[0]) - 1, dtype=torch.int64, device=dev)
+    rot = model.rotary
+    steps = {name: [] for name in ("qkv_gemv", "qk_norm_rope_store", "attention", "o_gemv", "add_rms_norm",
+                                   "router_topk", "expert_swiglu", "expert_down_reduce")}
+    h = model.embed(torch.ones(1, dtype=torch.long, device=dev))
+    with torch.inference_mode():
+        for i, lay in enumerate(model.layers):
+            at, mlp = lay.self_attn, lay.mlp
+            kc, vc = cache.k[i][:1], cache.v[i][:1]
+            qkv = at.qkv_proj(h, rms_weight=lay.input_layernorm.weight, rms_eps=model.rms_eps)
+            q = K.apply_qkv_decode(qkv, at.q_norm.weight, at.k_norm.weight, rot.cos_table, rot.sin_table, kc, vc, pos,
+                                   num_heads=at.num_heads, num_kv_heads=at.num_kv_heads, head_dim=at.head_dim,
+                                   rotary_dim=rot.rotary_dim, use_rope=at.use_rope, use_qk_norm=True,
+                                   eps=model.rms_eps, rope_table=True)
+            attn = K.decode_gqa_attn(q, kc, vc, pos, scale=at.scale, window=None, split_len=cache.split_len)
+            o = at.o_proj(attn.reshape(1, -1))
+            res, normed = K.add_rms_norm(h, o, lay.post_attention_layernorm.weight, model.rms_eps)
+            idx, wt = K.router_topk(normed, mlp.gate_weight, mlp.top_k)
+            hs = mlp.up_gate.swiglu(normed, idx)
+            h2 = mlp.down.down_reduce(hs, idx, wt, residual=res)
+            pl = lay.post_attention_layernorm.weight
+            steps["qkv_gemv"].append(lambda at=at, h=h, lay=lay: at.qkv_proj(
+                h, rms_weight=lay.input_layernorm.weight, rms_eps=model.rms_eps))
+            steps["qk_norm_rope_store"].append(lambda at=at, qkv=qkv, kc=kc, vc=vc: K.apply_qkv_decode(
+                qkv, at.q_norm.weight, at.k_norm.weight, rot.cos_table, rot.sin_table, kc, vc, pos,
+                num_heads=at.num_heads, num_kv_heads=at.num_kv_heads, head_dim=at.head_dim,
+                rotary_dim=rot.rotary_dim, use_rope=at.use_rope, use_qk_norm=True, eps=model.rms_eps,
+                rope_table=True))
+            steps["attention"].append(lambda at=at, q=q, kc=kc, vc=vc: K.decode_gqa_attn(
+                q, kc, vc, pos, scale=at.scale, window=None, split_len=cache.split_len))
+            steps["o_gemv"].append(lambda at=at, attn=attn: at.o_proj(attn.reshape(1, -1)))
+            steps["add_rms_norm"].append(lambda h=h, o=o, pl=pl: K.add_rms_norm(h, o, pl, model.rms_eps))
+            steps["router_topk"].append(lambda mlp=mlp, normed=normed: K.router_topk(normed, mlp.gate_weight,
+                                                                                      mlp.top_k))
+            steps["expert_swiglu"].append(lambda mlp=mlp, normed=normed, idx=idx: mlp.up_gate.swiglu(normed, idx))
+            steps["expert_down_reduce"].append(lambda mlp=mlp, hs=hs, idx=idx, wt=wt, res=res: mlp.down.down_reduce(
+                hs, idx, wt, residual=res))
+            h = h2
+        out = {}
+        for name, fns in steps.items():
+            for f in fns:
+                f()
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            st = torch.cuda.Stream(dev)
+            st.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(st):
+                with torch.cuda.graph(g, stream=st):
+                    for f in fns:
+                        f()
+            torch.cuda.current_stream(dev).wait_stream(st)
+            g.replay()
+            torch.cuda.synchronize(dev)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(10):
+                g.replay()
+            b.record()
+            torch.cuda.synchronize(dev)
+            out[name] = round(a.elapsed_time(b) * 1000.0 / (10 * len(fns)), 2)
+    return out
 
 
 def _profiled_traffic(name: str):

@@ -157,15 +157,19 @@ int maple_apply_qkv_decode(const void* qkv, int x_dtype, int64_t batch, int64_t 
 /* GQA decode attention over [start, seqlen[b] + 1) split in chunks of
  * split_len positions with an in-kernel log-sum-exp merge.  Replaces
  * kernels/decode_attn.py:470 decode_gqa_attn.  head_dim in {64,128,256},
- * H/Hkv <= 8, split_len in {32,64,128}.  A bounded wait that gives up sets
- * bit 1 of *err. */
+ * H/Hkv <= 8, split_len in {32,64,128}.  Up to 16 splits merge inside a
+ * thread-block cluster (no workspace needed); more use the workspace.
+ * kv_final = 1 promises that K/V of positions before seqlen[b] were written
+ * before the previous launch on the stream (true for decode rows, false for a
+ * prompt fed as rows), letting those rows load early.  A bounded wait that
+ * gives up sets bit 1 of *err. */
 int64_t maple_decode_gqa_workspace_bytes(int64_t batch, int64_t num_heads, int64_t head_dim, int64_t max_len,
                                          int64_t split_len);
 int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, int64_t num_heads, int64_t q_sb,
                           int64_t q_sh, const void* k_cache, const void* v_cache, int64_t cache_batch,
                           int64_t num_kv_heads, int64_t cache_sb, int64_t cache_sh, int64_t max_len,
                           int64_t head_dim, const int64_t* seqlen, const int32_t* row_map, float scale,
-                          int64_t window, int64_t split_len, void* out, int64_t o_sb, int64_t o_sh,
+                          int64_t window, int64_t split_len, int kv_final, void* out, int64_t o_sb, int64_t o_sh,
                           void* workspace, int64_t workspace_bytes, int* err, void* stream);
 
 /* RTN-4 GEMV y = x . (scale*code + bias)^T per group.  Replaces

@@ -18,8 +18,12 @@
 // K/V tiles of a split are staged in shared memory with cp.async.bulk (TMA
 // bulk copy) completing on an mbarrier; the wait is bounded and a timeout is
 // reported through the error word instead of hanging.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "launch.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace mb {
 
@@ -159,6 +163,7 @@ struct AttnParams {
   int* err;
   int64_t q_sb, q_sh, kc_sb, kc_sh, vc_sb, vc_sh, o_sb, o_sh;
   int Hq, Hkv, G, Bc, T, P, NS, window;
+  int kv_final;           // 1: K/V at positions < seqlen[b] were final before the previous launch
   float scale;
 };
 
@@ -361,6 +366,198 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
   }
 }
 
+
+// Short contexts (at most 16 splits): the splits of one (row, kv head) form a
+// thread-block cluster.  Each CTA leaves its split's (acc, m, l) in its own
+// shared memory; after a cluster barrier the rank-0 CTA merges them in split
+// order through distributed shared memory (same arithmetic as the workspace
+// merge).  With kv_final, K/V rows of positions before seqlen[b] are copied
+// before the PDL wait; only the newest position waits for the previous launch.
+template <int XT, int D>
+__global__ void __launch_bounds__(256) gqa_cluster_kernel(AttnParams p) {
+  constexpr int U = D / 32;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t bar[2];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int P = p.P, G = p.G;
+  const int es = XT == kBF16 ? 2 : 4;
+  unsigned char* ktile = smem;
+  unsigned char* vtile = smem + (size_t)P * D * es;
+  float* scores = reinterpret_cast<float*>(smem + 2 * (size_t)P * D * es);  // [8][P]
+  float* pb = scores + 8 * P;                                                 // [8][P]
+  float* part = pb + 8 * P;                                                   // [8][D] acc, then m[8], l[8]
+  float* part_m = part + 8 * D;
+  float* part_l = part_m + 8;
+
+  const int64_t pos = p.seqlen[b];
+  const int kv_len = (int)min(pos + 1, (int64_t)p.T);
+  const int start = p.window > 0 ? max(0, kv_len - p.window) : 0;
+  const int ns = kv_len > start ? (kv_len - start + P - 1) / P : 0;
+  const bool active = s < ns;
+  const int t0 = start + s * P;
+  const int n = active ? min(P, kv_len - t0) : 0;
+  int cb = b;
+  if (p.row_map != nullptr) cb = p.row_map[b];
+  const bool cb_ok = cb >= 0 && cb < p.Bc;
+  if (!cb_ok) cb = 0;
+  const char* ksrc = static_cast<const char*>(p.kc) + (cb * p.kc_sb + h * p.kc_sh + (int64_t)t0 * D) * es;
+  const char* vsrc = static_cast<const char*>(p.vc) + (cb * p.vc_sb + h * p.vc_sh + (int64_t)t0 * D) * es;
+  // rows [0, n_pre) are final before the previous launch
+  const int n_pre = (p.kv_final && active) ? max(0, min(n, (int)(pos - t0))) : 0;
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    if (n_pre > 0) {
+      mbar_expect_tx(&bar[0], 2u * n_pre * D * es);
+      bulk_g2s(ktile, ksrc, (unsigned)(n_pre * D * es), &bar[0]);
+      bulk_g2s(vtile, vsrc, (unsigned)(n_pre * D * es), &bar[0]);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (tid == 0) {
+    if (!cb_ok) atomicOr(p.err, kErrFlagBounds);
+    if (n > n_pre) {
+      const unsigned off = (unsigned)(n_pre * D * es), bytes = (unsigned)((n - n_pre) * D * es);
+      mbar_expect_tx(&bar[1], 2u * bytes);
+      bulk_g2s(ktile + off, ksrc + off, bytes, &bar[1]);
+      bulk_g2s(vtile + off, vsrc + off, bytes, &bar[1]);
+    }
+  }
+  float qv[8][U];
+#pragma unroll
+  for (int g = 0; g < 8; ++g)
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      qv[g][u] = (g < G && active) ? load_f<XT>(static_cast<const char*>(p.q) + (b * p.q_sb + (h * G + g) * p.q_sh) * es,
+                                                lane + 32 * u)
+                                   : 0.0f;
+  __syncthreads();  // barriers initialised before anyone waits
+  bool ok = true;
+  for (int k = 0; k < 2; ++k) {
+    const bool need = (k == 0) ? n_pre > 0 : n > n_pre;
+    if (need) {
+      bool ready = false;
+      for (int i = 0; i < kWaitSpins && !ready; ++i) ready = mbar_try_wait(&bar[k], 0);
+      if (!ready) {
+        ok = false;
+        if (tid == 0) atomicOr(p.err, kErrFlagTimeout);
+        for (int i = 0; i < kWaitSpins && !ready; ++i) ready = mbar_try_wait(&bar[k], 0);
+      }
+    }
+  }
+  const bool work = active && ok;
+  const float ninf = __int_as_float(0xff800000);
+  if (work) {
+    for (int grp = warp; grp * 4 < n; grp += 8) {
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int t = grp * 4 + i;
+        float kk[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) kk[u] = t < n ? load_f<XT>(ktile + (size_t)t * D * es, lane + 32 * u) : 0.0f;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          float pj[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int u = 0; u < U; ++u) pj[u & 3] = __fmaf_rn(qv[g][u], kk[u], pj[u & 3]);
+          v[i * 8 + g] = __fadd_rn(__fadd_rn(__fadd_rn(pj[0], pj[1]), pj[2]), pj[3]);
+        }
+      }
+#pragma unroll
+      for (int m = 16; m >= 1; m >>= 1) {
+        const bool upper = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < m; ++i) {
+          const float keep = upper ? v[i + m] : v[i];
+          const float send = upper ? v[i] : v[i + m];
+          v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
+        }
+      }
+      const int t = grp * 4 + (lane >> 3), g = lane & 7;
+      if (t < n && g < G) scores[g * P + t] = __fmul_rn(v[0], p.scale);
+    }
+  }
+  __syncthreads();
+  if (work && warp < G) {
+    const int g = warp;
+    float sv[4];
+    float m = ninf;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = lane + 32 * u;
+      sv[u] = (t < n) ? scores[g * P + t] : ninf;
+      m = fmaxf(m, sv[u]);
+    }
+    m = warp_max(m);
+    float pp[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = lane + 32 * u;
+      pp[u] = (t < n) ? mexp(__fsub_rn(sv[u], m)) : 0.0f;
+      if (t < P) pb[g * P + t] = (t < n) ? bf16_to_f32(f32_to_bf16(pp[u])) : 0.0f;
+    }
+    const float l = r128_lane_finish(pp[0], pp[1], pp[2], pp[3]);
+    __syncwarp();
+    float acc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) acc[u] = 0.0f;
+    for (int t = 0; t < n; ++t) {
+      const float pt = pb[g * P + t];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        acc[u] = __fmaf_rn(pt, load_f<XT>(vtile + (size_t)t * D * es, lane + 32 * u), acc[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) part[g * D + lane + 32 * u] = acc[u];
+    if (lane == 0) {
+      part_m[g] = m;
+      part_l[g] = l;
+    }
+  }
+  cluster.sync();
+  if (s == 0 && warp < G && ns > 0) {
+    const int g = warp, hq = h * G + g;
+    float mj_all = ninf;
+    if (lane < ns) mj_all = cluster.map_shared_rank(part_m, lane)[g];
+    const float M = warp_max(mj_all);
+    float num[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) num[u] = 0.0f;
+    float den = 0.0f;
+    for (int j0 = 0; j0 < ns; j0 += 4) {
+      float mj[4], lj[4], aj[4][U];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int j = j0 + i;
+        if (j < ns) {
+          const float* rp = cluster.map_shared_rank(part, j);
+          mj[i] = rp[8 * D + g];
+          lj[i] = rp[8 * D + 8 + g];
+#pragma unroll
+          for (int u = 0; u < U; ++u) aj[i][u] = rp[g * D + lane + 32 * u];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (j0 + i < ns) {
+          const float w = mexp(__fsub_rn(mj[i], M));
+          den = __fmaf_rn(w, lj[i], den);
+#pragma unroll
+          for (int u = 0; u < U; ++u) num[u] = __fmaf_rn(w, aj[i][u], num[u]);
+        }
+      }
+    }
+    char* o = static_cast<char*>(p.out) + (b * p.o_sb + hq * p.o_sh) * es;
+#pragma unroll
+    for (int u = 0; u < U; ++u) store_f<XT>(o, lane + 32 * u, __fdiv_rn(num[u], den));
+  }
+  cluster.sync();  // peers keep their shared memory until the merge has read it
+}
+
 }  // namespace mb
 
 using namespace mb;
@@ -416,9 +613,9 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
                                      int64_t cache_batch, int64_t num_kv_heads, int64_t cache_sb,
                                      int64_t cache_sh, int64_t max_len, int64_t head_dim,
                                      const int64_t* seqlen, const int32_t* row_map, float scale,
-                                     int64_t window, int64_t split_len, void* out, int64_t o_sb,
-                                     int64_t o_sh, void* workspace, int64_t workspace_bytes, int* err,
-                                     void* stream) {
+                                     int64_t window, int64_t split_len, int kv_final, void* out,
+                                     int64_t o_sb, int64_t o_sh, void* workspace, int64_t workspace_bytes,
+                                     int* err, void* stream) {
   if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_len <= 0) return kErrShape;
   if (batch == 0) return kOk;
   if (num_heads % num_kv_heads != 0 || num_heads / num_kv_heads > 8) return kErrShape;
@@ -433,8 +630,8 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
   const int64_t ns = (max_len + split_len - 1) / split_len;
   if (batch * num_kv_heads * (int64_t)sizeof(unsigned) > kAttnTicketBytes || ns > 65535 || batch > 65535)
     return kErrShape;
-  if (ns > 1 && (!workspace || workspace_bytes < maple_decode_gqa_workspace_bytes(batch, num_heads, head_dim,
-                                                                                  max_len, split_len)))
+  if (ns > 16 && (!workspace || workspace_bytes < maple_decode_gqa_workspace_bytes(batch, num_heads, head_dim,
+                                                                                   max_len, split_len)))
     return kErrWorkspace;
   AttnParams p{};
   p.q = q; p.kc = k_cache; p.vc = v_cache; p.seqlen = seqlen; p.row_map = row_map; p.out = out; p.err = err;
@@ -445,10 +642,47 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
   p.o_sb = o_sb; p.o_sh = o_sh;
   p.Hq = (int)num_heads; p.Hkv = (int)num_kv_heads; p.G = (int)(num_heads / num_kv_heads);
   p.Bc = (int)cache_batch; p.T = (int)max_len; p.P = (int)split_len; p.NS = (int)ns;
-  p.window = (int)window; p.scale = scale;
+  p.window = (int)window; p.scale = scale; p.kv_final = kv_final;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (ns <= 16) {
+    // one cluster of CL >= ns CTAs per (row, kv head), merged in shared memory
+    int cl = 1;
+    while (cl < ns) cl *= 2;
+    const size_t smem = 2 * (size_t)split_len * head_dim * es + 2 * 8 * (size_t)split_len * sizeof(float) +
+                        (8 * (size_t)head_dim + 16) * sizeof(float);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)cl, (unsigned)num_kv_heads, (unsigned)batch);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    cudaError_t e = cudaSuccess;
+#define MB_ATTC(XT, DD)                                                                                       \
+  do {                                                                                                        \
+    auto kern = gqa_cluster_kernel<XT, DD>;                                                                   \
+    if (cl > 8) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);            \
+    if (e == cudaSuccess && smem > 32 * 1024)                                                                 \
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                 \
+    if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, kern, p);                                              \
+  } while (0)
+    if (x_dtype == kBF16) {
+      if (head_dim == 64) MB_ATTC(kBF16, 64); else if (head_dim == 128) MB_ATTC(kBF16, 128); else MB_ATTC(kBF16, 256);
+    } else {
+      if (head_dim == 64) MB_ATTC(kF32, 64); else if (head_dim == 128) MB_ATTC(kF32, 128); else MB_ATTC(kF32, 256);
+    }
+#undef MB_ATTC
+    return e == cudaSuccess ? kOk : kErrCuda;
+  }
   const size_t smem = 2 * (size_t)split_len * head_dim * es + 2 * 8 * (size_t)split_len * sizeof(float);
   dim3 grid((unsigned)ns, (unsigned)num_kv_heads, (unsigned)batch);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
 #define MB_ATT(XT, DD)                                                                        \
   do {                                                                                        \

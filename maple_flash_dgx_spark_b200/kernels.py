@@ -371,9 +371,12 @@ def gqa_splits(max_len: int, window: int | None) -> int:
 
 
 def attn_split_len(max_len: int, batch: int = 1, num_kv_heads: int = 4) -> int:
-    """Positions per attention split (32, 64 or 128): the largest whose grid
-    (splits x kv heads x batch) still covers ~2 waves of 148 SMs.  A CUDA-graph
-    constant fixed with the cache, and part of the canonical arithmetic."""
+    """Positions per attention split (32, 64 or 128), a CUDA-graph constant
+    fixed with the cache and part of the canonical arithmetic.  Contexts up to
+    1024 use 64 (at most 16 splits, merged inside one thread-block cluster);
+    longer ones the largest split whose grid still covers ~2 waves of 148 SMs."""
+    if max_len <= 1024:
+        return 64
     for p in (128, 64):
         if batch * num_kv_heads * -(-max_len // p) >= 296:
             return p
@@ -381,11 +384,13 @@ def attn_split_len(max_len: int, batch: int = 1, num_kv_heads: int = 4) -> int:
 
 
 def decode_gqa_attn(q, k_cache, v_cache, seqlen, *, row_map=None, scale: float, window: int | None,
-                    workspace=None, split_len: int | None = None):
+                    workspace=None, split_len: int | None = None, kv_final: bool = False):
     """GQA attention for ``q_len=1``.  Reference kernels/decode_attn.py:470-592.
     ``q`` is ``[B, H, 1, D]``, caches ``[B, n_kv, T, D]``; ``seqlen[b]`` is the
     index just written.  ``workspace`` may be a byte tensor from
-    :func:`attn_workspace` (a reference-style tuple is accepted and ignored)."""
+    :func:`attn_workspace` (a reference-style tuple is accepted and ignored).
+    ``kv_final`` promises K/V before ``seqlen[b]`` was written before the
+    previous launch (decode rows), so those rows can load early."""
     op = "decode_gqa_attn"
     if q.ndim != 4 or q.shape[2] != 1:
         raise ValueError(f"decode_gqa_attn expects q [B, H, 1, D], got {tuple(q.shape)}.")
@@ -404,14 +409,15 @@ def decode_gqa_attn(q, k_cache, v_cache, seqlen, *, row_map=None, scale: float, 
     out = torch.empty_like(q)
     q3, o3 = q[:, :, 0, :], out[:, :, 0, :]
     L = lib()
-    nbytes = L.maple_decode_gqa_workspace_bytes(bsz, n_q, head_dim, max_len, P)
+    nbytes = L.maple_decode_gqa_workspace_bytes(bsz, n_q, head_dim, max_len, P) if -(-max_len // P) > 16 else 0
     ws = workspace if isinstance(workspace, torch.Tensor) and workspace.numel() >= nbytes else _ws(q.device, nbytes)
     sl = seqlen.reshape(-1).to(torch.int64)
     rm = row_map.reshape(-1).to(torch.int32) if row_map is not None else None
     check(L.maple_decode_gqa_attn(
         ptr(q3), dtype_code(q, op), bsz, n_q, q3.stride(0), q3.stride(1), ptr(k_cache), ptr(v_cache), k_cache.shape[0],
         n_kv, k_cache.stride(0), k_cache.stride(1), max_len, head_dim, ptr(sl), ptr(rm), float(scale),
-        int(window or 0), P, ptr(o3), o3.stride(0), o3.stride(1), ptr(ws), ws.numel(), ptr(_err(q.device)),
+        int(window or 0), P, int(bool(kv_final)), ptr(o3), o3.stride(0), o3.stride(1), ptr(ws),
+        ws.numel() if ws is not None else 0, ptr(_err(q.device)),
         stream_ptr(q.device)), op)
     return out
 

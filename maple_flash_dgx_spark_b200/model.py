@@ -206,7 +206,7 @@ class MapleAttention:
         self.use_rope = use_rope
         self.layer_idx = layer_idx
 
-    def __call__(self, hidden, seqlen, row_map, rotary, cache, *, rms_weight, rms_eps):
+    def __call__(self, hidden, seqlen, row_map, rotary, cache, *, rms_weight, rms_eps, kv_final=False):
         rows = hidden.shape[0]
         qkv = self.qkv_proj(hidden, rms_weight=rms_weight, rms_eps=rms_eps)
         k_cache, v_cache = cache.k[self.layer_idx], cache.v[self.layer_idx]
@@ -218,7 +218,7 @@ class MapleAttention:
                              rotary_dim=rotary.rotary_dim, use_rope=self.use_rope, use_qk_norm=True,
                              eps=self.q_norm.eps, rope_table=True)
         attn = decode_gqa_attn(q, k_cache, v_cache, seqlen, row_map=row_map, scale=self.scale,
-                               window=self.sliding_window, split_len=cache.split_len)
+                               window=self.sliding_window, split_len=cache.split_len, kv_final=kv_final)
         return self.o_proj(attn.reshape(rows, -1))
 
 
@@ -247,9 +247,9 @@ class MapleDecoderLayer:
         self.input_layernorm = input_layernorm
         self.post_attention_layernorm = post_attention_layernorm
 
-    def __call__(self, hidden, seqlen, row_map, rotary, cache):
+    def __call__(self, hidden, seqlen, row_map, rotary, cache, kv_final=False):
         attn_out = self.self_attn(hidden, seqlen, row_map, rotary, cache, rms_weight=self.input_layernorm.weight,
-                                  rms_eps=self.input_layernorm.eps)
+                                  rms_eps=self.input_layernorm.eps, kv_final=kv_final)
         hidden, mlp_in = add_rms_norm(hidden, attn_out, self.post_attention_layernorm.weight,
                                       self.post_attention_layernorm.eps)
         return self.mlp(mlp_in, residual=hidden)
@@ -472,7 +472,7 @@ class MapleForCausalLM:
         self.rotary.ensure_length(cache.max_len)
         hidden = self.embed(input_ids.reshape(rows))
         for layer in self.layers:
-            hidden = layer(hidden, seqlen, row_map, self.rotary, cache)
+            hidden = layer(hidden, seqlen, row_map, self.rotary, cache, kv_final=seq_len == 1)
         cache.advance(seq_len, bsz)
         keep = hidden if seq_len == 1 else hidden[-logits_to_keep:] if logits_to_keep else hidden
         normed = self.norm(keep)

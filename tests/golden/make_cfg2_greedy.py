@@ -21,7 +21,7 @@ sys.path.insert(0, str(HERE.parent.parent))
 from maple_flash_dgx_spark_b200.synth import synthetic_config  # noqa: E402  (config dict only)
 from oracle.model import OracleModel, synth_tokens  # noqa: E402
 
-SEED, PROMPT, N_NEW, SPLIT = 2, 512, 64, 32
+SEED, PROMPT, N_NEW, SPLIT = 2, 512, 64, 64
 
 
 def main():

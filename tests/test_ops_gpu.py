@@ -134,8 +134,14 @@ def _attn_case(rs, B, Hq, Hkv, D, T, lens, Bc=None):
     (2, 2, 2, 64, 64, [20, 64], 32, 0),
     (3, 16, 2, 128, 600, [600, 17, 333], 128, 0),
     (2, 8, 8, 128, 512, [512, 100], 64, 96),
+    (1, 32, 4, 128, 512, [512], 32, 0),
+    (2, 32, 4, 128, 1024, [1024, 700], 64, 0),
 ])
-def test_qkv_decode_and_attention(cuda, K, B, Hq, Hkv, D, T, lens, split, window):
+@pytest.mark.parametrize("kv_final", [False, True])
+def test_qkv_decode_and_attention(cuda, K, B, Hq, Hkv, D, T, lens, split, window, kv_final):
+    """Up to 16 splits merge inside a thread-block cluster (sizes 1-16, idle
+    ranks included), more through the workspace; kv_final loads the
+    already-final rows before the PDL wait."""
     rs = rng(B * 31 + T)
     qkv, qw, kw, kc, vc, pos, cos, sin = _attn_case(rs, B, Hq, Hkv, D, T, lens)
     kc_d, vc_d = to_dev(kc, cuda, torch.bfloat16), to_dev(vc, cuda, torch.bfloat16)
@@ -150,7 +156,8 @@ def test_qkv_decode_and_attention(cuda, K, B, Hq, Hkv, D, T, lens, split, window
     np.testing.assert_array_equal(to_np(q)[:, :, 0], q_o)
     np.testing.assert_array_equal(to_np(kc_d), kc_o)
     np.testing.assert_array_equal(to_np(vc_d), vc_o)
-    out = K.decode_gqa_attn(q, kc_d, vc_d, sl, scale=D ** -0.5, window=window or None, split_len=split)
+    out = K.decode_gqa_attn(q, kc_d, vc_d, sl, scale=D ** -0.5, window=window or None, split_len=split,
+                            kv_final=kv_final)
     out_o = oracle.decode_gqa(q_o, kc_o, vc_o, pos, scale=np.float32(D ** -0.5), window=window, split_len=split)
     np.testing.assert_array_equal(to_np(out)[:, :, 0], out_o)
 
