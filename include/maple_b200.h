@@ -73,6 +73,45 @@ int maple_ternary_gemv_noalloc(const void* x, int x_dtype, int64_t batch, int64_
                                const void* rms_w, int rms_dtype, float eps, void* y, int64_t y_row_stride,
                                void* stream);
 
+/* ---- batched GEMM (weights read once per batch) ----------------------
+ * Replaces the batched branch of kernels/ternary_gemv.py:355-388
+ * (_ternary_gemm_kernel :156-258) and, for the experts,
+ * kernels/ternary_expert.py:125-234 / :403-468 at more than a few tokens.
+ * Results are bit-identical to the per-row entry points above.
+ *
+ * maple_fxa_encode: FXA digits of `rows` activation rows (with the input
+ * RMSNorm folded in when rms_w != NULL) into `frag`
+ * (maple_fxa_frag_bytes(rows, k) bytes) and `meta` (maple_fxa_meta_bytes),
+ * both 16-byte aligned, consumed by the GEMMs below. */
+int64_t maple_fxa_frag_bytes(int64_t rows, int64_t k);
+int64_t maple_fxa_meta_bytes(int64_t rows);
+int maple_fxa_encode(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t x_row_stride, const void* rms_w,
+                     int rms_dtype, float eps, void* frag, void* meta, void* stream);
+
+/* y[r] = alpha * (codes . x_r) (* rstd_r when use_rstd) for the encoded rows;
+ * codes [n, k/16].  k <= 4096. */
+int maple_ternary_gemm(const void* frag, const void* meta, int64_t rows, int64_t k, const uint32_t* codes, int64_t n,
+                       const void* alpha, int alpha_dtype, int use_rstd, void* y, int y_dtype, int64_t y_row_stride,
+                       int* err, void* stream);
+
+/* Sorts the n_slots = tokens * top_k routed slots by expert: offsets [E+1]
+ * int32, list [n_slots] uint32 slot ids (bit 31 set for an out-of-range id,
+ * listed under expert 0; its output row is NaN). */
+int maple_moe_plan(const int32_t* expert_ids, int64_t n_slots, int64_t n_experts, int32_t* offsets, uint32_t* list,
+                   void* stream);
+
+/* Grouped expert GEMM over a plan: slot s reads encoded row s / in_div
+ * (in_div = top_k when rows are tokens, 1 when they are slots) and writes
+ * row s of y.  codes [n_experts, code_rows, k/16]; swiglu != 0 runs the
+ * up|gate + clamp + SiLU epilogue (code_rows = 2 I, y [n_slots, I]).
+ * plan_final = 1 promises the plan was written before the previous launch
+ * on the stream, so weights load before the dependency wait. */
+int maple_ternary_grouped_gemm(const void* frag, const void* meta, int64_t in_rows, int64_t k, const uint32_t* codes,
+                               int64_t n_experts, int64_t code_rows, const void* alpha, int alpha_dtype,
+                               const int32_t* offsets, const uint32_t* list, int64_t n_slots, int64_t in_div,
+                               int swiglu, int plan_final, void* y, int y_dtype, int64_t y_row_stride, int* err,
+                               void* stream);
+
 /* Selected-expert GEMV.  Replaces kernels/ternary_expert.py:125
  * ternary_expert_gemv and linear.py:51 PackedTernaryExperts.forward.
  * Slot z uses expert expert_ids[z] (rows of codes [n_experts, n, k/16]) and

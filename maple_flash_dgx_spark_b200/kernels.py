@@ -71,6 +71,13 @@ def ternary_gemv(
             raise ValueError(f"rms_weight has {rms.numel()} elements, expected {k_in}.")
     y = out if out is not None else torch.empty(batch, n_out, device=x.device, dtype=x.dtype)
     L = lib()
+    if batch >= GEMM_MIN_ROWS and k_in <= 4096:
+        frag, meta = fxa_encode(x_mat, rms, rms_eps)
+        check(L.maple_ternary_gemm(ptr(frag), ptr(meta), batch, k_in, ptr(packed_weight), n_out, ptr(alpha),
+                                   dtype_code(alpha, op), int(rms is not None), ptr(y), dtype_code(y, op),
+                                   y.stride(0) if y.dim() > 1 else n_out, ptr(_err(x.device)),
+                                   stream_ptr(x.device)), op)
+        return y.reshape(*leading, n_out)
     nbytes = L.maple_ternary_gemv_workspace_bytes(batch, n_out, k_in)
     ws = _lib.workspace(x.device).get(nbytes) if nbytes else None
     st = L.maple_ternary_gemv(
@@ -106,7 +113,68 @@ def _expert_nk(packed_weight: torch.Tensor, packed_kn: bool, op: str) -> torch.T
     return packed_weight.contiguous()
 
 
-def ternary_expert_gemv(x, packed_weight, row_alpha, expert_ids, *, packed_kn: bool = False):
+# Row counts from which the batched kernels (weights read once per batch) take
+# over from the per-row GEMV launches.
+GEMM_MIN_ROWS = 4
+GROUPED_MIN_TOKENS = 4
+
+
+def fxa_encode(x2d: torch.Tensor, rms_weight: torch.Tensor | None = None, eps: float = 1e-6):
+    """FXA digits of each row of ``x2d`` ``[R, K]`` (optionally RMS-normalised
+    by ``rms_weight``) for the batched GEMMs: returns ``(frag, meta)`` uint8
+    buffers of ``maple_fxa_frag_bytes`` / ``maple_fxa_meta_bytes``."""
+    op = "fxa_encode"
+    require_cuda(op, x2d, rms_weight)
+    rows, k_in = x2d.shape
+    if x2d.stride(-1) != 1 or (x2d.stride(0) * x2d.element_size()) % 16 or x2d.data_ptr() % 16:
+        x2d = x2d.contiguous()
+    L = lib()
+    frag = torch.empty(L.maple_fxa_frag_bytes(rows, k_in), dtype=torch.uint8, device=x2d.device)
+    meta = torch.empty(L.maple_fxa_meta_bytes(rows), dtype=torch.uint8, device=x2d.device)
+    check(L.maple_fxa_encode(ptr(x2d), dtype_code(x2d, op), rows, k_in, x2d.stride(0), ptr(rms_weight),
+                             dtype_code(rms_weight, op) if rms_weight is not None else 0, float(eps), ptr(frag),
+                             ptr(meta), stream_ptr(x2d.device)), op)
+    return frag, meta
+
+
+class MoePlan:
+    """(token, slot) pairs of a routing decision sorted by expert on the device
+    (``offsets [E+1]`` int32, ``slots`` uint32), shared by the grouped up|gate
+    and down GEMMs of one MoE layer."""
+
+    def __init__(self, offsets: torch.Tensor, slots: torch.Tensor, n_experts: int, n_slots: int):
+        self.offsets = offsets
+        self.slots = slots
+        self.n_experts = n_experts
+        self.n_slots = n_slots
+
+
+def moe_plan(expert_ids: torch.Tensor, n_experts: int) -> MoePlan:
+    op = "moe_plan"
+    require_cuda(op, expert_ids)
+    ids = expert_ids.reshape(-1).to(torch.int32).contiguous()
+    n = ids.numel()
+    offsets = torch.empty(n_experts + 1, dtype=torch.int32, device=ids.device)
+    slots = torch.empty(max(n, 1), dtype=torch.int32, device=ids.device)
+    check(lib().maple_moe_plan(ptr(ids), n, n_experts, ptr(offsets), ptr(slots), stream_ptr(ids.device)), op)
+    return MoePlan(offsets, slots, n_experts, n)
+
+
+def _grouped(op, x_rows, per, w, alpha, plan, swiglu, out_rows, n_out, dtype):
+    """Grouped expert GEMM: input row of slot s is ``s // per``."""
+    E, rows, nwords = w.shape
+    k_in = nwords * _CODES_PER_WORD
+    frag, meta = fxa_encode(x_rows)
+    y = torch.empty(out_rows, n_out, device=x_rows.device, dtype=dtype)
+    check(lib().maple_ternary_grouped_gemm(
+        ptr(frag), ptr(meta), x_rows.shape[0], k_in, ptr(w), E, rows, ptr(alpha), dtype_code(alpha, op),
+        ptr(plan.offsets), ptr(plan.slots), plan.n_slots, per, int(swiglu), 1, ptr(y), dtype_code(y, op), n_out,
+        ptr(_err(x_rows.device)), stream_ptr(x_rows.device)), op)
+    return y
+
+
+def ternary_expert_gemv(x, packed_weight, row_alpha, expert_ids, *, packed_kn: bool = False,
+                        plan: MoePlan | None = None):
     """Indexed GEMV over stacked experts.  Reference kernels/ternary_expert.py:125-234.
 
     ``x`` is one row per token (``x.shape[:-1] == expert_ids.shape[:-1]``) or one
@@ -135,6 +203,11 @@ def ternary_expert_gemv(x, packed_weight, row_alpha, expert_ids, *, packed_kn: b
     slots = ids.numel()
     xm = x.reshape(-1, k_in).contiguous()
     alpha = row_alpha.contiguous()
+    if k_in <= 4096 and (plan is not None or slots // max(id_shape[-1] if id_shape else 1, 1) >= GROUPED_MIN_TOKENS):
+        dtype_code(x, op)
+        plan = plan if plan is not None else moe_plan(ids, E)
+        y = _grouped(op, xm, per, w, alpha, plan, False, slots, N, x.dtype)
+        return y.reshape(*id_shape, N)
     y = torch.empty(slots, N, device=x.device, dtype=x.dtype)
     L = lib()
     ws = _ws(x.device, L.maple_ternary_expert_gemv_workspace_bytes(slots, N, k_in))
@@ -144,7 +217,8 @@ def ternary_expert_gemv(x, packed_weight, row_alpha, expert_ids, *, packed_kn: b
     return y.reshape(*id_shape, N)
 
 
-def ternary_expert_swiglu(x, packed_weight, row_alpha, expert_ids, *, packed_kn: bool = False):
+def ternary_expert_swiglu(x, packed_weight, row_alpha, expert_ids, *, packed_kn: bool = False,
+                          plan: MoePlan | None = None):
     """Fused up|gate GEMV + clamp + SiLU.  Reference kernels/ternary_expert.py:403-468.
     Returns ``[..., topk, I]`` with ``I = packed rows / 2``."""
     op = "ternary_expert_swiglu"
@@ -170,6 +244,11 @@ def ternary_expert_swiglu(x, packed_weight, row_alpha, expert_ids, *, packed_kn:
     tokens = xm.shape[0]
     ids = expert_ids.reshape(-1).to(torch.int32).contiguous()
     alpha = row_alpha.contiguous()
+    if k_in <= 4096 and (plan is not None or tokens >= GROUPED_MIN_TOKENS):
+        dtype_code(x, op)
+        plan = plan if plan is not None else moe_plan(ids, E)
+        y = _grouped(op, xm, topk, w, alpha, plan, True, tokens * topk, inter, x.dtype)
+        return y.reshape(*id_shape, inter)
     y = torch.empty(tokens * topk, inter, device=x.device, dtype=x.dtype)
     L = lib()
     ws = _ws(x.device, L.maple_ternary_expert_swiglu_workspace_bytes(tokens * topk, inter, k_in))
@@ -216,9 +295,16 @@ def ternary_expert_down_sum(x, packed_weight, row_alpha, expert_ids, topk_weight
 
 
 def ternary_expert_down_reduce(x, packed_weight, row_alpha, expert_ids, topk_weight, residual=None, *,
-                               packed_kn: bool = False):
+                               packed_kn: bool = False, plan: MoePlan | None = None):
     """The reference model's down + combine (model.py:471-473: ternary_expert_gemv
-    with per-slot outputs in ``x.dtype``, then moe_reduce_add) in one launch."""
+    with per-slot outputs in ``x.dtype``, then moe_reduce_add): one launch for a
+    few tokens; from GROUPED_MIN_TOKENS tokens (or with a ``plan``) the grouped
+    GEMM (each expert's weights read once) followed by moe_reduce_add, with the
+    same rounding."""
+    tokens = int(expert_ids.numel() // max(int(expert_ids.shape[-1]), 1)) if expert_ids.ndim else 0
+    if plan is not None or tokens >= GROUPED_MIN_TOKENS:
+        y = ternary_expert_gemv(x, packed_weight, row_alpha, expert_ids, packed_kn=packed_kn, plan=plan)
+        return moe_reduce_add(y, topk_weight, residual)
     return _down(x, packed_weight, row_alpha, expert_ids, topk_weight, residual, packed_kn,
                  lib().maple_ternary_expert_down_reduce, "ternary_expert_down_reduce")
 

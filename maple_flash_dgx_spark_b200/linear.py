@@ -43,21 +43,21 @@ class PackedTernaryExperts:
         self.packed_weight = packed_weight.contiguous()
         self.row_alpha = row_alpha.contiguous()
 
-    def forward(self, x, expert_ids):
-        return ternary_expert_gemv(x, self.packed_weight, self.row_alpha, expert_ids)
+    def forward(self, x, expert_ids, plan=None):
+        return ternary_expert_gemv(x, self.packed_weight, self.row_alpha, expert_ids, plan=plan)
 
-    def swiglu(self, x, expert_ids):
-        return ternary_expert_swiglu(x, self.packed_weight, self.row_alpha, expert_ids)
+    def swiglu(self, x, expert_ids, plan=None):
+        return ternary_expert_swiglu(x, self.packed_weight, self.row_alpha, expert_ids, plan=plan)
 
     def down_sum(self, x, expert_ids, topk_weight, residual=None):
         return ternary_expert_down_sum(x, self.packed_weight, self.row_alpha, expert_ids, topk_weight,
                                        residual=residual)
 
-    def down_reduce(self, x, expert_ids, topk_weight, residual=None):
-        """Down projection + the model's weighted combine + residual in one launch
-        (the rounding of ``forward`` followed by ``moe_reduce_add``)."""
+    def down_reduce(self, x, expert_ids, topk_weight, residual=None, plan=None):
+        """Down projection + the model's weighted combine + residual (the
+        rounding of ``forward`` followed by ``moe_reduce_add``)."""
         return ternary_expert_down_reduce(x, self.packed_weight, self.row_alpha, expert_ids, topk_weight,
-                                          residual=residual)
+                                          residual=residual, plan=plan)
 
     __call__ = forward
 

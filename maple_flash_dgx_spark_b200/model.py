@@ -21,10 +21,12 @@ from pathlib import Path
 import torch
 
 from maple_flash_dgx_spark_b200.kernels import (
+    GROUPED_MIN_TOKENS,
     add_rms_norm,
     apply_qkv_decode,
     attn_split_len,
     decode_gqa_attn,
+    moe_plan,
     rms_norm,
     router_topk,
 )
@@ -236,8 +238,12 @@ class MapleSparseMoeBlock:
 
     def __call__(self, hidden_states, residual=None):
         idx, wt = router_topk(hidden_states, self.gate_weight, self.top_k)
-        h = self.up_gate.swiglu(hidden_states, idx)
-        return self.down.down_reduce(h, idx, wt, residual=residual)
+        tokens = hidden_states.numel() // hidden_states.shape[-1]
+        # from a few tokens on, sort the slots by expert once and run each
+        # selected expert's weights once over all of its tokens
+        plan = moe_plan(idx, self.gate_weight.shape[0]) if tokens >= GROUPED_MIN_TOKENS else None
+        h = self.up_gate.swiglu(hidden_states, idx, plan=plan)
+        return self.down.down_reduce(h, idx, wt, residual=residual, plan=plan)
 
 
 class MapleDecoderLayer:

@@ -110,3 +110,37 @@ def test_cfg2_first_64_greedy_ids_equal_oracle(cuda):
     prompt = synth_tokens(gold["seed"], gold["prompt_len"], cfg["vocab_size"])
     res = run_generate(model, torch.from_numpy(prompt), max_tokens=gold["n_new"], temperature=0.0, log=None)
     assert res.token_ids == gold["ids"]
+
+
+def test_batched_decode_equals_single_sequences(cuda):
+    """Ragged prompts prefilled per slot, then decoded as one batch (batched
+    GEMM / grouped experts): every row's greedy ids and logits equal that
+    sequence decoded alone at batch 1."""
+    cfg = tiny_config(2)
+    model = build(cfg, 19, cuda)
+    lens = [5, 9, 12, 7, 16]
+    prompts = [torch.from_numpy(synth_tokens(100 + i, n, cfg["vocab_size"])).to(cuda) for i, n in enumerate(lens)]
+    B, n_new, max_len = len(lens), 10, 40
+    cache = model.make_cache(max_len=max_len, batch=B)
+    nxt = []
+    for b, p in enumerate(prompts):
+        with cache.prefill_slot(b):
+            nxt.append(int(model.forward(p.reshape(1, -1), cache=cache)[0, -1].argmax()))
+    ids = [[t] for t in nxt]
+    cur = torch.tensor(nxt, device=cuda).reshape(B, 1)
+    for _ in range(n_new):
+        logits = model.forward(cur, cache=cache)
+        cur = logits[:, -1].argmax(-1).reshape(B, 1)
+        for b in range(B):
+            ids[b].append(int(cur[b]))
+    for b, p in enumerate(prompts):
+        c1 = model.make_cache(max_len=max_len, batch=1)
+        assert c1.split_len == cache.split_len
+        t = int(model.forward(p.reshape(1, -1), cache=c1)[0, -1].argmax())
+        seq = [t]
+        for _ in range(n_new):
+            lg = model.forward(torch.tensor([[t]], device=cuda), cache=c1)
+            t = int(lg[0, -1].argmax())
+            seq.append(t)
+        assert seq == ids[b]
+        torch.testing.assert_close(lg[0, -1], logits[b, -1], rtol=0, atol=0)
