@@ -251,6 +251,39 @@ int maple_rtn4_embedding(const int64_t* ids, int64_t batch, const uint32_t* code
                          const void* biases, int s_dtype, int64_t vocab, int64_t hidden, int64_t group_size,
                          void* out, int out_dtype, int64_t out_row_stride, int* err, void* stream);
 
+/* ---- FlashHead (flash_head.py:330-369 FlashHead.__call__) ----------------
+ * maple_topk_select: indices of the k largest of n scores in ascending index
+ * order (replaces torch.topk at flash_head.py:343); NaN ranks highest, ties
+ * at the k-th value take the lowest indices.  k <= n <= 2^30. */
+int maple_topk_select(const void* x, int x_dtype, int64_t n, int64_t k, int32_t* out, void* stream);
+
+/* Fills out[0..vocab) with -inf, then writes the probe logits
+ * probe[p*cluster_size + i] to token token_map[cluster_ids[p]][i] and
+ * force[j] to token force_ids[j] (replaces the fill_/index_put_ at
+ * flash_head.py:365-368).  An out-of-range cluster or token is skipped and
+ * sets bit 2 of *err. */
+int maple_flash_scatter(const void* probe, int x_dtype, const int32_t* cluster_ids, int64_t n_probes,
+                        int64_t cluster_size, const int32_t* token_map, int64_t n_clusters, const void* force,
+                        const int64_t* force_ids, int64_t n_force, void* out, int64_t vocab, int* err,
+                        void* stream);
+
+/* ---- checkpoint packing (pack.py:23-149), bit-exact with the NumPy code ---
+ * maple_pack_codes: n_codes uint8 codes -> n_codes * bits / 32 words, codes
+ * LSB first, fields summed in 64 bits (bits = 2 or 4).
+ * maple_unpack_codes: the inverse, one uint8 per code.
+ * maple_ternarize: rows x k weights (k % 128 == 0, k <= 16384) -> packed
+ * codes [rows, k/16] and alpha [rows] (NumPy float32 pairwise means).
+ * maple_quantize_rtn / maple_dequantize_rtn: affine 4-bit RTN along rows
+ * (scales and biases fp32, [rows, k/group]). */
+int maple_pack_codes(const uint8_t* codes, int64_t n_codes, int bits, uint32_t* out, void* stream);
+int maple_unpack_codes(const uint32_t* words, int64_t n_words, int bits, uint8_t* out, void* stream);
+int maple_ternarize(const void* w, int w_dtype, int64_t rows, int64_t k, float threshold_scale, uint32_t* packed,
+                    void* alpha, int alpha_dtype, void* stream);
+int maple_quantize_rtn(const void* w, int w_dtype, int64_t rows, int64_t k, int64_t group_size, uint32_t* packed,
+                       float* scales, float* biases, void* stream);
+int maple_dequantize_rtn(const uint32_t* packed, const float* scales, const float* biases, int64_t rows, int64_t k,
+                         int64_t group_size, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,6 +41,13 @@ _SIGS: dict[str, tuple] = {
     "maple_ternary_gemv_workspace_bytes": (i64, [i64, i64, i64]),
     "maple_ternary_gemv": (i32, [vp, i32, i64, i64, i64, vp, i64, vp, i32, vp, i32, f32, vp, i64, vp, i64, vp]),
     "maple_ternary_gemv_noalloc": (i32, [vp, i32, i64, i64, i64, vp, i64, vp, i32, vp, i32, f32, vp, i64, vp]),
+    "maple_topk_select": (i32, [vp, i32, i64, i64, vp, vp]),
+    "maple_flash_scatter": (i32, [vp, i32, vp, i64, i64, vp, i64, vp, vp, i64, vp, i64, vp, vp]),
+    "maple_pack_codes": (i32, [vp, i64, i32, vp, vp]),
+    "maple_unpack_codes": (i32, [vp, i64, i32, vp, vp]),
+    "maple_ternarize": (i32, [vp, i32, i64, i64, f32, vp, vp, i32, vp]),
+    "maple_quantize_rtn": (i32, [vp, i32, i64, i64, i64, vp, vp, vp, vp]),
+    "maple_dequantize_rtn": (i32, [vp, vp, vp, i64, i64, i64, vp, vp]),
     "maple_fxa_frag_bytes": (i64, [i64, i64]),
     "maple_fxa_meta_bytes": (i64, [i64]),
     "maple_fxa_encode": (i32, [vp, i32, i64, i64, i64, vp, i32, f32, vp, vp, vp]),

@@ -42,7 +42,8 @@ def pack_2bit(codes: np.ndarray) -> np.ndarray:
     if k % 16:
         raise ValueError(f"2-bit packing requires the last axis to be a multiple of 16; got {k}.")
     c = codes.astype(np.uint64).reshape(*lead, k // 16, 16)
-    return np.bitwise_or.reduce(c << _SHIFTS_2, axis=-1).astype(np.uint32)
+    # the shifted fields are summed in 64 bits and narrowed (codes > 3 carry)
+    return np.sum(c << _SHIFTS_2, axis=-1, dtype=np.uint64).astype(np.uint32)
 
 
 def unpack_2bit(packed: np.ndarray) -> np.ndarray:
@@ -58,7 +59,7 @@ def pack_4bit(codes: np.ndarray) -> np.ndarray:
     if k % 8:
         raise ValueError(f"4-bit packing requires the last axis to be a multiple of 8; got {k}.")
     c = codes.astype(np.uint64).reshape(*lead, k // 8, 8)
-    return np.bitwise_or.reduce(c << _SHIFTS_4, axis=-1).astype(np.uint32)
+    return np.sum(c << _SHIFTS_4, axis=-1, dtype=np.uint64).astype(np.uint32)
 
 
 def unpack_4bit(packed: np.ndarray) -> np.ndarray:
@@ -325,6 +326,43 @@ def rtn4_gemv(x, packed, scales, biases=None, group_size=HEAD_GROUP_SIZE, row_in
     y = np.empty((x2.shape[0], n), np.float32)
     lib().orc_rtn4_gemv(x2, x2.shape[0], k, packed, n, scales, bp, int(group_size), rip, int(out_bf16), y)
     return y.reshape(*x.shape[:-1], n)
+
+
+def order_keys(x):
+    """float32 -> uint32 keys in the float order, NaN above everything."""
+    x = _f32(x)
+    u = x.view(np.uint32).astype(np.uint64)
+    key = np.where(u & 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)
+    return np.where(np.isnan(x), np.uint64(0xFFFFFFFF), key)
+
+
+def topk_select(scores, k):
+    """Indices of the k largest scores (ties -> lowest index), ascending; the
+    canonical form of flash_head.py:343 torch.topk as a set."""
+    keys = order_keys(np.asarray(scores).reshape(-1)).astype(np.int64)
+    order = np.lexsort((np.arange(keys.size), -keys))
+    return np.sort(order[:k]).astype(np.int32)
+
+
+def flash_head(hidden, *, centroids_weight, centroids_scales, centroids_biases, centroid_group, token_map,
+               head_weight, head_scales, head_biases, group_size, force_ids, force_weight, force_scales,
+               force_biases, n_probes, vocab_size):
+    """Reference flash_head.py:330-369 (FlashHead.__call__): logits [V] with
+    -inf outside the probed clusters' tokens and the forced tokens."""
+    hv = _f32(hidden).reshape(-1, _f32(hidden).shape[-1])[-1:]
+    scores = rtn4_gemv(hv, centroids_weight, centroids_scales, centroids_biases, centroid_group)[0]
+    cids = topk_select(scores, n_probes)
+    n_clusters, cs = token_map.shape
+    rows = (cids.astype(np.int64)[:, None] * cs + np.arange(cs)).reshape(-1)
+    nw = head_weight.shape[-1]
+    hb = None if head_biases is None else np.asarray(head_biases).reshape(n_clusters * cs, -1)
+    probe = rtn4_gemv(hv, np.asarray(head_weight).reshape(-1, nw), np.asarray(head_scales).reshape(n_clusters * cs, -1),
+                      hb, group_size, row_index=rows)[0]
+    full = np.full(vocab_size, -np.inf, np.float32)
+    full[np.asarray(token_map)[cids].reshape(-1)] = probe
+    if len(force_ids):
+        full[np.asarray(force_ids)] = rtn4_gemv(hv, force_weight, force_scales, force_biases, group_size)[0]
+    return full, cids
 
 
 def argmax(logits):
