@@ -144,3 +144,36 @@ def test_batched_decode_equals_single_sequences(cuda):
             seq.append(t)
         assert seq == ids[b]
         torch.testing.assert_close(lg[0, -1], logits[b, -1], rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+def test_batched_generate_equals_run_generate(cuda, graphs):
+    """Reference generate.py:842-1028: batched greedy decode (per-row caps,
+    retirement with slot compaction, bucketed graph widths) gives every row
+    the ids of decoding that prompt alone."""
+    from maple_flash_dgx_spark_b200.generate import batched_generate, run_generate
+
+    cfg = tiny_config(2)
+    model = build(cfg, 23, cuda)
+    lens = [6, 11, 4, 9, 13, 7]
+    caps = [12, 3, 9, 12, 5, 1]
+    prompts = [synth_tokens(200 + i, n, cfg["vocab_size"]) for i, n in enumerate(lens)]
+    res = batched_generate(model, prompts, max_new=caps, graphs=graphs, stop_ids=set(), log=None)
+    assert [len(t) for t in res.token_ids] == caps
+    for p, cap, got in zip(prompts, caps, res.token_ids):
+        want = run_generate(model, torch.from_numpy(p), max_tokens=cap, temperature=0.0, log=None).token_ids
+        assert got == want
+    if graphs:
+        assert res.widths and res.widths[0] == 6 and res.widths[-1] <= 2  # live rows shrink to narrower graphs
+
+
+def test_batched_generate_sampled_graph_equals_eager(cuda):
+    from maple_flash_dgx_spark_b200.generate import batched_generate
+
+    cfg = tiny_config(2)
+    model = build(cfg, 29, cuda)
+    prompts = [synth_tokens(300 + i, 5 + i, cfg["vocab_size"]) for i in range(5)]
+    kw = dict(max_tokens=10, temperature=0.9, top_p=0.9, top_k=16, seed=7, stop_ids=set(), log=None)
+    a = batched_generate(model, prompts, graphs=True, **kw)
+    b = batched_generate(model, prompts, graphs=False, **kw)
+    assert a.token_ids == b.token_ids
