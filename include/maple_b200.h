@@ -99,6 +99,19 @@ int maple_ternary_gemm(const void* frag, const void* meta, int64_t rows, int64_t
  * listed under expert 0; its output row is NaN). */
 int maple_moe_plan(const int32_t* expert_ids, int64_t n_slots, int64_t n_experts, int32_t* offsets, uint32_t* list,
                    void* stream);
+/* The same for the experts [e_first, e_first + n_local) held by one rank
+ * under expert parallelism (offsets [n_local+1] by local expert; slots of
+ * other ranks' experts are not listed). */
+int maple_moe_plan_range(const int32_t* expert_ids, int64_t n_slots, int64_t n_experts, int64_t e_first,
+                         int64_t n_local, int32_t* offsets, uint32_t* list, void* stream);
+
+/* Expert-parallel combine (model.py:471-473 moe_reduce_add, after an
+ * all-to-all): recv [world][tokens*topk][n] holds each rank's rows for this
+ * rank's tokens; y[t] = sum_j w[t,j] * recv[owner(e_tj)][t*topk+j] (+ residual)
+ * with owner(e) = e / (n_experts / world), in moe_reduce_add's order. */
+int maple_ep_combine(const void* recv, int x_dtype, int64_t world, int64_t tokens, int64_t topk, int64_t n,
+                     const int32_t* expert_ids, const float* topk_weight, int64_t n_experts, const void* residual,
+                     void* y, void* stream);
 
 /* Grouped expert GEMM over a plan: slot s reads encoded row s / in_div
  * (in_div = top_k when rows are tokens, 1 when they are slots) and writes

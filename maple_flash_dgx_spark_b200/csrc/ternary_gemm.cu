@@ -65,39 +65,46 @@ __global__ void __launch_bounds__(256) fxa_encode_kernel(const void* x, int64_t 
 }
 
 // --------------------------------------------------------------- plan ----
-// Counting sort of slots (t*top_k + j) by expert.  offsets[e] .. offsets[e+1]
-// index list[]; an out-of-range id is listed under expert 0 with kBadSlot set
-// (its output row becomes NaN, as in the batch-1 expert GEMV).  The order
-// inside an expert is irrelevant: every row's result is exact on its own.
-__global__ void __launch_bounds__(1024) moe_plan_kernel(const int* ids, int n_slots, int E, int* offsets,
-                                                        unsigned* list) {
-  extern __shared__ int cnt[];  // [E] counts, then [E] cursors
-  int* cur = cnt + E;
+// Counting sort of slots (t*top_k + j) by expert, for the experts
+// [e_first, e_first + n_local) held here (all of them on one GPU; a rank's
+// share under expert parallelism).  offsets[e] .. offsets[e+1] index list[]
+// by local expert.  An out-of-range id is listed under expert 0 with
+// kBadSlot set (its output row becomes NaN, as in the batch-1 expert GEMV).
+// The order inside an expert is irrelevant: every row's result is exact on
+// its own.
+__global__ void __launch_bounds__(1024) moe_plan_kernel(const int* ids, int n_slots, int E, int e_first, int n_local,
+                                                        int* offsets, unsigned* list) {
+  extern __shared__ int cnt[];  // [n_local] counts, then [n_local] cursors
+  int* cur = cnt + n_local;
   pdl_wait();
   pdl_trigger();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  for (int e = threadIdx.x; e < n_local; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   for (int s = threadIdx.x; s < n_slots; s += blockDim.x) {
     int e = ids[s];
     if (e < 0 || e >= E) e = 0;
-    atomicAdd(&cnt[e], 1);
+    e -= e_first;
+    if (e >= 0 && e < n_local) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     int acc = 0;
-    for (int e = 0; e < E; ++e) {
+    for (int e = 0; e < n_local; ++e) {
       offsets[e] = acc;
       cur[e] = acc;
       acc += cnt[e];
     }
-    offsets[E] = acc;
+    offsets[n_local] = acc;
   }
   __syncthreads();
   for (int s = threadIdx.x; s < n_slots; s += blockDim.x) {
     const int e0 = ids[s];
     const bool bad = e0 < 0 || e0 >= E;
-    const int pos = atomicAdd(&cur[bad ? 0 : e0], 1);
-    list[pos] = static_cast<unsigned>(s) | (bad ? kBadSlot : 0u);
+    const int e = (bad ? 0 : e0) - e_first;
+    if (e >= 0 && e < n_local) {
+      const int pos = atomicAdd(&cur[e], 1);
+      list[pos] = static_cast<unsigned>(s) | (bad ? kBadSlot : 0u);
+    }
   }
 }
 
@@ -455,18 +462,25 @@ extern "C" int maple_ternary_gemm(const void* frag, const void* meta, int64_t ro
   return e == cudaSuccess ? kOk : kErrCuda;
 }
 
-extern "C" int maple_moe_plan(const int32_t* ids, int64_t n_slots, int64_t n_experts, int32_t* offsets,
-                              uint32_t* list, void* stream) {
-  if (n_slots < 0 || n_experts <= 0 || n_experts > 8192) return kErrShape;
+extern "C" int maple_moe_plan_range(const int32_t* ids, int64_t n_slots, int64_t n_experts, int64_t e_first,
+                                    int64_t n_local, int32_t* offsets, uint32_t* list, void* stream) {
+  if (n_slots < 0 || n_experts <= 0 || n_local <= 0 || n_local > 8192 || e_first < 0 ||
+      e_first + n_local > n_experts)
+    return kErrShape;
   if (!offsets || (n_slots > 0 && (!ids || !list)) || n_slots > (1LL << 31) - 1) return kErrShape;
-  const size_t smem = 2 * (size_t)n_experts * sizeof(int);
+  const size_t smem = 2 * (size_t)n_local * sizeof(int);
   auto kern = moe_plan_kernel;
   cudaError_t e = cudaSuccess;
   if (smem > 32 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess)
     e = launch_k(kern, dim3(1), dim3(1024), smem, static_cast<cudaStream_t>(stream), ids, (int)n_slots,
-                 (int)n_experts, offsets, list);
+                 (int)n_experts, (int)e_first, (int)n_local, offsets, list);
   return e == cudaSuccess ? kOk : kErrCuda;
+}
+
+extern "C" int maple_moe_plan(const int32_t* ids, int64_t n_slots, int64_t n_experts, int32_t* offsets,
+                              uint32_t* list, void* stream) {
+  return maple_moe_plan_range(ids, n_slots, n_experts, 0, n_experts, offsets, list, stream);
 }
 
 extern "C" int maple_ternary_grouped_gemm(const void* frag, const void* meta, int64_t in_rows, int64_t k,

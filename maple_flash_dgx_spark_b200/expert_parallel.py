@@ -1,0 +1,215 @@
+"""Expert-parallel batched decode over the GPUs of one node.
+
+One process per GPU (``torch.distributed``, NCCL).  For a batch of B
+sequences on W ranks:
+
+* attention is data-parallel: rank r holds B/W sequences, their KV cache and
+  a replica of the attention, router and norm weights;
+* experts are partitioned: rank r holds experts [r*E/W, (r+1)*E/W);
+* per MoE layer, an all-gather carries every rank's routed rows and top-k ids
+  to every rank (dispatch), each rank runs its experts over the slots routed
+  to them (grouped GEMMs, weights read once), and an all-to-all returns to
+  each token's rank the rows computed for its slots (combine), summed in the
+  single-GPU order by ``ep_combine``;
+* the RTN-4 lm_head is vocabulary-sharded: each rank scores its V/W rows for
+  all B tokens, takes its local argmax, and an all-gather of (value, index)
+  candidates picks the global first maximum.
+
+Every per-row result equals single-GPU batched decode bit for bit: routing,
+expert rows, the combine order and the argmax tie rule are the same.
+
+Reference: model.py:448-474 (MoE block), generate.py:842-1028 (batched
+decode); the reference itself runs on one GPU.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from maple_flash_dgx_spark_b200.kernels import (
+    argmax,
+    ep_combine,
+    moe_plan,
+    rtn4_gemv,
+    router_topk,
+    ternary_expert_gemv,
+    ternary_expert_swiglu,
+)
+
+_EXPERT_KEYS = ("up_proj", "gate_proj", "down_proj")
+
+
+def expert_range(n_experts: int, rank: int, world: int) -> tuple[int, int]:
+    """(first expert, experts held) of ``rank``."""
+    if n_experts % world:
+        raise ValueError(f"{n_experts} experts do not split over {world} ranks.")
+    per = n_experts // world
+    return rank * per, per
+
+
+def token_range(batch: int, rank: int, world: int) -> tuple[int, int]:
+    """(first row, rows) of the batch held by ``rank``."""
+    if batch % world:
+        raise ValueError(f"batch {batch} does not split over {world} ranks.")
+    per = batch // world
+    return rank * per, per
+
+
+def shard_expert_weights(weights: dict, config: dict, rank: int, world: int) -> dict:
+    """Keep only this rank's experts of every layer (packed-ternary-v1 names)."""
+    e0, n = expert_range(int(config["num_experts"]), rank, world)
+    out = {}
+    for k, v in weights.items():
+        if ".mlp.switch_mlp." in k and any(f".{e}." in k for e in _EXPERT_KEYS):
+            out[k] = v[e0:e0 + n].contiguous()
+        else:
+            out[k] = v
+    return out
+
+
+class EPExchange:
+    """The collectives of one expert-parallel MoE layer.  Layout only (no
+    compute), so the same code runs over NCCL on GPUs and over gloo in the
+    CPU tests."""
+
+    def __init__(self, group, rank: int, world: int, n_experts: int):
+        self.group = group
+        self.rank = rank
+        self.world = world
+        self.n_experts = n_experts
+        self.e_first, self.n_local = expert_range(n_experts, rank, world)
+
+    def dispatch(self, hidden: torch.Tensor, idx: torch.Tensor):
+        """All-gather ``hidden [T, H]`` and ``idx [T, k]`` (int32) from every
+        rank as one packed byte buffer; returns ``x_all [W*T, H]`` (rows in
+        rank order, a strided view) and ``ids_all [W*T, k]``."""
+        T, H = hidden.shape
+        k = idx.shape[1]
+        hb = H * hidden.element_size()
+        send = torch.empty(T, hb + 4 * k, dtype=torch.uint8, device=hidden.device)
+        send[:, :hb].copy_(hidden.contiguous().view(torch.uint8).reshape(T, hb))
+        send[:, hb:].copy_(idx.to(torch.int32).contiguous().view(torch.uint8).reshape(T, 4 * k))
+        recv = torch.empty(self.world * T, hb + 4 * k, dtype=torch.uint8, device=hidden.device)
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+        x_all = recv[:, :hb].view(hidden.dtype)
+        ids_all = recv[:, hb:].contiguous().view(torch.int32)
+        return x_all, ids_all
+
+    def combine_exchange(self, y_all: torch.Tensor) -> torch.Tensor:
+        """``y_all [W*T*k, N]`` (rows by slot of the gathered tokens) ->
+        ``[W, T*k, N]``: from every rank, its rows for this rank's slots."""
+        rows, n = y_all.shape
+        recv = torch.empty_like(y_all)
+        dist.all_to_all_single(recv, y_all.contiguous(), group=self.group)
+        return recv.view(self.world, rows // self.world, n)
+
+    def gather_rows(self, x: torch.Tensor) -> torch.Tensor:
+        out = torch.empty(self.world * x.shape[0], *x.shape[1:], dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
+        return out
+
+
+class EPMoeBlock:
+    """Drop-in for ``MapleSparseMoeBlock`` holding this rank's experts only."""
+
+    def __init__(self, block, exchange: EPExchange):
+        self.block = block
+        self.ex = exchange
+
+    def __call__(self, hidden_states, residual=None):
+        b = self.block
+        idx, wt = router_topk(hidden_states, b.gate_weight, b.top_k)
+        x_all, ids_all = self.ex.dispatch(hidden_states, idx)
+        plan = moe_plan(ids_all, self.ex.n_experts, e_first=self.ex.e_first, n_local=self.ex.n_local)
+        h = ternary_expert_swiglu(x_all, b.up_gate.packed_weight, b.up_gate.row_alpha, ids_all, plan=plan)
+        y = ternary_expert_gemv(h, b.down.packed_weight, b.down.row_alpha, ids_all, plan=plan)
+        recv = self.ex.combine_exchange(y.reshape(-1, y.shape[-1]))
+        return ep_combine(recv, idx, wt, self.ex.n_experts, residual)
+
+
+class EPHead:
+    """Vocabulary-sharded RTN-4 lm_head with the greedy pick: rank r scores
+    rows [r*V/W, (r+1)*V/W) for every gathered token, and the candidates'
+    (value, index) pairs meet in an all-gather."""
+
+    def __init__(self, lm_head, exchange: EPExchange):
+        V = lm_head.packed_weight.shape[0]
+        w = exchange.world
+        if V % w:
+            raise ValueError(f"vocab {V} does not split over {w} ranks.")
+        self.shard = V // w
+        r0 = exchange.rank * self.shard
+        self.codes = lm_head.packed_weight[r0:r0 + self.shard].contiguous()
+        self.scales = lm_head.scales[r0:r0 + self.shard].contiguous()
+        self.biases = None if lm_head.biases is None else lm_head.biases[r0:r0 + self.shard].contiguous()
+        self.group_size = lm_head.group_size
+        self.ex = exchange
+
+    def next_ids(self, normed: torch.Tensor) -> torch.Tensor:
+        T = normed.shape[0]
+        h_all = self.ex.gather_rows(normed)
+        logits = rtn4_gemv(h_all, self.codes, self.scales, self.biases, group_size=self.group_size)
+        li = argmax(logits)
+        lv = logits.gather(1, li.reshape(-1, 1)).float()
+        cand = torch.cat([lv.view(torch.int32), li.to(torch.int32).reshape(-1, 1)], 1)  # [W*T, 2] int32
+        allc = self.ex.gather_rows(cand).view(self.ex.world, -1, 2)  # [W, W*T, 2]
+        vals = allc[:, :, 0].contiguous().view(torch.float32).t().contiguous()  # [W*T, W]
+        r = argmax(vals)  # ties and NaN: lowest rank = lowest vocabulary index
+        rows = torch.arange(vals.shape[0], device=normed.device)
+        ids = allc[r, rows, 1].long() + r * self.shard
+        return ids[self.ex.rank * T:(self.ex.rank + 1) * T]
+
+
+class EPDecoder:
+    """One greedy decode step of this rank's rows: embedding, the layers
+    (data-parallel attention, expert-parallel MoE), final norm, sharded head."""
+
+    def __init__(self, model, exchange: EPExchange):
+        self.model = model
+        self.ex = exchange
+        for layer in model.layers:
+            if not isinstance(layer.mlp, EPMoeBlock):
+                layer.mlp = EPMoeBlock(layer.mlp, exchange)
+        self.head = EPHead(model.lm_head, exchange)
+
+    def step(self, tokens: torch.Tensor, cache) -> torch.Tensor:
+        m = self.model
+        rows = tokens.shape[0]
+        seqlen = cache.seqlen[:rows]
+        row_map = cache.row_map[:rows] if cache.remap else None
+        m.rotary.ensure_length(cache.max_len)
+        hidden = m.embed(tokens.reshape(rows))
+        for layer in m.layers:
+            hidden = layer(hidden, seqlen, row_map, m.rotary, cache, kv_final=True)
+        cache.advance(1, rows)
+        return self.head.next_ids(m.norm(hidden))
+
+
+class EPDecodeGraph:
+    """``EPDecoder.step`` captured in a CUDA graph (collectives included)."""
+
+    def __init__(self, decoder: EPDecoder, cache, rows: int, warmup: int = 3):
+        dev = decoder.model.device
+        self.token_ids = torch.zeros(rows, 1, dtype=torch.long, device=dev)
+        snap = (cache.seqlen.clone(), list(cache.seen))
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            for _ in range(warmup):
+                decoder.step(self.token_ids, cache)
+                cache.seqlen.copy_(snap[0])
+                cache.seen = list(snap[1])
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=st):
+                self.next_id = decoder.step(self.token_ids, cache)
+        torch.cuda.current_stream(dev).wait_stream(st)
+        torch.cuda.synchronize(dev)
+        cache.seqlen.copy_(snap[0])
+        cache.seen = list(snap[1])
+
+    def replay(self, tokens: torch.Tensor | None = None) -> torch.Tensor:
+        if tokens is not None:
+            self.token_ids.copy_(tokens.reshape(-1, 1))
+        self.graph.replay()
+        return self.next_id

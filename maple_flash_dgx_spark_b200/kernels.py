@@ -149,23 +149,50 @@ class MoePlan:
         self.n_slots = n_slots
 
 
-def moe_plan(expert_ids: torch.Tensor, n_experts: int) -> MoePlan:
+def moe_plan(expert_ids: torch.Tensor, n_experts: int, *, e_first: int = 0, n_local: int | None = None) -> MoePlan:
+    """Sort the routed slots by expert.  With ``e_first`` / ``n_local`` only the
+    experts ``[e_first, e_first + n_local)`` (one rank's share under expert
+    parallelism) are listed, indexed locally."""
     op = "moe_plan"
     require_cuda(op, expert_ids)
     ids = expert_ids.reshape(-1).to(torch.int32).contiguous()
     n = ids.numel()
-    offsets = torch.empty(n_experts + 1, dtype=torch.int32, device=ids.device)
+    n_local = n_experts if n_local is None else int(n_local)
+    offsets = torch.empty(n_local + 1, dtype=torch.int32, device=ids.device)
     slots = torch.empty(max(n, 1), dtype=torch.int32, device=ids.device)
-    check(lib().maple_moe_plan(ptr(ids), n, n_experts, ptr(offsets), ptr(slots), stream_ptr(ids.device)), op)
-    return MoePlan(offsets, slots, n_experts, n)
+    check(lib().maple_moe_plan_range(ptr(ids), n, n_experts, int(e_first), n_local, ptr(offsets), ptr(slots),
+                                     stream_ptr(ids.device)), op)
+    return MoePlan(offsets, slots, n_local, n)
 
 
-def _grouped(op, x_rows, per, w, alpha, plan, swiglu, out_rows, n_out, dtype):
+def ep_combine(recv: torch.Tensor, expert_ids: torch.Tensor, topk_weight: torch.Tensor, n_experts: int,
+               residual: torch.Tensor | None = None) -> torch.Tensor:
+    """Expert-parallel weighted top-k sum: ``recv [world, tokens*topk, N]`` holds
+    every rank's expert rows for this rank's tokens; the row of the rank that
+    owns each slot's expert enters ``moe_reduce_add``'s sum.  Returns
+    ``[tokens, N]``."""
+    op = "ep_combine"
+    require_cuda(op, recv, expert_ids, topk_weight, residual)
+    world, rows, n = recv.shape
+    tokens, topk = expert_ids.shape
+    if rows != tokens * topk:
+        raise ValueError(f"recv rows {rows} != tokens*topk {tokens * topk}.")
+    r = recv.contiguous()
+    ids = expert_ids.to(torch.int32).contiguous()
+    w = topk_weight.float().contiguous()
+    res = residual.reshape(tokens, n).contiguous() if residual is not None else None
+    y = torch.empty(tokens, n, device=recv.device, dtype=recv.dtype)
+    check(lib().maple_ep_combine(ptr(r), dtype_code(r, op), world, tokens, topk, n, ptr(ids), ptr(w), n_experts,
+                                 ptr(res), ptr(y), stream_ptr(recv.device)), op)
+    return y
+
+
+def _grouped(op, x_rows, per, w, alpha, plan, swiglu, out_rows, n_out, dtype, out=None):
     """Grouped expert GEMM: input row of slot s is ``s // per``."""
     E, rows, nwords = w.shape
     k_in = nwords * _CODES_PER_WORD
     frag, meta = fxa_encode(x_rows)
-    y = torch.empty(out_rows, n_out, device=x_rows.device, dtype=dtype)
+    y = out if out is not None else torch.empty(out_rows, n_out, device=x_rows.device, dtype=dtype)
     check(lib().maple_ternary_grouped_gemm(
         ptr(frag), ptr(meta), x_rows.shape[0], k_in, ptr(w), E, rows, ptr(alpha), dtype_code(alpha, op),
         ptr(plan.offsets), ptr(plan.slots), plan.n_slots, per, int(swiglu), 1, ptr(y), dtype_code(y, op), n_out,

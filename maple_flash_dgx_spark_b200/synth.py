@@ -124,13 +124,17 @@ def synthetic_tokens(seed: int, n: int, vocab: int, device, stream: int = S_PROM
     return t
 
 
-def fill_kv_cache(cache, seed: int, length: int) -> None:
+def fill_kv_cache(cache, seed: int, length: int, row0: int = 0, total_rows: int | None = None) -> None:
     """Fill positions [0, length) of every layer's K/V with bf16 N(0, 1) (the
-    configs' random cached context) and set every row's length to ``length``."""
+    configs' random cached context) and set every row's length to ``length``.
+    ``row0`` / ``total_rows``: the cache holds rows [row0, row0 + batch) of a
+    ``total_rows``-row batch (a data-parallel rank), with those rows' values."""
     for i in range(len(cache.k)):
         for kind, t in ((L_KCACHE, cache.k[i]), (L_VCACHE, cache.v[i])):
             B, Hkv, T, D = t.shape
-            tmp = _normal(seed, layer_stream(i, kind), (B, Hkv, length, D), t.device, 1.0)
-            t[:, :, :length].copy_(tmp)
+            n = B if total_rows is None else int(total_rows)
+            tmp = _normal(seed, layer_stream(i, kind), (n, Hkv, length, D), t.device, 1.0)
+            t[:, :, :length].copy_(tmp[row0:row0 + B])
+            del tmp
     cache.seqlen.fill_(length)
     cache.seen = [length] * cache.batch
