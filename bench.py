@@ -372,11 +372,15 @@ def run_bs64(args):
     with torch.inference_mode():
         if world > 1:
             dec = EPDecoder(model, EPExchange(None, rank, world, cfg["num_experts"]))
+            holder = {}  # the only reference to the captured graph (freed before the group is destroyed)
             try:
-                g = EPDecodeGraph(dec, cache, T)
-                step = g.replay
-                nxt_of = lambda: g.next_id  # noqa: E731
-                ids_buf = g.token_ids
+                holder["g"] = EPDecodeGraph(dec, cache, T)
+                ids_buf = holder["g"].token_ids
+
+                def step(tok=None):
+                    return holder["g"].replay()
+
+                nxt_of = lambda: holder["g"].next_id  # noqa: E731
             except Exception as exc:  # NCCL capture unsupported: eager steps (same collectives)
                 graph_kind = f"eager ({type(exc).__name__})"
                 ids_buf = torch.zeros(T, 1, dtype=torch.long, device=dev)
@@ -487,8 +491,13 @@ def run_bs64(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        if graph_kind == "cuda graph":
-            del g
+        # a CUDA graph holding NCCL calls must be released before the group goes
+        import gc
+
+        holder.clear()
+        del step, nxt_of
+        gc.collect()
+        torch.cuda.synchronize(dev)
         dist.barrier()
         dist.destroy_process_group()
 

@@ -138,8 +138,11 @@ __host__ __device__ constexpr size_t tgemm_red_bytes() {
   return (size_t)(WK > 1 ? WK - 1 : 1) * WM * (RC / 2) * 32 * 4 * sizeof(int);
 }
 
-template <int AT, int OT, int MODE, int WM, int WK, int NI, int RC>
-__global__ void __launch_bounds__(32 * WM * WK) tgemm_kernel(TGemmParams p) {
+// NBUF = 2 double-buffers the digit chunks (many rows per CTA); NBUF = 1
+// halves the shared memory for decode-sized groups (one chunk per expert),
+// so two CTAs share an SM.
+template <int AT, int OT, int MODE, int WM, int WK, int NI, int RC, int NBUF>
+__global__ void __launch_bounds__(32 * WM * WK, NBUF == 1 ? 2 : 1) tgemm_kernel(TGemmParams p) {
   constexpr int NT = 32 * WM * WK, NP = RC / 2;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ uint64_t bar[2];
@@ -152,8 +155,8 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemm_kernel(TGemmParams p) {
   const int rowu2 = iters * 128;
   const size_t buf_bytes = (size_t)RC * rowu2 * sizeof(uint2);
   uint2* buf0 = reinterpret_cast<uint2*>(smem);
-  int* meta_s = reinterpret_cast<int*>(smem + 2 * buf_bytes);                       // [2][RC][8]
-  int* red = reinterpret_cast<int*>(smem + 2 * buf_bytes + 2 * RC * kMetaInts * 4);  // [WK-1][WM][NP][32][4]
+  int* meta_s = reinterpret_cast<int*>(smem + NBUF * buf_bytes);                          // [NBUF][RC][8]
+  int* red = reinterpret_cast<int*>(smem + NBUF * buf_bytes + NBUF * RC * kMetaInts * 4);  // [WK-1][WM][NP][32][4]
 
   const bool grouped = p.offsets != nullptr;
   const int e = grouped ? blockIdx.y : 0;
@@ -222,7 +225,7 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemm_kernel(TGemmParams p) {
   __syncthreads();
   // Stage chunk c into buffer c & 1 (thread 0).
   auto issue = [&](int c) {
-    const int b = c & 1;
+    const int b = c % NBUF;
     const int n = min(RC, count - c * RC);
     unsigned bytes = 0;
     for (int i = 0; i < n; ++i) {
@@ -242,17 +245,23 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemm_kernel(TGemmParams p) {
   if (tid == 0) issue(0);
 
   for (int c = 0; c < nchunks; ++c) {
-    const int b = c & 1;
-    if (tid == 0 && c + 1 < nchunks) {
-      fence_proxy_async_smem();
-      issue(c + 1);
+    const int b = c % NBUF;
+    const unsigned par = (unsigned)(c / NBUF) & 1u;
+    if (tid == 0) {
+      if (NBUF == 2 && c + 1 < nchunks) {
+        fence_proxy_async_smem();
+        issue(c + 1);
+      } else if (NBUF == 1 && c > 0) {
+        fence_proxy_async_smem();
+        issue(c);
+      }
     }
-    const bool ready = mbar_wait_bounded(&bar[b], (c >> 1) & 1);
+    const bool ready = mbar_wait_bounded(&bar[b], par);
     if (__syncthreads_or(!ready)) {
       if (tid == 0) atomicOr(p.err, kErrFlagTimeout);
       // let copies still in flight land before the block exits
-      mbar_wait_bounded(&bar[b], (c >> 1) & 1);
-      if (c + 1 < nchunks) mbar_wait_bounded(&bar[b ^ 1], ((c + 1) >> 1) & 1);
+      mbar_wait_bounded(&bar[b], par);
+      if (NBUF == 2 && c + 1 < nchunks) mbar_wait_bounded(&bar[b ^ 1], (unsigned)((c + 1) / NBUF) & 1u);
       return;
     }
     const uint2* fr = buf0 + (size_t)b * RC * rowu2;
@@ -349,11 +358,11 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemm_kernel(TGemmParams p) {
   }
 }
 
-template <int AT, int OT, int MODE, int WM, int WK, int NI, int RC>
+template <int AT, int OT, int MODE, int WM, int WK, int NI, int RC, int NBUF>
 cudaError_t launch_tgemm(const TGemmParams& p, dim3 grid, cudaStream_t st) {
-  const size_t smem = 2 * (size_t)RC * p.iters * 128 * sizeof(uint2) + 2 * RC * kMetaInts * 4 +
+  const size_t smem = NBUF * (size_t)RC * p.iters * 128 * sizeof(uint2) + NBUF * RC * kMetaInts * 4 +
                       tgemm_red_bytes<WM, WK, RC>();
-  auto kern = tgemm_kernel<AT, OT, MODE, WM, WK, NI, RC>;
+  auto kern = tgemm_kernel<AT, OT, MODE, WM, WK, NI, RC, NBUF>;
   if (smem > 32 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -366,22 +375,29 @@ cudaError_t launch_tgemm(const TGemmParams& p, dim3 grid, cudaStream_t st) {
 inline int tgemm_wm(int iters) { return iters <= 8 ? 4 : 2; }
 inline int tile_rows(int mode, int iters) { return (mode == kGSwiglu ? 8 : 16) * tgemm_wm(iters); }
 
-template <int AT, int OT, int MODE>
-cudaError_t dispatch_tgemm(const TGemmParams& p, dim3 grid, cudaStream_t st) {
-  if (p.iters <= 4) return launch_tgemm<AT, OT, MODE, 4, 2, 2, 16>(p, grid, st);   // K <= 1024
-  if (p.iters <= 8) return launch_tgemm<AT, OT, MODE, 4, 2, 4, 8>(p, grid, st);    // K <= 2048
-  if (p.iters <= 16) return launch_tgemm<AT, OT, MODE, 2, 4, 4, 4>(p, grid, st);   // K <= 4096
+template <int AT, int OT, int MODE, int NBUF>
+cudaError_t dispatch_tgemm_buf(const TGemmParams& p, dim3 grid, cudaStream_t st) {
+  if (p.iters <= 4) return launch_tgemm<AT, OT, MODE, 4, 2, 2, 16, NBUF>(p, grid, st);   // K <= 1024
+  if (p.iters <= 8) return launch_tgemm<AT, OT, MODE, 4, 2, 4, 8, NBUF>(p, grid, st);    // K <= 2048
+  if (p.iters <= 16) return launch_tgemm<AT, OT, MODE, 2, 4, 4, 4, NBUF>(p, grid, st);   // K <= 4096
   return cudaErrorInvalidValue;
 }
 
+// One buffer when a CTA sees at most about one chunk of rows.
+template <int AT, int OT, int MODE>
+cudaError_t dispatch_tgemm(const TGemmParams& p, dim3 grid, cudaStream_t st, bool single_chunk) {
+  return single_chunk ? dispatch_tgemm_buf<AT, OT, MODE, 1>(p, grid, st) : dispatch_tgemm_buf<AT, OT, MODE, 2>(p, grid, st);
+}
+
 template <int MODE>
-cudaError_t dispatch_tgemm_types(const TGemmParams& p, int a_dtype, int y_dtype, dim3 grid, cudaStream_t st) {
+cudaError_t dispatch_tgemm_types(const TGemmParams& p, int a_dtype, int y_dtype, dim3 grid, cudaStream_t st,
+                                 bool single_chunk) {
   if (a_dtype == kBF16) {
-    return y_dtype == kBF16 ? dispatch_tgemm<kBF16, kBF16, MODE>(p, grid, st)
-                            : dispatch_tgemm<kBF16, kF32, MODE>(p, grid, st);
+    return y_dtype == kBF16 ? dispatch_tgemm<kBF16, kBF16, MODE>(p, grid, st, single_chunk)
+                            : dispatch_tgemm<kBF16, kF32, MODE>(p, grid, st, single_chunk);
   }
-  return y_dtype == kBF16 ? dispatch_tgemm<kF32, kBF16, MODE>(p, grid, st)
-                          : dispatch_tgemm<kF32, kF32, MODE>(p, grid, st);
+  return y_dtype == kBF16 ? dispatch_tgemm<kF32, kBF16, MODE>(p, grid, st, single_chunk)
+                          : dispatch_tgemm<kF32, kF32, MODE>(p, grid, st, single_chunk);
 }
 
 }  // namespace mb
@@ -458,7 +474,7 @@ extern "C" int maple_ternary_gemm(const void* frag, const void* meta, int64_t ro
   const int gy = (chunks + p.chunks_per_cta - 1) / p.chunks_per_cta;
   if (gy > 65535) return kErrShape;
   cudaError_t e = dispatch_tgemm_types<kGPlain>(p, alpha_dtype, y_dtype, dim3((unsigned)tiles, (unsigned)gy),
-                                               static_cast<cudaStream_t>(stream));
+                                                static_cast<cudaStream_t>(stream), p.chunks_per_cta <= 1);
   return e == cudaSuccess ? kOk : kErrCuda;
 }
 
@@ -511,7 +527,10 @@ extern "C" int maple_ternary_grouped_gemm(const void* frag, const void* meta, in
   const int per = tile_rows(swiglu ? kGSwiglu : kGPlain, p.iters);
   dim3 grid((unsigned)((p.n_out + per - 1) / per), (unsigned)n_experts);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = swiglu ? dispatch_tgemm_types<kGSwiglu>(p, alpha_dtype, y_dtype, grid, st)
-                         : dispatch_tgemm_types<kGPlain>(p, alpha_dtype, y_dtype, grid, st);
+  // decode-sized routing (about one chunk of slots per expert): one buffer, two CTAs per SM
+  const int rc = p.iters <= 4 ? 16 : p.iters <= 8 ? 8 : 4;
+  const bool single = n_slots <= (int64_t)rc * n_experts;
+  cudaError_t e = swiglu ? dispatch_tgemm_types<kGSwiglu>(p, alpha_dtype, y_dtype, grid, st, single)
+                         : dispatch_tgemm_types<kGPlain>(p, alpha_dtype, y_dtype, grid, st, single);
   return e == cudaSuccess ? kOk : kErrCuda;
 }
