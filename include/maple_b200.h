@@ -235,6 +235,15 @@ int maple_rtn4_gemv(const void* x, int x_dtype, int64_t batch, int64_t k, int64_
 
 /* RTN-4 GEMV over rows head[cluster_ids[r / C], r % C] (FlashHead probes).
  * Replaces kernels/rtn4.py:514 rtn4_indexed_gemv. */
+/* Batched RTN-4 head for batch >= 2 (k <= 4096): same results as
+ * maple_rtn4_gemv row by row, with the head streamed once per chunk of up to
+ * 16 rows.  scratch: maple_rtn4_frag_bytes(batch, k) bytes, 16-byte aligned,
+ * for the encoded rows.  A bounded wait that gives up sets bit 1 of *err. */
+int64_t maple_rtn4_frag_bytes(int64_t rows, int64_t k);
+int maple_rtn4_gemm(const void* x, int x_dtype, int64_t batch, int64_t k, int64_t x_row_stride, const uint32_t* codes,
+                    int64_t n, const void* scales, const void* biases, int s_dtype, int64_t group_size, void* y,
+                    int64_t y_row_stride, void* scratch, int64_t scratch_bytes, int* err, void* stream);
+
 int maple_rtn4_indexed_gemv(const void* x, int x_dtype, int64_t batch, int64_t k, int64_t x_row_stride,
                             const uint32_t* codes, int64_t n_clusters, int64_t cluster_size,
                             const void* scales, const void* biases, int s_dtype, int64_t group_size,

@@ -13,6 +13,7 @@
 //   tensor pipe), X_g = sum_{k in g} X_k (exact), accumulated in double in
 //   group order as acc = (acc + s_g*C_g) + b_g*X_g, rounded once to fp32.
 // Symmetric heads (biases == NULL) use b_g = -8 * s_g.
+#include "bulk.cuh"
 #include "fxa.cuh"
 #include "launch.cuh"
 
@@ -447,6 +448,197 @@ __global__ void embed_rtn4_kernel(const int64_t* ids, const uint32_t* codes, con
 using namespace mb;
 
 namespace {
+// ---------------------------------------------------- batched RTN-4 head --
+// For B > 1 rows the head is streamed once per chunk of up to 2*NP rows
+// instead of once per row: rtn4_encode_kernel FXA-encodes each row once (4-bit
+// fragment layout, compact: entry (i*16 + l) for lane l < 16 of fragment
+// i = it*4 + m) with its per-group sums X_g, and rtn4_gemm_kernel stages a
+// chunk's digits in shared memory while a persistent grid of 8-warp CTAs
+// streams 16-row tiles of the head, one MMA serving two rows (B columns 0-3
+// row a, 4-7 row b).  The per-group double accumulation is the batch-1
+// kernel's, so each row's logits are bit-identical to it.
+constexpr int kXgStride = 64;  // group sums per row (K / G <= 64)
+
+template <int XT>
+__global__ void __launch_bounds__(256) rtn4_encode_kernel(const void* x, int64_t x_stride, int K, int G, uint2* frag,
+                                                          int* meta, long long* xg) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ FxaBlock fb;
+  __shared__ long long s_xg[kXgStride];
+  const int iters = K / 128;
+  uint2* fr = reinterpret_cast<uint2*>(smem);
+  float* xsm = reinterpret_cast<float*>(smem + (size_t)iters * 128 * sizeof(uint2));
+  const int64_t r = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  const void* xr = static_cast<const char*>(x) + r * x_stride * (XT == kBF16 ? 2 : 4);
+  fxa_prologue<XT, kF32, false, 4, 256>(xr, nullptr, K, 0.0f, 0, iters, xsm, nullptr, fr, fb, s_xg, G);
+  uint4* o = reinterpret_cast<uint4*>(frag + r * iters * 64);
+  const uint4* f4 = reinterpret_cast<const uint4*>(fr);
+  for (int c = threadIdx.x; c < iters * 32; c += 256) o[c] = f4[(c >> 3) * 16 + (c & 7)];
+  for (int g = threadIdx.x; g < kXgStride; g += 256) xg[r * kXgStride + g] = g < K / G ? s_xg[g] : 0;
+  if (threadIdx.x < 8) meta[r * 8 + threadIdx.x] = threadIdx.x == 0 ? fb.s : 0;
+}
+
+struct Rtn4GemmParams {
+  const uint32_t* codes;   // [n_out, K/8]
+  const void* scales;      // [n_out, K/G]
+  const void* biases;      // [n_out, K/G] or nullptr (symmetric)
+  const uint2* frag;       // [B, iters*64]
+  const int* meta;         // [B, 8]
+  const long long* xg;     // [B, 64]
+  void* y;                 // [B, n_out]
+  int* err;
+  int64_t y_stride;
+  int n_out, K, nwords, G, iters, B;
+};
+
+template <int XT, int ST, int NP>
+__global__ void __launch_bounds__(256, 1) rtn4_gemm_kernel(Rtn4GemmParams p) {
+  constexpr int CH = 2 * NP;  // rows per chunk
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ uint64_t bar;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int c0 = blockIdx.y * CH;
+  const int nt = min(CH, p.B - c0);
+  const int rowu2 = p.iters * 64;
+  uint2* dig = reinterpret_cast<uint2*>(smem);
+  long long* sxg = reinterpret_cast<long long*>(smem + (size_t)CH * rowu2 * sizeof(uint2));
+  int* smeta = reinterpret_cast<int*>(sxg + CH * kXgStride);
+  pdl_wait();
+  pdl_trigger();
+  if (tid == 0) mbar_init(&bar, 1);
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned b_dig = (unsigned)(nt * rowu2 * sizeof(uint2)), b_xg = (unsigned)(nt * kXgStride * 8),
+                   b_meta = (unsigned)(nt * 32);
+    mbar_expect_tx(&bar, b_dig + b_xg + b_meta);
+    bulk_g2s(dig, p.frag + (int64_t)c0 * rowu2, b_dig, &bar);
+    bulk_g2s(sxg, p.xg + (int64_t)c0 * kXgStride, b_xg, &bar);
+    bulk_g2s(smeta, p.meta + (int64_t)c0 * 8, b_meta, &bar);
+  }
+  const bool ready = mbar_wait_bounded(&bar, 0);
+  if (__syncthreads_or(!ready)) {
+    if (tid == 0) atomicOr(p.err, kErrFlagTimeout);
+    mbar_wait_bounded(&bar, 0);
+    return;
+  }
+  const int ngroups = p.K / p.G;
+  const bool split_iter = p.G == 64;
+  const int ipg = p.G >= 128 ? p.G / 128 : 1;
+  const int es_s = ST == kBF16 ? 2 : 4;
+  const int ntiles = (p.n_out + 15) / 16;
+  const int half = lane >> 4, l16 = lane & 15;
+  const int my_tok = t >> 1;  // lanes t<2: row a of a pair, t>=2: row b
+  const float nanv = __int_as_float(0x7fc00000);
+
+  for (int tile = blockIdx.x * 8 + warp; tile < ntiles; tile += gridDim.x * 8) {
+    const int rg = tile * 16 + g, rh = rg + 8;
+    const bool ok_g = rg < p.n_out, ok_h = rh < p.n_out;
+    const uint32_t* cgp = p.codes + (int64_t)(ok_g ? rg : 0) * p.nwords;
+    const uint32_t* chp = p.codes + (int64_t)(ok_h ? rh : 0) * p.nwords;
+    const char* sg_row = static_cast<const char*>(p.scales) + (int64_t)(ok_g ? rg : 0) * ngroups * es_s;
+    const char* sh_row = static_cast<const char*>(p.scales) + (int64_t)(ok_h ? rh : 0) * ngroups * es_s;
+    const char* bg_row = p.biases ? static_cast<const char*>(p.biases) + (int64_t)(ok_g ? rg : 0) * ngroups * es_s
+                                  : nullptr;
+    const char* bh_row = p.biases ? static_cast<const char*>(p.biases) + (int64_t)(ok_h ? rh : 0) * ngroups * es_s
+                                  : nullptr;
+    double accd[NP][2];
+    int acc[NP][4], acc2[NP][4];
+#pragma unroll
+    for (int q = 0; q < NP; ++q) {
+      accd[q][0] = accd[q][1] = 0.0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[q][j] = acc2[q][j] = 0;
+    }
+    auto load_w = [&](int it, uint4& ra, uint4& rb) {
+      ra = make_uint4(0, 0, 0, 0);
+      rb = make_uint4(0, 0, 0, 0);
+      if (it < p.iters) {
+        const int word = it * 16 + 4 * t;
+        if (ok_g) ra = ld_stream_u4(cgp + word);
+        if (ok_h) rb = ld_stream_u4(chp + word);
+      }
+    };
+    auto finish = [&](int (&c)[NP][4], int gi) {
+      float sg = 0.f, sh = 0.f, bg = 0.f, bh = 0.f;
+      if ((t & 1) == 0) {
+        sg = ok_g ? load_f<ST>(sg_row, gi) : 0.f;
+        sh = ok_h ? load_f<ST>(sh_row, gi) : 0.f;
+        bg = bg_row ? (ok_g ? load_f<ST>(bg_row, gi) : 0.f) : __fmul_rn(-8.0f, sg);
+        bh = bh_row ? (ok_h ? load_f<ST>(bh_row, gi) : 0.f) : __fmul_rn(-8.0f, sh);
+      }
+#pragma unroll
+      for (int q = 0; q < NP; ++q) {
+        const long long pg = (long long)c[q][0] + 128LL * c[q][1];
+        const long long ph = (long long)c[q][2] + 128LL * c[q][3];
+        const long long ug = __shfl_down_sync(0xffffffffu, pg, 1);
+        const long long uh = __shfl_down_sync(0xffffffffu, ph, 1);
+        if ((t & 1) == 0) {
+          const long long Cg = pg + 16384LL * ug, Ch = ph + 16384LL * uh;
+          const double xgv = (double)sxg[(2 * q + my_tok) * kXgStride + gi];
+          accd[q][0] = __dadd_rn(__dadd_rn(accd[q][0], __dmul_rn((double)sg, (double)Cg)), __dmul_rn((double)bg, xgv));
+          accd[q][1] = __dadd_rn(__dadd_rn(accd[q][1], __dmul_rn((double)sh, (double)Ch)), __dmul_rn((double)bh, xgv));
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) c[q][j] = 0;
+      }
+    };
+    uint4 wa[4], wb[4];
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) load_w(ii, wa[ii], wb[ii]);
+    for (int it0 = 0; it0 < p.iters; it0 += 4) {
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) {
+        const int it = it0 + ii;
+        if (it < p.iters) {
+          const uint32_t ga[4] = {wa[ii].x, wa[ii].y, wa[ii].z, wa[ii].w};
+          const uint32_t gb[4] = {wb[ii].x, wb[ii].y, wb[ii].z, wb[ii].w};
+          load_w(it + 4, wa[ii], wb[ii]);
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const uint32_t a0 = ga[m] & 0x0f0f0f0fu, a2 = (ga[m] >> 4) & 0x0f0f0f0fu;
+            const uint32_t a1 = gb[m] & 0x0f0f0f0fu, a3 = (gb[m] >> 4) & 0x0f0f0f0fu;
+            const int ent = (it * 4 + m) * 16 + l16;
+#pragma unroll
+            for (int q = 0; q < NP; ++q) {
+              const uint2 bv = dig[(size_t)(2 * q + half) * rowu2 + ent];
+              if (split_iter) {
+                const uint2 lo = t < 2 ? bv : make_uint2(0u, 0u);
+                const uint2 hi = t < 2 ? make_uint2(0u, 0u) : bv;
+                mma_u8s8(acc[q], a0, a1, a2, a3, lo.x, lo.y);
+                mma_u8s8(acc2[q], a0, a1, a2, a3, hi.x, hi.y);
+              } else {
+                mma_u8s8(acc[q], a0, a1, a2, a3, bv.x, bv.y);
+              }
+            }
+          }
+          if (split_iter) {
+            finish(acc, 2 * it);
+            finish(acc2, 2 * it + 1);
+          } else if ((it + 1) % ipg == 0) {
+            finish(acc, it / ipg);
+          }
+        }
+      }
+    }
+    if ((t & 1) == 0) {
+#pragma unroll
+      for (int q = 0; q < NP; ++q) {
+        const int tok = 2 * q + my_tok;
+        if (tok < nt) {
+          const int s = smeta[tok * 8];
+          const bool bad = s == kFxaNonFinite;
+          char* yr = static_cast<char*>(p.y) + (int64_t)(c0 + tok) * p.y_stride * (XT == kBF16 ? 2 : 4);
+          if (ok_g) store_f<XT>(yr, rg, bad ? nanv : __double2float_rn(accd[q][0] * pow2d(-s)));
+          if (ok_h) store_f<XT>(yr, rh, bad ? nanv : __double2float_rn(accd[q][1] * pow2d(-s)));
+        }
+      }
+    }
+  }
+}
+
 int rtn4_launch(Rtn4Params& p, int x_dtype, int s_dtype, int64_t batch, void* stream) {
   const size_t smem = (size_t)p.iters * 128 * sizeof(uint2) + (size_t)p.K * sizeof(float);
   const int nblk = (p.n_out + 63) / 64;
@@ -507,6 +699,71 @@ extern "C" int maple_rtn4_indexed_gemv(const void* x, int x_dtype, int64_t batch
   p.n_out = (int)(n_probes * cluster_size); p.K = (int)k; p.nwords = (int)(k / 8); p.G = (int)group_size;
   p.iters = (int)(k / 128); p.cluster_size = (int)cluster_size; p.n_clusters = (int)n_clusters;
   return rtn4_launch(p, x_dtype, s_dtype, batch, stream);
+}
+
+extern "C" int64_t maple_rtn4_frag_bytes(int64_t rows, int64_t k) {
+  if (rows < 0 || k <= 0) return -1;
+  return rows * (k / 128) * 64 * 8 + rows * (32 + kXgStride * 8);
+}
+
+// Batched head: scratch (maple_rtn4_frag_bytes) holds the encoded rows, their
+// metadata and group sums.
+extern "C" int maple_rtn4_gemm(const void* x, int x_dtype, int64_t batch, int64_t k, int64_t x_row_stride,
+                               const uint32_t* codes, int64_t n, const void* scales, const void* biases, int s_dtype,
+                               int64_t group_size, void* y, int64_t y_row_stride, void* scratch,
+                               int64_t scratch_bytes, int* err, void* stream) {
+  if (batch < 0 || n < 0) return kErrShape;
+  if (batch == 0 || n == 0) return kOk;
+  if (int rc = rtn4_checks(x_dtype, s_dtype, k, group_size)) return rc;
+  if (k > 4096) return kErrShape;
+  if (!x || !codes || !scales || !y || !err || !scratch) return kErrShape;
+  if ((reinterpret_cast<uintptr_t>(codes) | reinterpret_cast<uintptr_t>(scratch)) & 15) return kErrAlign;
+  if (((reinterpret_cast<uintptr_t>(x) & 15) != 0) || ((x_row_stride * (x_dtype == kBF16 ? 2 : 4)) & 15))
+    return kErrAlign;
+  if (scratch_bytes < maple_rtn4_frag_bytes(batch, k)) return kErrWorkspace;
+  if (batch > 65535 * 16 || n > (1LL << 31) - 64) return kErrShape;
+  const int K = (int)k, iters = K / 128;
+  uint2* frag = static_cast<uint2*>(scratch);
+  int* meta = reinterpret_cast<int*>(static_cast<char*>(scratch) + batch * iters * 64 * 8);
+  long long* xg = reinterpret_cast<long long*>(meta + batch * 8);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+  const size_t esmem = (size_t)iters * 128 * sizeof(uint2) + (size_t)K * sizeof(float);
+  if (x_dtype == kBF16) {
+    if (esmem > 32 * 1024) e = cudaFuncSetAttribute(rtn4_encode_kernel<kBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)esmem);
+    if (e == cudaSuccess) e = launch_k(rtn4_encode_kernel<kBF16>, dim3((unsigned)batch), dim3(256), esmem, st, x, x_row_stride, K, (int)group_size, frag, meta, xg);
+  } else {
+    if (esmem > 32 * 1024) e = cudaFuncSetAttribute(rtn4_encode_kernel<kF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)esmem);
+    if (e == cudaSuccess) e = launch_k(rtn4_encode_kernel<kF32>, dim3((unsigned)batch), dim3(256), esmem, st, x, x_row_stride, K, (int)group_size, frag, meta, xg);
+  }
+  if (e != cudaSuccess) return kErrCuda;
+  Rtn4GemmParams p{};
+  p.codes = codes; p.scales = scales; p.biases = biases; p.frag = frag; p.meta = meta; p.xg = xg; p.y = y; p.err = err;
+  p.y_stride = y_row_stride; p.n_out = (int)n; p.K = K; p.nwords = K / 8; p.G = (int)group_size; p.iters = iters;
+  p.B = (int)batch;
+  const int np = K <= 2048 ? 8 : 4;
+  const int chunks = (int)((batch + 2 * np - 1) / (2 * np));
+  const int ntiles = (int)((n + 15) / 16);
+  int gx = 148 / chunks;
+  if (gx < 1) gx = 1;
+  if (gx > (ntiles + 7) / 8) gx = (ntiles + 7) / 8;
+  const size_t smem = (size_t)2 * np * iters * 64 * sizeof(uint2) + (size_t)2 * np * (kXgStride * 8 + 32);
+  dim3 grid((unsigned)gx, (unsigned)chunks);
+#define MB_RG(XT, ST, NP)                                                                                    \
+  do {                                                                                                       \
+    auto kern = rtn4_gemm_kernel<XT, ST, NP>;                                                                \
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                  \
+    if (e == cudaSuccess) e = launch_k(kern, grid, dim3(256), smem, st, p);                                  \
+  } while (0)
+  if (np == 8) {
+    if (x_dtype == kBF16) { if (s_dtype == kBF16) MB_RG(kBF16, kBF16, 8); else MB_RG(kBF16, kF32, 8); }
+    else { if (s_dtype == kBF16) MB_RG(kF32, kBF16, 8); else MB_RG(kF32, kF32, 8); }
+  } else {
+    if (x_dtype == kBF16) { if (s_dtype == kBF16) MB_RG(kBF16, kBF16, 4); else MB_RG(kBF16, kF32, 4); }
+    else { if (s_dtype == kBF16) MB_RG(kF32, kBF16, 4); else MB_RG(kF32, kF32, 4); }
+  }
+#undef MB_RG
+  return e == cudaSuccess ? kOk : kErrCuda;
 }
 
 extern "C" int64_t maple_argmax_workspace_bytes(int64_t batch, int64_t vocab) {

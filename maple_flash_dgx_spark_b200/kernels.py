@@ -117,6 +117,7 @@ def _expert_nk(packed_weight: torch.Tensor, packed_kn: bool, op: str) -> torch.T
 # over from the per-row GEMV launches.
 GEMM_MIN_ROWS = 4
 GROUPED_MIN_TOKENS = 4
+HEAD_GEMM_MIN_ROWS = 2
 
 
 def fxa_encode(x2d: torch.Tensor, rms_weight: torch.Tensor | None = None, eps: float = 1e-6):
@@ -573,8 +574,16 @@ def rtn4_gemv(x, packed_weight, scales, biases, group_size: int = 64, *, packed_
     s = scales.contiguous()
     b = biases.contiguous() if biases is not None else None
     y = torch.empty(batch, n_out, device=x.device, dtype=x.dtype)
-    check(lib().maple_rtn4_gemv(ptr(xm), dtype_code(x, op), batch, k_in, k_in, ptr(w), n_out, ptr(s), ptr(b),
-                                dtype_code(s, op), group_size, ptr(y), n_out, stream_ptr(x.device)), op)
+    L = lib()
+    if batch >= HEAD_GEMM_MIN_ROWS and k_in <= 4096:
+        # rows encoded once, the head streamed once per chunk of 16 rows
+        scratch = torch.empty(L.maple_rtn4_frag_bytes(batch, k_in), dtype=torch.uint8, device=x.device)
+        check(L.maple_rtn4_gemm(ptr(xm), dtype_code(x, op), batch, k_in, k_in, ptr(w), n_out, ptr(s), ptr(b),
+                                dtype_code(s, op), group_size, ptr(y), n_out, ptr(scratch), scratch.numel(),
+                                ptr(_err(x.device)), stream_ptr(x.device)), op)
+        return y.reshape(*leading, n_out)
+    check(L.maple_rtn4_gemv(ptr(xm), dtype_code(x, op), batch, k_in, k_in, ptr(w), n_out, ptr(s), ptr(b),
+                            dtype_code(s, op), group_size, ptr(y), n_out, stream_ptr(x.device)), op)
     return y.reshape(*leading, n_out)
 
 

@@ -199,18 +199,25 @@ def test_attention_vs_sdpa(cuda, K):
         torch.testing.assert_close(out[b:b + 1].float(), ref, rtol=1e-2, atol=1e-2)
 
 
-@pytest.mark.parametrize("group,symmetric,B", [(128, True, 1), (64, False, 1), (128, False, 3), (256, True, 2)])
-def test_rtn4_gemv(cuda, K, group, symmetric, B):
+@pytest.mark.parametrize("group,symmetric,B,k", [(128, True, 1, 2048), (64, False, 1, 2048), (128, False, 3, 2048),
+                                                (256, True, 2, 2048), (128, True, 17, 2048), (64, True, 5, 2048),
+                                                (128, True, 64, 2048), (128, False, 9, 4096)])
+def test_rtn4_gemv(cuda, K, group, symmetric, B, k):
+    """Batch >= 2 runs the batched head (rows encoded once, head streamed per
+    16-row chunk); every row equals the batch-1 kernel's row."""
     rs = rng(group + B)
-    N, k = 1000, 2048
+    N = 1000
     x = randn_bf(rs, B, k)
     codes = rs.randint(0, 16, size=(N, k)).astype(np.uint32)
     packed = oracle.pack_4bit(codes)
     s = bf(np.abs(rs.standard_normal((N, k // group))) * 0.003 + 1e-4)
     b = None if symmetric else bf(rs.standard_normal((N, k // group)) * 0.01)
-    y = K.rtn4_gemv(to_dev(x, cuda, torch.bfloat16), to_dev(packed, cuda), to_dev(s, cuda, torch.bfloat16),
-                    None if b is None else to_dev(b, cuda, torch.bfloat16), group_size=group)
+    xd, pd = to_dev(x, cuda, torch.bfloat16), to_dev(packed, cuda)
+    sd, bd = to_dev(s, cuda, torch.bfloat16), None if b is None else to_dev(b, cuda, torch.bfloat16)
+    y = K.rtn4_gemv(xd, pd, sd, bd, group_size=group)
     np.testing.assert_array_equal(to_np(y), oracle.rtn4_gemv(x, packed, s, b, group))
+    for r in {0, B - 1}:
+        torch.testing.assert_close(y[r:r + 1], K.rtn4_gemv(xd[r:r + 1], pd, sd, bd, group_size=group), rtol=0, atol=0)
 
 
 def test_rtn4_indexed_gemv(cuda, K):
