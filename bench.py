@@ -35,10 +35,12 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--breakdown", action="store_true",
                     help="also time each operator of the decode step in its own CUDA graph (48 layers)")
-    ap.add_argument("--workload", choices=["bs1", "bs64"], default="bs1",
+    ap.add_argument("--workload", choices=["bs1", "bs64", "long"], default="bs1",
                     help="bs1: configs[2] batch-1 decode (default); bs64: configs[3] batch-64 decode at 8192 "
-                         "cached positions per row")
-    ap.add_argument("--context", type=int, default=8192, help="bs64: cached positions per row")
+                         "cached positions per row; long: configs[4] long-context sampling (FlashHead at batch 1)")
+    ap.add_argument("--context", type=int, default=None,
+                    help="cached positions per row (bs64: 8192, long: 65536)")
+    ap.add_argument("--batch", type=int, default=1, help="long: rows (1, 16 or 256)")
     return ap.parse_args()
 
 
@@ -171,6 +173,9 @@ def main():
         return
     if args.workload == "bs64":
         run_bs64(args)
+        return
+    if args.workload == "long":
+        run_long(args)
         return
     import torch
 
@@ -351,7 +356,7 @@ def run_bs64(args):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    B, ctx = 64, int(args.context)
+    B, ctx = 64, int(args.context or 8192)
     cfg = synthetic_config(num_layers=args.layers)
     W, Kst = args.warmup, args.steps
     weights = synthetic_weights(cfg, SEED, dev)
@@ -500,6 +505,164 @@ def run_bs64(args):
         torch.cuda.synchronize(dev)
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_long(args):
+    """configs[4]: ``--batch`` rows (1, 16 or 256) with ``--context`` (65536)
+    random cached positions each; every step samples with the fused sampler
+    (T=1.0, top_p 0.95, top_k 20) from per-sequence counter-based uniforms.
+    Batch 1 scores through FlashHead (4748 clusters x 32, 512 probes) with the
+    dense RTN-4 head run alongside off the clock for the top-20 check; batch
+    16/256 use the dense batched head.  Batch 256 does not fit (1.65 TB of
+    K/V): its rows alias 16 physical cache rows through the row map -- every
+    row's K/V is read as issued, the rows sharing a physical row write the
+    same new position (last writer wins), so it is a throughput stress only."""
+    import torch
+
+    from maple_flash_dgx_spark_b200 import kernels as K
+    from maple_flash_dgx_spark_b200.flash_head import attach_flash_head
+    from maple_flash_dgx_spark_b200.model import MapleForCausalLM, packed_decode_bytes
+    from maple_flash_dgx_spark_b200.synth import fill_kv_cache, synthetic_config, synthetic_tokens, synthetic_weights
+
+    world, rank, local = _dist()
+    if world > 1:
+        raise SystemExit("--workload long runs one GPU per process")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, ctx = int(args.batch), int(args.context or 65536)
+    phys = min(B, 16)
+    cfg = synthetic_config(num_layers=args.layers)
+    W, Kst = args.warmup, args.steps
+    weights = synthetic_weights(cfg, SEED, dev)
+    use_flash = B == 1
+    t_cluster = 0.0
+    if use_flash:
+        t0 = time.perf_counter()
+        attach_flash_head(cfg, weights, n_clusters=4748, n_probes=512)
+        torch.cuda.synchronize(dev)
+        t_cluster = time.perf_counter() - t0
+    model = MapleForCausalLM.from_weight_dict(cfg, weights, device=dev, use_flash_head=use_flash)
+    del weights
+    torch.cuda.empty_cache()
+    cache = model.make_cache(max_len=ctx + W + Kst + 8, batch=phys)
+    fill_kv_cache(cache, SEED, ctx)
+    if B > phys:  # aliased rows (throughput stress)
+        cache.batch = B
+        cache.seqlen = torch.full((B,), ctx, dtype=torch.int64, device=dev)
+        cache.seen = [ctx] * B
+        cache.row_of = list(range(B))
+        cache.row_map = (torch.arange(B, device=dev) % phys).to(torch.int32)
+        cache.remap = True
+    ids = torch.zeros(B, 1, dtype=torch.long, device=dev)
+    ids.copy_(synthetic_tokens(SEED, B, cfg["vocab_size"], dev).reshape(B, 1))
+    rng = K.RowUniform(range(1000, 1000 + B), dev)
+    ws = K.batched_sampler_workspace(cfg["vocab_size"], 20, B, dev)
+
+    def step():
+        logits = model.forward(ids, cache=cache, logits_to_keep=1)
+        return K.fused_sample_batched(logits[:, -1, :], rng(), temperature=1.0, top_p=0.95, top_k=20, workspace=ws)
+
+    with torch.inference_mode():
+        snap = (cache.seqlen.clone(), list(cache.seen))
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                step()
+                cache.seqlen.copy_(snap[0])
+                cache.seen = list(snap[1])
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=st):
+                nxt = step()
+        torch.cuda.current_stream(dev).wait_stream(st)
+        torch.cuda.synchronize(dev)
+        cache.seqlen.copy_(snap[0])
+        cache.seen = list(snap[1])
+        for _ in range(W):
+            graph.replay()
+            ids.copy_(nxt.reshape(B, 1))
+        torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            torch.cuda.nvtx.range_push("maple_decode")
+            start.record()
+            for _ in range(Kst):
+                graph.replay()
+                ids.copy_(nxt.reshape(B, 1))
+            end.record()
+            torch.cuda.synchronize(dev)
+            torch.cuda.nvtx.range_pop()
+        ms = start.elapsed_time(end)
+        cache.advance_host(W + Kst, B)
+        tok_s = B * Kst / (ms / 1000.0)
+        pin_in = torch.empty(B, 1, dtype=torch.long, pin_memory=True)
+        pin_out = torch.empty(B, dtype=torch.long, pin_memory=True)
+        pin_in.copy_(ids.cpu())
+        ev = torch.cuda.Event()
+        ne2e = max(1, min(Kst, 16))
+        torch.cuda.synchronize(dev)
+        t_0 = time.perf_counter()
+        for _ in range(ne2e):
+            ids.copy_(pin_in, non_blocking=True)
+            graph.replay()
+            pin_out.copy_(nxt.reshape(B), non_blocking=True)
+            ev.record()
+            ev.synchronize()
+            pin_in[:, 0] = pin_out
+        e2e = B * ne2e / (time.perf_counter() - t_0)
+        cache.advance_host(ne2e, B)
+        flash = None
+        if use_flash:
+            # FlashHead vs the dense head on random decode-like hidden states: top-20 recall at 512 probes
+            hs = torch.randn(8, 1, 1, cfg["hidden_size"], device=dev).to(torch.bfloat16)
+            rec = []
+            for h in hs:
+                fl = model.lm_head_flash(h).reshape(-1).float()
+                de = model.lm_head(h.reshape(1, -1)).reshape(-1).float()
+                a = set(torch.topk(fl, 20).indices.tolist())
+                b_ = set(torch.topk(de, 20).indices.tolist())
+                rec.append(len(a & b_) / 20.0)
+            flash = {"n_clusters": 4748, "n_probes": 512, "recall_at_20": sum(rec) / len(rec),
+                     "head_bytes": model.lm_head_flash.head_bytes(), "clustering_s": round(t_cluster, 1)}
+        att = model.layers[0].self_attn
+        q = torch.randn(phys, model.num_heads, 1, model.head_dim, device=dev).to(torch.bfloat16)
+        pos = torch.full((phys,), ctx, dtype=torch.int64, device=dev)
+        fns = [lambda i=i: K.decode_gqa_attn(q, cache.k[i], cache.v[i], pos, scale=att.scale, window=None,
+                                             split_len=cache.split_len, kv_final=True)
+               for i in range(len(model.layers))]
+        att_us = _time_graph(fns, dev) * 1000.0 / len(fns)
+        kv_per_launch = phys * model.num_kv_heads * model.head_dim * 2 * 2 * (ctx + 1)
+    peak, peak_kind = _peaks()
+    wb = packed_decode_bytes(cfg)
+    head = flash["head_bytes"] if flash else wb["head_bytes"]
+    kv_step = B * cfg["num_hidden_layers"] * cfg["num_key_value_heads"] * cfg["head_dim"] * 2 * 2 * (ctx + W + Kst // 2)
+    expert_rows = min(B * cfg["num_experts_per_tok"], cfg["num_experts"])
+    weights_step = wb["packed_weight_bytes"] - wb["head_bytes"] + head + wb["expert_bytes"] * (expert_rows /
+                                                                                             cfg["num_experts_per_tok"] - 1)
+    step_bytes = int(weights_step + kv_step)
+    sec = ms / Kst / 1000.0
+    line = {
+        "metric": f"decode tok/s (long context {ctx}, bs{B}, configs[4])", "value": tok_s, "unit": "tok/s",
+        "n_gpus": 1, "steps": Kst, "warmup": W, "ms_per_step": ms / Kst, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights of the configs[2] architecture; K/V bf16 N(0,1))",
+        "config": {"workload": f"configs[4]: bs{B}, {ctx} cached positions, sampled T=1.0 top_p=0.95 top_k=20, "
+                               f"per-sequence counter RNG, {'FlashHead 4748x32 / 512 probes' if use_flash else 'dense RTN-4 head'}",
+                   "global_batch": B, "seq_len": ctx, "physical_cache_rows": phys,
+                   "parallelism": "single", "l2": f"{step_bytes / 1e9:.1f} GB streamed per step (> 126 MB L2)"},
+        "hbm_roofline_step": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / sec / 1e9, "peak_gbs": peak,
+                              "frac": step_bytes / sec / 1e9 / peak},
+        "roofline": {"kernel": f"gqa decode attention ({phys} rows x {ctx} positions)", "bound": "hbm",
+                     "achieved": kv_per_launch / (att_us * 1e-6) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": kv_per_launch / (att_us * 1e-6) / 1e9 / peak, "traffic": None,
+                     "algorithmic_bytes": kv_per_launch, "launch_us": att_us, "peak_kind": f"{peak_kind} hbm_gbs"},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 8 * B},
+        "gpu_launches": Kst * (8 * cfg["num_hidden_layers"] + 8),
+        "clocks": clocks.summary(),
+    }
+    if flash:
+        line["flash_head"] = flash
+    print(json.dumps(line), flush=True)
 
 
 def swiglu_roofline(model, prompt, dev):

@@ -264,6 +264,13 @@ int maple_fused_sample(const void* logits, int x_dtype, int64_t batch, int64_t v
                        const float* uniform, float temperature, float top_p, int64_t top_k, int64_t* out,
                        void* workspace, int64_t workspace_bytes, void* stream);
 
+/* One uniform in [0, 1) per row for the fused sampler from a per-sequence
+ * seed: splitmix64 of (seeds[b], *counter); the kernel advances *counter, so
+ * a captured decode graph draws new values every replay.  No reference
+ * counterpart (the reference draws from per-request torch generators,
+ * server.py:591-596; sampler parity is defined on the uniform). */
+int maple_row_uniform(const uint64_t* seeds, int64_t batch, int64_t* counter, float* out, void* stream);
+
 /* Embedding gather (plain table) and RTN-4 gather + dequant.  Replace
  * kernels/rtn4.py:27 rtn4_embedding / linear.py:95 PackedRTN4Embedding.  An
  * out-of-range id writes zeros and sets bit 2 of *err. */

@@ -79,6 +79,7 @@ _SIGS: dict[str, tuple] = {
                                     f32, i64, i64, i32, vp, i64, i64, vp, i64, vp, vp]),
     "maple_rtn4_gemv": (i32, [vp, i32, i64, i64, i64, vp, i64, vp, vp, i32, i64, vp, i64, vp]),
     "maple_rtn4_frag_bytes": (i64, [i64, i64]),
+    "maple_row_uniform": (i32, [vp, i64, vp, vp, vp]),
     "maple_rtn4_gemm": (i32, [vp, i32, i64, i64, i64, vp, i64, vp, vp, i32, i64, vp, i64, vp, i64, vp, vp]),
     "maple_rtn4_indexed_gemv": (i32, [vp, i32, i64, i64, i64, vp, i64, i64, vp, vp, i32, i64, vp, i64, vp, i64,
                                       vp]),

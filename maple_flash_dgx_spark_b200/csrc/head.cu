@@ -639,6 +639,31 @@ __global__ void __launch_bounds__(256, 1) rtn4_gemm_kernel(Rtn4GemmParams p) {
   }
 }
 
+// ------------------------------------------------- per-row sampler draws --
+// One uniform in [0, 1) per row from a counter-based generator: the
+// splitmix64 finaliser of (row seed, step), the step a device counter that
+// the kernel advances, so a captured decode graph draws fresh values on every
+// replay.  Stands in for the per-request torch.Generator draws of
+// server.py:591-596 (the sampler's parity is defined on the uniform).
+__device__ __forceinline__ uint64_t row_mix(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ULL;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+
+__global__ void __launch_bounds__(1024) row_uniform_kernel(const uint64_t* seeds, int64_t* counter, int B, float* out) {
+  pdl_wait();
+  pdl_trigger();
+  const uint64_t step = static_cast<uint64_t>(counter[0]);
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const uint64_t h = row_mix(row_mix(seeds[b]) ^ (step * 0xD1B54A32D192ED03ULL));
+    out[b] = static_cast<float>(h >> 40) * (1.0f / 16777216.0f);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) counter[0] = static_cast<int64_t>(step + 1);
+}
+
 int rtn4_launch(Rtn4Params& p, int x_dtype, int s_dtype, int64_t batch, void* stream) {
   const size_t smem = (size_t)p.iters * 128 * sizeof(uint2) + (size_t)p.K * sizeof(float);
   const int nblk = (p.n_out + 63) / 64;
@@ -763,6 +788,16 @@ extern "C" int maple_rtn4_gemm(const void* x, int x_dtype, int64_t batch, int64_
     else { if (s_dtype == kBF16) MB_RG(kF32, kBF16, 4); else MB_RG(kF32, kF32, 4); }
   }
 #undef MB_RG
+  return e == cudaSuccess ? kOk : kErrCuda;
+}
+
+extern "C" int maple_row_uniform(const uint64_t* seeds, int64_t batch, int64_t* counter, float* out,
+                                 void* stream) {
+  if (batch < 0 || batch > 65535) return kErrShape;
+  if (batch == 0) return kOk;
+  if (!seeds || !counter || !out) return kErrShape;
+  cudaError_t e = launch_k(row_uniform_kernel, dim3(1), dim3(1024), 0, static_cast<cudaStream_t>(stream), seeds,
+                           counter, (int)batch, out);
   return e == cudaSuccess ? kOk : kErrCuda;
 }
 

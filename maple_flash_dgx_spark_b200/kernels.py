@@ -717,6 +717,23 @@ def fused_sample_batched(logits, uniform, *, temperature: float, top_p: float, t
     return _sample(logits, uniform, temperature, top_p, top_k, ws, out)
 
 
+class RowUniform:
+    """Per-sequence uniforms for the fused sampler: row b draws
+    splitmix64(seed_b, step) with the step counter kept on the device, so the
+    draw can live inside a captured decode graph."""
+
+    def __init__(self, seeds, device):
+        self.seeds = torch.as_tensor(list(seeds), dtype=torch.int64).to(device).view(torch.uint64) \
+            if not isinstance(seeds, torch.Tensor) else seeds.to(device=device, dtype=torch.int64).view(torch.uint64)
+        self.counter = torch.zeros(1, dtype=torch.int64, device=device)
+        self.out = torch.empty(self.seeds.numel(), dtype=torch.float32, device=device)
+
+    def __call__(self) -> torch.Tensor:
+        check(lib().maple_row_uniform(ptr(self.seeds), self.seeds.numel(), ptr(self.counter), ptr(self.out),
+                                      stream_ptr(self.out.device)), "row_uniform")
+        return self.out
+
+
 def sampler_workspace(vocab: int, top_k: int, device):
     """Preallocated sampler scratch (zeroed; the kernel leaves it reusable).  Reference kernels/sampler.py:209."""
     return batched_sampler_workspace(vocab, top_k, 1, device)

@@ -298,3 +298,16 @@ def test_synthetic_generator_matches_oracle(cuda):
     np.testing.assert_array_equal(to_np(scales), s_o)
     tok = S.synthetic_tokens(5, 100, 151936, cuda)
     np.testing.assert_array_equal(to_np(tok), om.synth_tokens(5, 100, 151936))
+
+
+def test_row_uniform_per_sequence(cuda, K):
+    """Counter-based per-row uniforms: in [0, 1), a fresh draw per call, the
+    same sequence for the same seeds, independent of the other rows."""
+    a = K.RowUniform([7, 8, 9], cuda)
+    b = K.RowUniform([7, 100, 9], cuda)
+    d1, d2 = a().clone(), a().clone()
+    e1 = b().clone()
+    assert ((d1 >= 0) & (d1 < 1)).all() and not torch.equal(d1, d2)
+    assert d1[0] == e1[0] and d1[2] == e1[2] and d1[1] != e1[1]
+    c = K.RowUniform([7, 8, 9], cuda)
+    torch.testing.assert_close(c(), d1, rtol=0, atol=0)
