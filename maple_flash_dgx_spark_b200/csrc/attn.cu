@@ -130,6 +130,7 @@ struct AttnParams {
   int64_t q_sb, q_sh, kc_sb, kc_sh, vc_sb, vc_sh, o_sb, o_sh;
   int Hq, Hkv, G, Bc, T, P, NS, window;
   int kv_final;           // 1: K/V at positions < seqlen[b] were final before the previous launch
+  int defer_merge;        // 1: leave the split partials for gqa_merge_kernel (long contexts)
   float scale;
 };
 
@@ -277,7 +278,7 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
       }
     }
   }
-  if (ns == 1) return;
+  if (ns == 1 || p.defer_merge) return;
 
   // Last split of (b, h) merges all splits in split order.
   __threadfence();
@@ -524,6 +525,60 @@ __global__ void __launch_bounds__(256) gqa_cluster_kernel(AttnParams p) {
   cluster.sync();  // peers keep their shared memory until the merge has read it
 }
 
+
+// Merge of long contexts' split partials, one CTA per (row, query head) and
+// one thread per dimension, so hundreds of splits are read by many SMs at
+// once rather than by the last split's CTA.  Same arithmetic as the in-kernel
+// merge: M = max_j m_j, w_j = exp(m_j - M), den and num as fmaf chains in
+// split order, out = num / den.
+template <int XT, int D>
+__global__ void __launch_bounds__(D) gqa_merge_kernel(AttnParams p) {
+  __shared__ float s_max[D / 32];
+  const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+  const int hq = blockIdx.x, b = blockIdx.y;
+  const int es = XT == kBF16 ? 2 : 4;
+  pdl_wait();
+  pdl_trigger();
+  const int64_t pos = p.seqlen[b];
+  const int kv_len = (int)min(pos + 1, (int64_t)p.T);
+  const int start = p.window > 0 ? max(0, kv_len - p.window) : 0;
+  const int ns = kv_len > start ? (kv_len - start + p.P - 1) / p.P : 0;
+  if (ns <= 1) return;  // a single split was stored directly
+  const float* ml = p.ws_ml + ((int64_t)b * p.Hq + hq) * p.NS * 2;
+  const float* ac = p.ws_acc + ((int64_t)b * p.Hq + hq) * p.NS * D;
+  float M = __int_as_float(0xff800000);
+  for (int j = d; j < ns; j += D) M = fmaxf(M, __ldcg(ml + 2 * j));
+  M = warp_max(M);
+  if (lane == 0) s_max[warp] = M;
+  __syncthreads();
+  M = s_max[0];
+#pragma unroll
+  for (int w = 1; w < D / 32; ++w) M = fmaxf(M, s_max[w]);
+  float num = 0.0f, den = 0.0f;
+  constexpr int kB = 8;
+  for (int j0 = 0; j0 < ns; j0 += kB) {
+    float mj[kB], lj[kB], aj[kB];
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      const int j = j0 + i;
+      if (j < ns) {
+        mj[i] = __ldcg(ml + 2 * j);
+        lj[i] = __ldcg(ml + 2 * j + 1);
+        aj[i] = __ldcg(ac + (int64_t)j * D + d);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+      if (j0 + i < ns) {
+        const float w = mexp(__fsub_rn(mj[i], M));
+        den = __fmaf_rn(w, lj[i], den);
+        num = __fmaf_rn(w, aj[i], num);
+      }
+    }
+  }
+  store_f<XT>(static_cast<char*>(p.out) + (b * p.o_sb + hq * p.o_sh) * es, d, __fdiv_rn(num, den));
+}
+
 }  // namespace mb
 
 using namespace mb;
@@ -650,11 +705,16 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
   const size_t smem = 2 * (size_t)split_len * head_dim * es + 2 * 8 * (size_t)split_len * sizeof(float);
   dim3 grid((unsigned)ns, (unsigned)num_kv_heads, (unsigned)batch);
   cudaError_t e = cudaSuccess;
+  // Long contexts: the splits' merge gets its own launch spread over
+  // (row, query head) CTAs instead of one CTA per (row, kv head).
+  p.defer_merge = ns >= 128 ? 1 : 0;
 #define MB_ATT(XT, DD)                                                                        \
   do {                                                                                        \
     auto kern = gqa_decode_kernel<XT, DD>;                                                    \
     if (smem > 32 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    if (e == cudaSuccess) launch_k(kern, dim3(grid), dim3(128), smem, st, p);                                   \
+    if (e == cudaSuccess) e = launch_k(kern, dim3(grid), dim3(128), smem, st, p);                               \
+    if (e == cudaSuccess && p.defer_merge)                                                    \
+      e = launch_k(gqa_merge_kernel<XT, DD>, dim3((unsigned)num_heads, (unsigned)batch), dim3(DD), 0, st, p);   \
   } while (0)
   if (x_dtype == kBF16) {
     if (head_dim == 64) MB_ATT(kBF16, 64); else if (head_dim == 128) MB_ATT(kBF16, 128); else MB_ATT(kBF16, 256);

@@ -136,6 +136,8 @@ def _attn_case(rs, B, Hq, Hkv, D, T, lens, Bc=None):
     (2, 8, 8, 128, 512, [512, 100], 64, 96),
     (1, 32, 4, 128, 512, [512], 32, 0),
     (2, 32, 4, 128, 1024, [1024, 700], 64, 0),
+    (1, 32, 4, 128, 8192, [8192], 64, 0),
+    (3, 16, 2, 128, 16384, [16384, 9000, 1], 128, 0),
 ])
 @pytest.mark.parametrize("kv_final", [False, True])
 def test_qkv_decode_and_attention(cuda, K, B, Hq, Hkv, D, T, lens, split, window, kv_final):
