@@ -363,7 +363,7 @@ def run_bs64(args):
     T, t0 = B, 0
     if world > 1:
         from maple_flash_dgx_spark_b200.expert_parallel import (EPDecodeGraph, EPDecoder, EPExchange,
-                                                                shard_expert_weights, token_range)
+                                                                EPExchangeP2P, shard_expert_weights, token_range)
 
         weights = shard_expert_weights(weights, cfg, rank, world)
         t0, T = token_range(B, rank, world)
@@ -376,7 +376,14 @@ def run_bs64(args):
     graph_kind = "cuda graph"
     with torch.inference_mode():
         if world > 1:
-            dec = EPDecoder(model, EPExchange(None, rank, world, cfg["num_experts"]))
+            # MAPLE_EP_TRANSPORT=nccl selects the NCCL collectives; default: NVLink peer-store kernels
+            transport = os.environ.get("MAPLE_EP_TRANSPORT", "p2p")
+            if transport == "nccl":
+                ex = EPExchange(None, rank, world, cfg["num_experts"])
+            else:
+                ex = EPExchangeP2P(None, rank, world, cfg["num_experts"], tokens=T, hidden=cfg["hidden_size"],
+                                   topk=cfg["num_experts_per_tok"], device=dev)
+            dec = EPDecoder(model, ex)
             holder = {}  # the only reference to the captured graph (freed before the group is destroyed)
             try:
                 holder["g"] = EPDecodeGraph(dec, cache, T)
@@ -482,6 +489,7 @@ def run_bs64(args):
         "config": {"workload": f"configs[3]: bs64 greedy decode, {ctx} cached positions per row", "global_batch": B,
                    "seq_len": ctx, "context": [ctx0, ctx0 + Kst],
                    "parallelism": f"ep{world}+dp-attention{world}" if world > 1 else "single", "step": graph_kind,
+                   "ep_transport": os.environ.get("MAPLE_EP_TRANSPORT", "p2p") if world > 1 else None,
                    "l2": f"{step_bytes / 1e9:.1f} GB streamed per GPU per step (> 126 MB L2), no flush needed"},
         "hbm_roofline_step": {"bytes_per_gpu_step": step_bytes, "achieved_gbs": step_bytes / sec / 1e9,
                               "peak_gbs": peak, "frac": step_bytes / sec / 1e9 / peak},
@@ -503,6 +511,8 @@ def run_bs64(args):
         del step, nxt_of
         gc.collect()
         torch.cuda.synchronize(dev)
+        if hasattr(ex, "close"):
+            ex.close()
         dist.barrier()
         dist.destroy_process_group()
 

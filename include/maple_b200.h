@@ -113,6 +113,30 @@ int maple_ep_combine(const void* recv, int x_dtype, int64_t world, int64_t token
                      const int32_t* expert_ids, const float* topk_weight, int64_t n_experts, const void* residual,
                      void* y, void* stream);
 
+/* Expert-parallel exchange over NVLink peer memory (no reference
+ * counterpart; replaces the NCCL all-gather / all-to-all of the EP layer).
+ * peer_bases[r] is rank r's symmetric buffer (same size and layout on every
+ * rank, mapped here through CUDA IPC; peer_bases[rank] is this rank's own),
+ * zero-filled before first use; off_recv / off_flags locate the receive area
+ * and the maple_p2p_flag_bytes() flag area in it.  seq / ticket: this rank's
+ * device counters for the call type (one pair per call type, zeroed once).
+ * Waits for the peers are bounded; a wait that gives up sets bit 1 of *err.
+ *
+ * maple_p2p_allgather: bytes_per_rank (multiple of 16) from src land at
+ * recv + rank * bytes_per_rank on every rank.
+ * maple_p2p_combine: the slot rows y[s] (s < world*T*topk, rows of all ranks'
+ * tokens) of this rank's experts go to the owning rank's recv area; then
+ * out[t] = sum_j w_mine[t,j] * row(owner(e_tj), t*topk+j) (+ residual) for
+ * this rank's T tokens, in moe_reduce_add's order. */
+int64_t maple_p2p_flag_bytes(void);
+int maple_p2p_allgather(void* const* peer_bases, int world, int rank, int64_t off_recv, int64_t off_flags,
+                        const void* src, int64_t bytes_per_rank, unsigned* seq, unsigned* ticket, int* err,
+                        void* stream);
+int maple_p2p_combine(void* const* peer_bases, int world, int rank, int64_t off_recv, int64_t off_flags, const void* y,
+                      int x_dtype, const int32_t* ids_all, int64_t tokens_per_rank, int64_t topk, int64_t n,
+                      int64_t n_experts, const int32_t* ids_mine, const float* w_mine, const void* residual, void* out,
+                      unsigned* seq, unsigned* ticket, int* err, void* stream);
+
 /* Grouped expert GEMM over a plan: slot s reads encoded row s / in_div
  * (in_div = top_k when rows are tokens, 1 when they are slots) and writes
  * row s of y.  codes [n_experts, code_rows, k/16]; swiglu != 0 runs the

@@ -55,6 +55,10 @@ _SIGS: dict[str, tuple] = {
     "maple_moe_plan": (i32, [vp, i64, i64, vp, vp, vp]),
     "maple_moe_plan_range": (i32, [vp, i64, i64, i64, i64, vp, vp, vp]),
     "maple_ep_combine": (i32, [vp, i32, i64, i64, i64, i64, vp, vp, i64, vp, vp, vp]),
+    "maple_p2p_flag_bytes": (i64, []),
+    "maple_p2p_allgather": (i32, [vp, i32, i32, i64, i64, vp, i64, vp, vp, vp, vp]),
+    "maple_p2p_combine": (i32, [vp, i32, i32, i64, i64, vp, i32, vp, i64, i64, i64, i64, vp, vp, vp, vp, vp, vp,
+                                vp, vp]),
     "maple_ternary_grouped_gemm": (i32, [vp, vp, i64, i64, vp, i64, i64, vp, i32, vp, vp, i64, i64, i32, i32, vp,
                                          i32, i64, vp, vp]),
     "maple_ternary_expert_gemv_workspace_bytes": (i64, [i64, i64, i64]),

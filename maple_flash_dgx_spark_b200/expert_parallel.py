@@ -24,8 +24,13 @@ decode); the reference itself runs on one GPU.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
+
+from maple_flash_dgx_spark_b200 import _lib
+from maple_flash_dgx_spark_b200._lib import check, dtype_code, lib, ptr, stream_ptr
 
 from maple_flash_dgx_spark_b200.kernels import (
     argmax,
@@ -110,6 +115,135 @@ class EPExchange:
         return out
 
 
+class _DeviceMem:
+    """__cuda_array_interface__ view of raw device memory (zero-copy)."""
+
+    def __init__(self, addr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (addr, False), "version": 3,
+                                         "strides": None}
+
+
+class SymmetricBuffer:
+    """One device buffer of the same size on every rank, mapped into the other
+    ranks through CUDA IPC (cudaIpcGetMemHandle / cudaIpcOpenMemHandle), zeroed.
+    ``bases`` is the ctypes array of every rank's address as seen here."""
+
+    def __init__(self, nbytes: int, group, rank: int, world: int, device: torch.device):
+        from cuda.bindings import runtime as rt
+
+        self.rt, self.rank, self.world, self.group = rt, rank, world, group
+        self.nbytes = int(nbytes)
+        with torch.cuda.device(device):
+            err, base = rt.cudaMalloc(self.nbytes)
+            if err != rt.cudaError_t.cudaSuccess:
+                raise RuntimeError(f"cudaMalloc of the symmetric buffer failed: {err}")
+            rt.cudaMemset(base, 0, self.nbytes)
+            rt.cudaDeviceSynchronize()
+            err, handle = rt.cudaIpcGetMemHandle(base)
+            if err != rt.cudaError_t.cudaSuccess:
+                raise RuntimeError(f"cudaIpcGetMemHandle failed: {err}")
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle.reserved), group=group)
+        self.own = int(base)
+        self.opened = []
+        addrs = []
+        with torch.cuda.device(device):
+            for r in range(world):
+                if r == rank:
+                    addrs.append(self.own)
+                    continue
+                h = rt.cudaIpcMemHandle_t()
+                h.reserved = handles[r]
+                err, peer = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+                if err != rt.cudaError_t.cudaSuccess:
+                    raise RuntimeError(f"cudaIpcOpenMemHandle of rank {r} failed: {err}")
+                self.opened.append(peer)
+                addrs.append(int(peer))
+        dist.barrier(group=group)
+        self.bases = (ctypes.c_void_p * world)(*addrs)
+        self.device = device
+
+    def view(self, offset: int, nbytes: int) -> torch.Tensor:
+        return torch.as_tensor(_DeviceMem(self.own + offset, nbytes), device=self.device)
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers, then free this rank's."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            self.rt.cudaIpcCloseMemHandle(p)
+        dist.barrier(group=self.group)
+        self.rt.cudaFree(self.own)
+        self.own = None
+
+
+def _round256(n: int) -> int:
+    return (n + 255) // 256 * 256
+
+
+class EPExchangeP2P(EPExchange):
+    """EPExchange over NVLink peer memory: ``dispatch`` is a peer-store
+    all-gather kernel and ``combine`` sends each rank's expert rows to the
+    token owners and sums them in the same kernel (``maple_p2p_*``).  Buffers
+    are sized for ``tokens`` rows per rank, fixed for the object's life."""
+
+    def __init__(self, group, rank: int, world: int, n_experts: int, *, tokens: int, hidden: int, topk: int,
+                 device: torch.device, dtype=torch.bfloat16):
+        super().__init__(group, rank, world, n_experts)
+        self.tokens, self.hidden, self.topk, self.dtype = tokens, hidden, topk, dtype
+        es = torch.tensor([], dtype=dtype).element_size()
+        self.hb = hidden * es
+        self.rowbytes = (self.hb + 4 * topk + 15) // 16 * 16
+        self.off_disp = 0
+        self.off_comb = _round256(world * tokens * self.rowbytes)
+        self.off_flags = self.off_comb + _round256(world * tokens * topk * hidden * es)
+        total = self.off_flags + _round256(lib().maple_p2p_flag_bytes())
+        self.buf = SymmetricBuffer(total, group, rank, world, device)
+        self.recv = self.buf.view(self.off_disp, world * tokens * self.rowbytes).view(world * tokens, self.rowbytes)
+        self.send = torch.zeros(tokens, self.rowbytes, dtype=torch.uint8, device=device)
+        self.state = torch.zeros(4, dtype=torch.int32, device=device)  # seq/ticket of dispatch, then of combine
+        self.err = _lib.error_word(device)
+        self.device = device
+        self.ids_all = None
+
+    def _state(self, i):
+        return self.state.data_ptr() + 4 * i
+
+    def dispatch(self, hidden: torch.Tensor, idx: torch.Tensor):
+        T, H = hidden.shape
+        k = idx.shape[1]
+        if T != self.tokens or H != self.hidden or k != self.topk:
+            raise ValueError(f"EPExchangeP2P sized for {self.tokens}x{self.hidden} top-{self.topk}, got {T}x{H} "
+                             f"top-{k}.")
+        self.send[:, :self.hb].copy_(hidden.contiguous().view(torch.uint8).reshape(T, self.hb))
+        self.send[:, self.hb:self.hb + 4 * k].copy_(idx.to(torch.int32).contiguous().view(torch.uint8)
+                                                    .reshape(T, 4 * k))
+        check(lib().maple_p2p_allgather(self.buf.bases, self.world, self.rank, self.off_disp, self.off_flags,
+                                        ptr(self.send), T * self.rowbytes, self._state(0), self._state(1),
+                                        ptr(self.err), stream_ptr(self.device)), "p2p_dispatch")
+        x_all = self.recv[:, :self.hb].view(hidden.dtype)
+        self.ids_all = self.recv[:, self.hb:self.hb + 4 * k].contiguous().view(torch.int32)
+        return x_all, self.ids_all
+
+    def combine(self, y_all: torch.Tensor, idx: torch.Tensor, wt: torch.Tensor, residual=None) -> torch.Tensor:
+        y = y_all.reshape(-1, self.hidden).contiguous()
+        out = torch.empty(self.tokens, self.hidden, dtype=y.dtype, device=y.device)
+        ids = idx.to(torch.int32).contiguous()
+        w = wt.float().contiguous()
+        res = residual.reshape(self.tokens, self.hidden).contiguous() if residual is not None else None
+        check(lib().maple_p2p_combine(self.buf.bases, self.world, self.rank, self.off_comb, self.off_flags, ptr(y),
+                                      dtype_code(y, "p2p_combine"), ptr(self.ids_all), self.tokens, self.topk,
+                                      self.hidden, self.n_experts, ptr(ids), ptr(w), ptr(res), ptr(out),
+                                      self._state(2), self._state(3), ptr(self.err), stream_ptr(self.device)),
+              "p2p_combine")
+        return out
+
+    def close(self) -> None:
+        self.buf.close()
+
+
 class EPMoeBlock:
     """Drop-in for ``MapleSparseMoeBlock`` holding this rank's experts only."""
 
@@ -124,6 +258,8 @@ class EPMoeBlock:
         plan = moe_plan(ids_all, self.ex.n_experts, e_first=self.ex.e_first, n_local=self.ex.n_local)
         h = ternary_expert_swiglu(x_all, b.up_gate.packed_weight, b.up_gate.row_alpha, ids_all, plan=plan)
         y = ternary_expert_gemv(h, b.down.packed_weight, b.down.row_alpha, ids_all, plan=plan)
+        if isinstance(self.ex, EPExchangeP2P):
+            return self.ex.combine(y, idx, wt, residual)
         recv = self.ex.combine_exchange(y.reshape(-1, y.shape[-1]))
         return ep_combine(recv, idx, wt, self.ex.n_experts, residual)
 

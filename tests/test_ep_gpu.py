@@ -39,12 +39,12 @@ def _reference_ids(dev):
     return torch.stack(out, 1)
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, transport):
     import datetime
 
     import torch.distributed as dist
 
-    from maple_flash_dgx_spark_b200.expert_parallel import (EPDecodeGraph, EPDecoder, EPExchange,
+    from maple_flash_dgx_spark_b200.expert_parallel import (EPDecodeGraph, EPDecoder, EPExchange, EPExchangeP2P,
                                                             shard_expert_weights, token_range)
     from maple_flash_dgx_spark_b200.model import MapleForCausalLM
     from maple_flash_dgx_spark_b200.synth import fill_kv_cache, synthetic_tokens, synthetic_weights
@@ -56,10 +56,14 @@ def _worker(rank, world, port, q):
                             device_id=dev)
     try:
         cfg = _cfg()
-        ex = EPExchange(None, rank, world, cfg["num_experts"])
+        t0, T = token_range(B, rank, world)
+        if transport == "p2p":
+            ex = EPExchangeP2P(None, rank, world, cfg["num_experts"], tokens=T, hidden=cfg["hidden_size"],
+                               topk=cfg["num_experts_per_tok"], device=dev)
+        else:
+            ex = EPExchange(None, rank, world, cfg["num_experts"])
         w = shard_expert_weights(synthetic_weights(cfg, SEED, dev), cfg, rank, world)
         model = MapleForCausalLM.from_weight_dict(cfg, w, device=dev)
-        t0, T = token_range(B, rank, world)
         cache = model.make_cache(max_len=CTX + STEPS + 2, batch=T)
         fill_kv_cache(cache, SEED, CTX, row0=t0, total_rows=B)
         tok = synthetic_tokens(SEED, B, cfg["vocab_size"], dev)[t0:t0 + T].reshape(T, 1)
@@ -75,12 +79,19 @@ def _worker(rank, world, port, q):
                 cache.advance_host(1, T)
                 ids.append(tok.reshape(-1).cpu())
             del g
+        from maple_flash_dgx_spark_b200 import _lib
+
+        assert int(_lib.error_word(dev).item()) == 0, "a bounded peer wait gave up"
+        if transport == "p2p":
+            ex.close()
         q.put((rank, torch.stack(ids, 1)))
     finally:
         dist.destroy_process_group()
 
 
-def test_ep_decode_equals_single_gpu(cuda):
+@pytest.mark.parametrize("transport", ["nccl", "p2p"])
+def test_ep_decode_equals_single_gpu(cuda, transport):
+    """NCCL collectives, and the NVLink peer-store exchange kernels."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -91,7 +102,7 @@ def test_ep_decode_equals_single_gpu(cuda):
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, transport)) for r in range(2)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=300) for _ in range(2))
