@@ -205,6 +205,16 @@ int maple_router_topk(const void* x, int x_dtype, int64_t x_row_stride, int64_t 
                       const void* gate, int gate_dtype, int64_t n_experts, int64_t topk, int32_t* idx,
                       float* wt, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* add_rms_norm (fused_norm.py:128-161) fused in front of router_topk: for
+ * each token row, residual_out = x + y and normed_out = RMSNorm(x + y) * norm_w
+ * (the add_rms_norm kernel's arithmetic), and the router runs on normed_out.
+ * x, y, residual_out, normed_out share x_dtype and row_stride.  No separate
+ * reference entry (model.py:498-506 calls the two in sequence). */
+int maple_add_norm_router_topk(const void* x, const void* y, int x_dtype, int64_t row_stride, int64_t tokens, int64_t k,
+                               const void* norm_w, int norm_dtype, float eps, const void* gate, int gate_dtype,
+                               int64_t n_experts, int64_t topk, void* residual_out, void* normed_out, int32_t* idx,
+                               float* wt, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* RMSNorm and residual add + RMSNorm.  Replace kernels/fused_norm.py:105
  * rms_norm and :128 add_rms_norm (residual = x + y, out = norm(residual)). */
 int maple_rms_norm(const void* x, int x_dtype, int64_t rows, int64_t n, int64_t x_row_stride, const void* w,

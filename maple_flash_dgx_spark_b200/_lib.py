@@ -74,6 +74,8 @@ _SIGS: dict[str, tuple] = {
     "maple_moe_reduce_add": (i32, [vp, i32, i64, i64, vp, i64, i64, i64, vp, i64, vp, i64, vp]),
     "maple_router_topk_workspace_bytes": (i64, [i64, i64]),
     "maple_router_topk": (i32, [vp, i32, i64, i64, i64, vp, i32, i64, i64, vp, vp, vp, i64, vp]),
+    "maple_add_norm_router_topk": (i32, [vp, vp, i32, i64, i64, i64, vp, i32, f32, vp, i32, i64, i64, vp, vp, vp, vp,
+                                         vp, i64, vp]),
     "maple_rms_norm": (i32, [vp, i32, i64, i64, i64, vp, i32, f32, vp, i64, vp]),
     "maple_add_rms_norm": (i32, [vp, vp, i32, i64, i64, i64, i64, vp, i32, f32, vp, i64, vp, i64, vp]),
     "maple_apply_qkv_decode": (i32, [vp, i32, i64, i64, vp, vp, i32, vp, vp, i32, i64, i64, vp, i64, i64, vp, vp,

@@ -23,16 +23,27 @@ struct RouterParams {
   float* wt;           // [T, topk]
   float* logits;       // [T, E] scratch
   unsigned* tickets;   // [T]
+  // Fused residual add + RMSNorm in front of the router (FUSE): x is the
+  // residual stream, y the attention output; every CTA forms v = x + y and
+  // the normed row in the add_rms_norm kernel's order, CTA 0 of a token
+  // writes residual_out = v and normed_out, and the logits use the normed row.
+  const void* y;
+  const void* norm_w;
+  void* residual_out;
+  void* normed_out;
   int64_t x_stride;
-  int E, K, topk;
+  int E, K, topk, norm_w_bf16;
+  float eps;
 };
 
 constexpr int kRouterWarps = 8;
 
-template <int XT, int GT>
+template <int XT, int GT, bool FUSE>
 __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
-  extern __shared__ __align__(16) unsigned char rsm[];  // x as fp32 [K] | gate rows raw [8][K]
+  extern __shared__ __align__(16) unsigned char rsm[];  // x as fp32 [K] | gate rows raw [8][K] | (FUSE) y, w [K]
   __shared__ int s_last;
+  __shared__ float s_part[128];
+  __shared__ float s_rstd;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tok = blockIdx.y;
   const int e0 = blockIdx.x * kRouterWarps;
@@ -58,11 +69,51 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
       for (int b = tid; b < nbytes; b += 256) gs[b] = gsrc[b];
     }
   }
+  float* ys = reinterpret_cast<float*>(gs + (size_t)kRouterWarps * p.K * ges);
+  float* ws = ys + p.K;
+  if constexpr (FUSE) {
+    if (p.norm_w_bf16) stage_row<kBF16, 256, 4>(p.norm_w, p.K, ws, tid);
+    else stage_row<kF32, 256, 4>(p.norm_w, p.K, ws, tid);
+  }
   pdl_wait();
   pdl_trigger();
-  const char* xr = static_cast<const char*>(p.x) + tok * p.x_stride * (XT == kBF16 ? 2 : 4);
+  const int es = XT == kBF16 ? 2 : 4;
+  const char* xr = static_cast<const char*>(p.x) + tok * p.x_stride * es;
   stage_row<XT, 256, 2>(xr, p.K, xs, tid);
+  if constexpr (FUSE) stage_row<XT, 256, 2>(static_cast<const char*>(p.y) + tok * p.x_stride * es, p.K, ys, tid);
   __syncthreads();
+  if constexpr (FUSE) {
+    // v = x + y, sum of squares by 128 threads (thread j: elements j, j+128, ...), R128 finish
+    float ss = 0.0f;
+    if (tid < 128) {
+      for (int k = tid; k < p.K; k += 128) {
+        const float v = __fadd_rn(xs[k], ys[k]);
+        ss = __fmaf_rn(v, v, ss);
+      }
+      s_part[tid] = ss;
+    }
+    __syncthreads();
+    if (tid < 32) {
+      const float tot = r128_smem_finish(s_part, tid);
+      if (tid == 0) s_rstd = rstd_of(tot, p.K, p.eps);
+    }
+    __syncthreads();
+    const float rstd = s_rstd;
+    char* res = static_cast<char*>(p.residual_out) + tok * p.x_stride * es;
+    char* nrm = static_cast<char*>(p.normed_out) + tok * p.x_stride * es;
+    for (int k = tid; k < p.K; k += 256) {
+      const float v = __fadd_rn(xs[k], ys[k]);
+      const float nv = __fmul_rn(__fmul_rn(v, rstd), ws[k]);
+      float nq = nv;
+      if constexpr (XT == kBF16) nq = bf16_to_f32(f32_to_bf16(nv));
+      if (blockIdx.x == 0) {
+        store_f<XT>(res, k, v);
+        store_f<XT>(nrm, k, nv);
+      }
+      xs[k] = nq;  // the router reads the stored (rounded) normed row
+    }
+    __syncthreads();
+  }
   if (warp < ne) {
     const unsigned char* gr = gs + (size_t)warp * p.K * ges;
     // Lane l owns R128 partials j = l + 32u (elements j, j+128, ...).
@@ -283,10 +334,10 @@ extern "C" int64_t maple_router_topk_workspace_bytes(int64_t tokens, int64_t n_e
   return kTicketBytesMoe + tokens * n_experts * (int64_t)sizeof(float);
 }
 
-extern "C" int maple_router_topk(const void* x, int x_dtype, int64_t x_row_stride, int64_t tokens,
-                                 int64_t k, const void* gate, int gate_dtype, int64_t n_experts,
-                                 int64_t topk, int32_t* idx, float* wt, void* workspace,
-                                 int64_t workspace_bytes, void* stream) {
+static int router_common(const void* x, int x_dtype, int64_t x_row_stride, int64_t tokens, int64_t k,
+                         const void* gate, int gate_dtype, int64_t n_experts, int64_t topk, int32_t* idx, float* wt,
+                         void* workspace, int64_t workspace_bytes, const void* y, const void* norm_w,
+                         int norm_dtype, float eps, void* residual_out, void* normed_out, void* stream) {
   if (tokens < 0 || k <= 0 || n_experts <= 0 || topk <= 0) return kErrShape;
   if (tokens == 0) return kOk;
   if (topk > n_experts || topk > 32 || n_experts > 256) return kErrShape;
@@ -299,15 +350,29 @@ extern "C" int maple_router_topk(const void* x, int x_dtype, int64_t x_row_strid
   p.tickets = static_cast<unsigned*>(workspace);
   p.logits = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytesMoe);
   p.x_stride = x_row_stride; p.E = (int)n_experts; p.K = (int)k; p.topk = (int)topk;
+  p.y = y; p.norm_w = norm_w; p.norm_w_bf16 = norm_dtype == kBF16; p.eps = eps;
+  p.residual_out = residual_out; p.normed_out = normed_out;
+  if (y != nullptr) {
+    if (!norm_w || !residual_out || !normed_out) return kErrShape;
+    if (norm_dtype != kF32 && norm_dtype != kBF16) return kErrDtype;
+  }
   dim3 grid((unsigned)((n_experts + kRouterWarps - 1) / kRouterWarps), (unsigned)tokens);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const size_t smem = (size_t)k * sizeof(float) + (size_t)kRouterWarps * k * (gate_dtype == kBF16 ? 2 : 4);
+  const bool fuse = p.y != nullptr;
+  const size_t smem = (size_t)k * sizeof(float) + (size_t)kRouterWarps * k * (gate_dtype == kBF16 ? 2 : 4) +
+                      (fuse ? 2 * (size_t)k * sizeof(float) : 0);
   if (smem > 200 * 1024) return kErrShape;
-#define MB_ROUTER(XT, GT)                                                                                 \
-  do {                                                                                                    \
-    if (smem > 32 * 1024)                                                                                 \
-      cudaFuncSetAttribute(router_kernel<XT, GT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    launch_k(router_kernel<XT, GT>, dim3(grid), dim3(256), smem, st, p);                                                    \
+#define MB_ROUTER(XT, GT)                                                                                       \
+  do {                                                                                                          \
+    if (fuse) {                                                                                                 \
+      if (smem > 32 * 1024)                                                                                     \
+        cudaFuncSetAttribute(router_kernel<XT, GT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+      launch_k(router_kernel<XT, GT, true>, dim3(grid), dim3(256), smem, st, p);                               \
+    } else {                                                                                                    \
+      if (smem > 32 * 1024)                                                                                     \
+        cudaFuncSetAttribute(router_kernel<XT, GT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+      launch_k(router_kernel<XT, GT, false>, dim3(grid), dim3(256), smem, st, p);                              \
+    }                                                                                                           \
   } while (0)
   if (x_dtype == kBF16) {
     if (gate_dtype == kBF16) MB_ROUTER(kBF16, kBF16); else MB_ROUTER(kBF16, kF32);
@@ -316,6 +381,24 @@ extern "C" int maple_router_topk(const void* x, int x_dtype, int64_t x_row_strid
   }
 #undef MB_ROUTER
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+extern "C" int maple_router_topk(const void* x, int x_dtype, int64_t x_row_stride, int64_t tokens,
+                                 int64_t k, const void* gate, int gate_dtype, int64_t n_experts,
+                                 int64_t topk, int32_t* idx, float* wt, void* workspace,
+                                 int64_t workspace_bytes, void* stream) {
+  return router_common(x, x_dtype, x_row_stride, tokens, k, gate, gate_dtype, n_experts, topk, idx, wt, workspace,
+                       workspace_bytes, nullptr, nullptr, 0, 0.0f, nullptr, nullptr, stream);
+}
+
+extern "C" int maple_add_norm_router_topk(const void* x, const void* y, int x_dtype, int64_t row_stride,
+                                          int64_t tokens, int64_t k, const void* norm_w, int norm_dtype, float eps,
+                                          const void* gate, int gate_dtype, int64_t n_experts, int64_t topk,
+                                          void* residual_out, void* normed_out, int32_t* idx, float* wt,
+                                          void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!y) return kErrShape;
+  return router_common(x, x_dtype, row_stride, tokens, k, gate, gate_dtype, n_experts, topk, idx, wt, workspace,
+                       workspace_bytes, y, norm_w, norm_dtype, eps, residual_out, normed_out, stream);
 }
 
 namespace {

@@ -382,6 +382,39 @@ def router_topk(x, gate_weight, top_k):
     return idx.reshape(*leading, top_k), wt.reshape(*leading, top_k)
 
 
+def add_rms_norm_router_topk(x, y, norm_weight, eps: float, gate_weight, top_k):
+    """``add_rms_norm`` followed by ``router_topk`` in one launch: returns
+    ``(x + y, rms_norm(x + y) * w, idx, weight)`` with both operators' exact
+    results (reference model.py:498-506 runs them in sequence)."""
+    op = "add_rms_norm_router_topk"
+    require_cuda(op, x, y, norm_weight, gate_weight)
+    if x.shape != y.shape or x.dtype != y.dtype:
+        raise ValueError("x and y must have the same shape and dtype.")
+    n_exp, k_in = gate_weight.shape
+    if x.shape[-1] != k_in or norm_weight.numel() != k_in:
+        raise ValueError(f"hidden size mismatch: x {tuple(x.shape)}, norm {norm_weight.numel()}, gate {k_in}.")
+    if top_k > n_exp:
+        raise ValueError(f"top_k={top_k} exceeds {n_exp} experts.")
+    leading = x.shape[:-1]
+    xm = x.reshape(-1, k_in).contiguous()
+    ym = y.reshape(-1, k_in).contiguous()
+    tokens = xm.shape[0]
+    w = norm_weight.reshape(-1).contiguous()
+    g = gate_weight.contiguous()
+    res = torch.empty_like(xm)
+    normed = torch.empty_like(xm)
+    idx = torch.empty(tokens, top_k, device=x.device, dtype=torch.int32)
+    wt = torch.empty(tokens, top_k, device=x.device, dtype=torch.float32)
+    L = lib()
+    ws = _ws(x.device, L.maple_router_topk_workspace_bytes(tokens, n_exp))
+    check(L.maple_add_norm_router_topk(ptr(xm), ptr(ym), dtype_code(x, op), k_in, tokens, k_in, ptr(w),
+                                       dtype_code(w, op), float(eps), ptr(g), dtype_code(g, op), n_exp, top_k,
+                                       ptr(res), ptr(normed), ptr(idx), ptr(wt), ptr(ws), ws.numel(),
+                                       stream_ptr(x.device)), op)
+    return (res.reshape(x.shape), normed.reshape(x.shape), idx.reshape(*leading, top_k),
+            wt.reshape(*leading, top_k))
+
+
 def rms_norm(x, weight, eps: float = 1e-6):
     """RMSNorm over the last dim (fp32 math, output ``x.dtype``).  Reference kernels/fused_norm.py:105-125."""
     op = "rms_norm"

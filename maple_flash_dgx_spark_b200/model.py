@@ -23,6 +23,7 @@ import torch
 from maple_flash_dgx_spark_b200.kernels import (
     GROUPED_MIN_TOKENS,
     add_rms_norm,
+    add_rms_norm_router_topk,
     apply_qkv_decode,
     attn_split_len,
     decode_gqa_attn,
@@ -236,8 +237,18 @@ class MapleSparseMoeBlock:
         self.top_k = top_k
         self.moe_intermediate = moe_intermediate
 
+    def fused_add_norm(self, hidden, attn_out, norm: "MapleRMSNorm"):
+        """The decoder layer's post-attention add + RMSNorm fused into the
+        router launch; returns the layer output."""
+        residual, normed, idx, wt = add_rms_norm_router_topk(hidden, attn_out, norm.weight, norm.eps,
+                                                             self.gate_weight, self.top_k)
+        return self._experts(normed, idx, wt, residual)
+
     def __call__(self, hidden_states, residual=None):
         idx, wt = router_topk(hidden_states, self.gate_weight, self.top_k)
+        return self._experts(hidden_states, idx, wt, residual)
+
+    def _experts(self, hidden_states, idx, wt, residual):
         tokens = hidden_states.numel() // hidden_states.shape[-1]
         # from a few tokens on, sort the slots by expert once and run each
         # selected expert's weights once over all of its tokens
@@ -256,6 +267,8 @@ class MapleDecoderLayer:
     def __call__(self, hidden, seqlen, row_map, rotary, cache, kv_final=False):
         attn_out = self.self_attn(hidden, seqlen, row_map, rotary, cache, rms_weight=self.input_layernorm.weight,
                                   rms_eps=self.input_layernorm.eps, kv_final=kv_final)
+        if hasattr(self.mlp, "fused_add_norm"):
+            return self.mlp.fused_add_norm(hidden, attn_out, self.post_attention_layernorm)
         hidden, mlp_in = add_rms_norm(hidden, attn_out, self.post_attention_layernorm.weight,
                                       self.post_attention_layernorm.eps)
         return self.mlp(mlp_in, residual=hidden)

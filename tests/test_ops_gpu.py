@@ -313,3 +313,20 @@ def test_row_uniform_per_sequence(cuda, K):
     assert d1[0] == e1[0] and d1[2] == e1[2] and d1[1] != e1[1]
     c = K.RowUniform([7, 8, 9], cuda)
     torch.testing.assert_close(c(), d1, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("T", [1, 5])
+def test_add_norm_router_fused_equals_sequence(cuda, K, T):
+    """The fused add + RMSNorm + router launch returns exactly what
+    add_rms_norm followed by router_topk returns."""
+    rs = rng(60 + T)
+    H, E = 2048, 64
+    x = to_dev(randn_bf(rs, T, H), cuda, torch.bfloat16)
+    y = to_dev(randn_bf(rs, T, H, scale=0.5), cuda, torch.bfloat16)
+    w = to_dev((1 + 0.05 * rs.standard_normal(H)).astype(np.float32), cuda)
+    g = to_dev(randn_bf(rs, E, H, scale=0.02), cuda, torch.bfloat16)
+    res, normed = K.add_rms_norm(x, y, w, 1e-6)
+    idx, wt = K.router_topk(normed, g, 8)
+    r2, n2, i2, w2 = K.add_rms_norm_router_topk(x, y, w, 1e-6, g, 8)
+    for a, b in ((res, r2), (normed, n2), (idx, i2), (wt, w2)):
+        torch.testing.assert_close(a, b, rtol=0, atol=0)
