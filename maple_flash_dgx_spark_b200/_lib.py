@@ -95,6 +95,9 @@ _SIGS: dict[str, tuple] = {
     "maple_fused_sample": (i32, [vp, i32, i64, i64, i64, vp, f32, f32, i64, vp, vp, i64, vp]),
     "maple_embedding": (i32, [vp, i64, vp, i32, i64, i64, vp, i32, i64, vp, vp]),
     "maple_rtn4_embedding": (i32, [vp, i64, vp, vp, vp, i32, i64, i64, i64, vp, i32, i64, vp, vp]),
+    "maple_decode_layers_workspace_bytes": (i64, [i64, i64, i64, i64, i64, i64, i64, i64, i64]),
+    "maple_decode_layers": (i32, [vp, i64, vp, vp, vp, vp, vp, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
+                                  i64, i64, i64, i64, i64, i64, i32, i32, i32, f32, f32, vp, i64, vp, vp]),
     "maple_synth_ternary": (i32, [ctypes.c_uint64, ctypes.c_uint64, i64, vp, vp]),
     "maple_synth_normal": (i32, [ctypes.c_uint64, ctypes.c_uint64, i64, ctypes.c_double, f32, i32, i32, vp, vp]),
     "maple_synth_rtn4_sym": (i32, [ctypes.c_uint64, ctypes.c_uint64, i64, i64, i64, ctypes.c_double, vp, vp, vp]),

@@ -183,10 +183,10 @@ __device__ __forceinline__ uint32_t signed_digits(uint32_t raw) {
   return ((raw | 0x80808080u) - 0x40404040u) ^ 0x80808080u;
 }
 
-// Shift, rstd and digit totals shared by a block.
+// Shift, rstd and digit totals shared by a block (up to 16 warps).
 struct FxaBlock {
-  unsigned amax[8];
-  int rawsum[8][4];
+  unsigned amax[16];
+  int rawsum[16][4];
   int s;
   float rstd;
   int tot[4];  // sum over the fragment's codes of digit j (balanced)
