@@ -55,7 +55,8 @@ namespace mb {
 
 constexpr int kStepThreads = 256;
 constexpr int kStepWarps = kStepThreads / 32;
-constexpr int kStepNI = 8;         // K iterations per warp held in registers
+constexpr int kStepNI = 8;         // K iterations per warp held in registers (down phase)
+constexpr int kQkvTpw = 2, kOTpw = 1, kSwTpw = 2;  // 16-row tiles per warp in the split-K phases
 constexpr int kStepMaxTopk = 8;
 constexpr int kStepMaxG = 8;       // query heads per KV head
 constexpr int kStepMaxE = 256;
@@ -74,24 +75,27 @@ struct StepParams {
   int H, Hq, Hkv, D, R, E, topk, I, T, Bc, P, NS;
   int64_t kc_sb, kc_sh;        // cache strides (elements), identical for K and V
   float eps, scale;
-  int wm_qkv, wm_o, wm_sw;     // row tiles per item of the QKV, O and SwiGLU phases
+  int qkv_nks, qkv_ipw, o_nks, o_ipw, sw_nks, sw_ipw;  // split-K slices and iterations per slice
   // scratch
-  uint16_t* qkv;               // [(Hq + 2 Hkv) D]
+  unsigned long long* qkv_sum; // [(Hq + 2 Hkv) D] exact int64 row sums, zero between uses
+  unsigned long long* o_sum;   // [H]
+  unsigned long long* sw_sum;  // [topk, 2 I]
+  uint16_t* ybuf;              // [topk, H] expert outputs of the down projection
+  float* meta;                 // [0] QKV shift (int), [1] rstd, [2] O shift (int), [3] SwiGLU shift (int)
   uint16_t* attn;              // [Hq D]
-  uint16_t* o;                 // [H]
   uint16_t* resid;             // [H]
   uint16_t* normed;            // [H]
-  uint16_t* hact;              // [topk, I]
   float* logits;               // [E]
   float* att_acc;              // [Hq, NS, D]
   float* att_ml;               // [Hq, NS, 2]
   unsigned* sync;              // [0] barrier arrivals, [1] CTAs retired, [2] trace switch
-  int64_t* trace;              // [n_layers * 6][2][grid] barrier arrival / release times (ns), then checkpoints
+  int64_t* trace;              // [n_layers * 6 + 1][2][grid] barrier arrival / release times (ns), then checkpoints
   int64_t trace_bytes;
   unsigned* att_tickets;       // [Hkv]
   int* err;
   // dynamic shared memory carve-up (bytes)
   int off_frag, off_xs, off_xr, off_att, off_layers, off_in, off_post, off_qn, off_kn, off_cos, off_sin, off_gate;
+  int frag_entries;
 };
 
 __device__ __forceinline__ float ldf(const void* p, int64_t i, int f32) {
@@ -142,6 +146,9 @@ __device__ __forceinline__ bool grid_barrier(const StepParams& p, unsigned& epoc
   ++epoch;
   if (threadIdx.x == 0 && *s_ok) {
     if (trace != nullptr) trace[blockIdx.x] = global_ns();
+    // the CTA's writes and reductions before the barrier are visible to every
+    // CTA after it (the fence after bar.sync covers the whole CTA)
+    __threadfence();
     red_release_add(&p.sync[0], 1u);
     const unsigned target = epoch * gridDim.x;
     bool done = false;
@@ -231,12 +238,56 @@ __device__ __forceinline__ int amax_exchange(StepShared& S, unsigned amax) {
   return fxa_shift(a);
 }
 
-// Fragments of codes [0, iters*256) of xs (n values) by threads t_local of
-// nt (a multiple of 32) and each warp's raw digit sums in S.fb.rawsum.
+// Staged activations live in shared memory at pidx(k) = k + k/32: the
+// fragment builder's reads (8 codes at stride 4 from 16-code groups 64
+// apart) and the stagers' 8-consecutive-value writes then meet at most two
+// accesses per bank.
+__device__ __forceinline__ int pidx(int k) { return k + (k >> 5); }
+__host__ __device__ constexpr int padded_len(int n) { return n + (n >> 5) + 1; }
+
+// fxa_build's fragment entries (2-bit layout) from xs stored at pidx(k).
+// Each thread owns whole combos (8 codes x 4 digits); it writes the digits
+// in an order rotated by m & 3 so a warp's 8-byte stores spread over the
+// banks.  Only the digit half of an entry is written: the zero half (B
+// columns 4-7) is cleared once per launch and never written again.
+__device__ __forceinline__ void build_frag2(const float* xs, int n, int s, bool bad, int iters, uint2* frag,
+                                            int t_local, int nt, int (&raws)[4]) {
+  constexpr int off[8] = {0, 4, 8, 12, 1, 5, 9, 13};
+  for (int c = t_local; c < iters * 32; c += nt) {
+    const int it = c >> 5, r = c & 31;
+    const int m = r >> 2, t = r & 3;
+    const int k0 = it * 256 + 16 * (4 * t + (m >> 1)) + 2 * (m & 1);
+    uint32_t u[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int k = k0 + off[e];
+      const int X = (k < n && !bad) ? fxa_enc(xs[pidx(k)], s) : 0;
+      u[e] = static_cast<uint32_t>(X + kFxaOffset);
+    }
+    uint2* dst = frag + (it * 8 + m) * 32 + t;
+    const int rot = m & 3;
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = (jj + rot) & 3;
+      const uint32_t w0 = raw_digits(u[0], u[1], u[2], u[3], j);
+      const uint32_t w1 = raw_digits(u[4], u[5], u[6], u[7], j);
+      const int add = static_cast<int>(__dp4a(w0, 0x01010101u, __dp4a(w1, 0x01010101u, 0u)));
+      raws[0] += j == 0 ? add : 0;
+      raws[1] += j == 1 ? add : 0;
+      raws[2] += j == 2 ? add : 0;
+      raws[3] += j == 3 ? add : 0;
+      dst[4 * j] = make_uint2(signed_digits(w0), signed_digits(w1));
+    }
+  }
+}
+
+// Fragments of codes [0, iters*256) of xs (n values at pidx) by threads
+// t_local of nt (a multiple of 32) and each warp's raw digit sums in
+// S.fb.rawsum.
 __device__ __forceinline__ void build_frags(StepShared& S, const float* xs, int n, int s, int iters, uint2* frag,
                                             int t_local, int nt) {
   int raws[4] = {0, 0, 0, 0};
-  fxa_build<2>(xs, n, s, s == kFxaNonFinite, iters, frag, t_local, nt, raws);
+  build_frag2(xs, n, s, s == kFxaNonFinite, iters, frag, t_local, nt, raws);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -276,131 +327,295 @@ __device__ __forceinline__ void load_tile(const uint32_t* codes, int row_g, int 
   }
 }
 
-// ------------------------------------------------------------ dense GEMV --
-// y[n] = bf16(fxa(S_n) [* rstd] * alpha[n]) for n < N over the activation x
-// (bf16, K elements), with the input RMSNorm folded in when rms_w (staged in
-// shared memory) is given.  Same arithmetic as tgemv2_kernel.  Items: 16*WM
-// rows; the 8 warps are WM row tiles x (8/WM) K slices whose exact int32
-// partials add up in shared memory.  The activation is read once (one L2
-// round trip); the RMS partial sums run between the two prologue barriers.
-template <int NI>
-__device__ __forceinline__ void dense_gemv(StepShared& S, const StepSmem& M, const void* x, const void* rms_w,
-                                           int norm_f32, float eps, const uint32_t* codes, const void* alpha,
-                                           int alpha_f32, uint16_t* y, int N, int K, int WM) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
-  const int WK = kStepWarps / WM;
-  const int wm = warp % WM, wk = warp / WM;
-  const int nwords = K / 16, iters_total = (nwords + 15) / 16;
-  const int ipw = (iters_total + WK - 1) / WK;
-  const int it0 = wk * ipw, my_iters = max(0, min(ipw, iters_total - it0));
-  const int per_item = 16 * WM, n_items = (N + per_item - 1) / per_item;
-  const bool rms = rms_w != nullptr;
-  bool first = true;
-  int s = 0;
-  int tot[4] = {0, 0, 0, 0};
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-    const int row_g = item * per_item + 16 * wm + g, row_h = row_g + 8;
-    const bool ok_g = row_g < N, ok_h = row_h < N;
-    uint4 wa[NI], wb[NI];
-    load_tile(codes, row_g, row_h, ok_g, ok_h, nwords, it0, my_iters, t, wa, wb);
-    tmark(S, 1);
-    if (first) {
-      // stage x (8 values per 16-byte chunk), x_hat = x * w, local |x_hat| max
-      const int nch = K / 8;
-      uint4 r[4];
+// ------------------------------------------------------- split-K GEMV ----
+// The packed GEMVs of a layer run split-K over CTAs: an item is a block of
+// rows and a K slice of `ipw` iterations (256 codes each).  A CTA reads the
+// whole activation row (the FXA shift needs max|x| over all of K) but
+// encodes only its slice, contracts its rows against it, and adds the exact
+// partial sums S_slice = sum_j 128^j (acc_j - tot_j) to an int64 accumulator
+// per row with atomics: the total is the exact integer contraction whatever
+// the split, so the phase that reads a row finishes it exactly as the
+// single-CTA kernels do (fxa_value(S, s) [* rstd] * alpha).  The producer's
+// CTA 0 publishes the shift (and rstd) in p.meta.
+struct SplitGeom {
+  int tpw, nks, ipw;  // tiles of 16 rows per warp, K slices, iterations per slice
+  __device__ int rows_per_item() const { return kStepWarps * tpw * 16; }
+};
+
+// Stage this thread's chunks of the activation (8 values per chunk): values
+// of the slice [k0, k0 + n_slice) go to M.xs at pidx(k - k0); returns the
+// thread's max |x|.  fetch(c, v) fills chunk c's 8 values.
+template <typename Fetch>
+__device__ __forceinline__ unsigned stage_slice(const StepSmem& M, int K, int k0, int n_slice, Fetch fetch) {
+  unsigned amax = 0;
+  for (int c = threadIdx.x; c < K / 8; c += kStepThreads) {
+    float v[8];
+    fetch(c, v);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (tid + i * kStepThreads < nch) r[i] = ld_u4(static_cast<const char*>(x) + (size_t)(tid + i * kStepThreads) * 16);
-      unsigned amax = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int c = tid + i * kStepThreads;
-        if (c < nch) {
-          float v[8];
-          widen_u4<kBF16>(r[i], v);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int k = c * 8 + e;
-            float h = v[e];
-            if (rms) {
-              M.xr[k] = v[e];
-              h = __fmul_rn(v[e], ldf(rms_w, k, norm_f32));
-            }
-            M.xs[k] = h;
-            amax = max(amax, __float_as_uint(h) & 0x7fffffffu);
-          }
-        }
-      }
-      s = amax_exchange(S, amax);
-      if (rms && tid < 128) {
-        float ss = 0.0f;
-        for (int k = tid; k < K; k += 128) ss = __fmaf_rn(M.xr[k], M.xr[k], ss);
-        S.part[0][tid] = ss;
-      }
-      build_frags(S, M.xs, K, s, iters_total, M.frag, tid, kStepThreads);
-      __syncthreads();
-      digit_totals(S, iters_total, tot);
-      first = false;
+    for (int e = 0; e < 8; ++e) {
+      const int k = c * 8 + e;
+      amax = max(amax, __float_as_uint(v[e]) & 0x7fffffffu);
+      if (k >= k0 && k < k0 + n_slice) M.xs[pidx(k - k0)] = v[e];
     }
-    tmark(S, 2);
+  }
+  return amax;
+}
+
+// Contract this warp's TPW row tiles (code rows row_of(j) + g, + 8) over the
+// slice's fragments and add the exact partial sums to sums[out_row(j) + ...].
+template <int TPW, int NI, typename RowOf, typename OutOf>
+__device__ __forceinline__ void splitk_contract(const StepSmem& M, const uint32_t* codes, int nwords, int it0,
+                                                int n_it, const int (&tot)[4], RowOf row_of, OutOf out_of,
+                                                unsigned long long* sums) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  uint4 wa[TPW][NI], wb[TPW][NI];
+#pragma unroll
+  for (int j = 0; j < TPW; ++j) {
+    const int r = row_of(j);
+    load_tile<NI>(codes, r + g, r + g + 8, r >= 0, r >= 0, nwords, it0, n_it, t, wa[j], wb[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < TPW; ++j) {
     int acc[4] = {0, 0, 0, 0};
-    contract_tile2<NI>(wa, wb, my_iters, M.frag + (size_t)it0 * 256, lane, acc);
-    if (wk > 0) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) S.red[(wk - 1) * WM + wm][lane][j] = acc[j];
+    contract_tile2<NI>(wa[j], wb[j], n_it, M.frag, lane, acc);
+    long long Sg, Sh;
+    combine_digits(acc, tot, t, Sg, Sh);
+    const int o = out_of(j);
+    if (t == 0 && o >= 0 && row_of(j) >= 0) {
+      atomicAdd(&sums[o + g], static_cast<unsigned long long>(Sg));
+      atomicAdd(&sums[o + g + 8], static_cast<unsigned long long>(Sh));
     }
-    __syncthreads();
-    tmark(S, 3);
-    if (wk == 0) {
-      for (int w2 = 1; w2 < WK; ++w2)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[j] += S.red[(w2 - 1) * WM + wm][lane][j];
-      long long Sg, Sh;
-      combine_digits(acc, tot, t, Sg, Sh);
-      const float rstd = rms ? rstd_of(r128_smem_finish(S.part[0], lane), K, eps) : 1.0f;
-      if (t == 0) {
-        const bool nan_out = (s == kFxaNonFinite);
-        auto value = [&](int row, long long Sv) -> float {
-          float v = nan_out ? __int_as_float(0x7fc00000) : fxa_value(Sv, s);
-          if (rms) v = __fmul_rn(v, rstd);
-          return __fmul_rn(v, ldf(alpha, row, alpha_f32));
-        };
-        if (ok_g) y[row_g] = f32_to_bf16(value(row_g, Sg));
-        if (ok_h) y[row_h] = f32_to_bf16(value(row_h, Sh));
-      }
-    }
-    __syncthreads();
-    tmark(S, 4);
   }
 }
 
-// -------------------------------------------------------------- SwiGLU ----
+// Exact value of a finished row: fxa_value(S, s) (NaN when the activation
+// was not finite) -- the value tgemv2_kernel computes before its scalings.
+__device__ __forceinline__ float fxa_row(long long S, int s) {
+  return s == kFxaNonFinite ? __int_as_float(0x7fc00000) : fxa_value(S, s);
+}
+
+__device__ __forceinline__ void zero_share(unsigned long long* p, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * kStepThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kStepThreads)
+    p[i] = 0ull;
+}
+
+// -------------------------------------------------------------- QKV ----
+// x = this layer's input: the previous layer's down outputs combined in slot
+// order with the residual, x[k] = bf16(fmaf-chain_s(w_s, y_s[k]) +
+// resid[k]) (down_sum_kernel MODE 0 / moe_reduce_add), or the embedded token
+// for layer 0.  Every CTA forms x (CTA 0 stores it); then the RMSNorm-folded
+// QKV GEMV, split-K, into p.qkv_sum; CTA 0 publishes the shift and rstd.
+template <int TPW>
+__device__ __forceinline__ void qkv_phase(StepShared& S, const StepSmem& M, const StepParams& p,
+                                          const maple_decode_layer& w, bool first_layer) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int K = p.H, N = (p.Hq + 2 * p.Hkv) * p.D;
+  const SplitGeom G{TPW, p.qkv_nks, p.qkv_ipw};
+  const int nwords = K / 16, iters_total = (nwords + 15) / 16;
+  const int n_rb = (N + G.rows_per_item() - 1) / G.rows_per_item();
+  const int n_items = n_rb * G.nks;
+  const int item = blockIdx.x;
+  const bool has_item = item < n_items;
+  const int rb = item / G.nks, ks = item % G.nks;
+  const int it0 = ks * G.ipw, n_it = max(0, min(G.ipw, iters_total - it0));
+  const int k0 = it0 * 256, n_slice = min(K, (it0 + n_it) * 256) - k0;
+  if (!has_item && blockIdx.x != 0) return;
+  // x, x_hat = x * w_in; raw x to xr for the RMS partials
+  auto fetch = [&](int c, float (&v)[8]) {
+    float xv[8];
+    if (first_layer) {
+      widen_u4<kBF16>(ld_u4(reinterpret_cast<const char*>(p.x) + (size_t)c * 16), xv);
+    } else {
+      uint4 yr[kStepMaxTopk];
+#pragma unroll
+      for (int s = 0; s < kStepMaxTopk; ++s)
+        if (s < p.topk) yr[s] = ld_u4(reinterpret_cast<const char*>(p.ybuf + (int64_t)s * p.H) + (size_t)c * 16);
+      float rv[8];
+      widen_u4<kBF16>(ld_u4(reinterpret_cast<const char*>(p.resid) + (size_t)c * 16), rv);
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < kStepMaxTopk; ++s) {
+        if (s < p.topk) {
+          float yv[8];
+          widen_u4<kBF16>(yr[s], yv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(S.wts[s], yv[e], acc[e]);
+        }
+      }
+      uint32_t q[4];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint16_t b = f32_to_bf16(__fadd_rn(acc[e], rv[e]));
+        xv[e] = bf16_to_f32(b);
+        if (e & 1) q[e >> 1] |= static_cast<uint32_t>(b) << 16;
+        else q[e >> 1] = b;
+      }
+      if (blockIdx.x == 0)
+        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.x) + (size_t)c * 16) = make_uint4(q[0], q[1], q[2], q[3]);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int k = c * 8 + e;
+      M.xr[k] = xv[e];
+      v[e] = __fmul_rn(xv[e], ldf(M.in_norm, k, p.norm_f32));
+    }
+  };
+  const unsigned amax = stage_slice(M, K, k0, n_slice, fetch);
+  if (!has_item) return;  // CTA 0 without an item has stored x
+  const int s = amax_exchange(S, amax);
+  if (tid < 128) {
+    float ss = 0.0f;
+    for (int k = tid; k < K; k += 128) ss = __fmaf_rn(M.xr[k], M.xr[k], ss);
+    S.part[0][tid] = ss;
+  }
+  build_frags(S, M.xs, n_slice, s, n_it, M.frag, tid, kStepThreads);
+  __syncthreads();
+  int tot[4];
+  digit_totals(S, n_it, tot);
+  if (blockIdx.x == 0 && warp == 0) {
+    const float rstd = rstd_of(r128_smem_finish(S.part[0], tid & 31), K, p.eps);
+    if (tid == 0) {
+      reinterpret_cast<int*>(p.meta)[0] = s;
+      p.meta[1] = rstd;
+    }
+  }
+  tmark(S, 2);
+  const int base = rb * G.rows_per_item() + warp * TPW * 16;
+  splitk_contract<TPW, 4>(M, w.qkv_codes, nwords, it0, n_it, tot,
+                          [&](int j) { const int r = base + 16 * j; return r < N ? r : -1; },
+                          [&](int j) { return base + 16 * j; }, p.qkv_sum);
+}
+
+// ---------------------------------------------------------------- O ----
+// The attention output (bf16 [Hq D]) against the O rows, split-K into
+// p.o_sum; CTA 0 publishes the shift.  Also clears the QKV accumulators the
+// attention phase has finished reading.
+template <int TPW>
+__device__ __forceinline__ void o_phase(StepShared& S, const StepSmem& M, const StepParams& p,
+                                        const maple_decode_layer& w) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  zero_share(p.qkv_sum, (int64_t)(p.Hq + 2 * p.Hkv) * p.D);
+  const int K = p.Hq * p.D, N = p.H;
+  const SplitGeom G{TPW, p.o_nks, p.o_ipw};
+  const int nwords = K / 16, iters_total = (nwords + 15) / 16;
+  const int n_rb = (N + G.rows_per_item() - 1) / G.rows_per_item();
+  const int item = blockIdx.x;
+  if (item >= n_rb * G.nks) return;
+  const int rb = item / G.nks, ks = item % G.nks;
+  const int it0 = ks * G.ipw, n_it = max(0, min(G.ipw, iters_total - it0));
+  const int k0 = it0 * 256, n_slice = min(K, (it0 + n_it) * 256) - k0;
+  const unsigned amax = stage_slice(M, K, k0, n_slice, [&](int c, float (&v)[8]) {
+    widen_u4<kBF16>(ld_u4(reinterpret_cast<const char*>(p.attn) + (size_t)c * 16), v);
+  });
+  const int s = amax_exchange(S, amax);
+  build_frags(S, M.xs, n_slice, s, n_it, M.frag, tid, kStepThreads);
+  __syncthreads();
+  int tot[4];
+  digit_totals(S, n_it, tot);
+  if (blockIdx.x == 0 && tid == 0) reinterpret_cast<int*>(p.meta)[2] = s;
+  tmark(S, 2);
+  const int base = rb * G.rows_per_item() + warp * TPW * 16;
+  splitk_contract<TPW, 4>(M, w.o_codes, nwords, it0, n_it, tot,
+                          [&](int j) { const int r = base + 16 * j; return r < N ? r : -1; },
+                          [&](int j) { return base + 16 * j; }, p.o_sum);
+}
+
+// ----------------------------------------------------------- router ----
+// o[k] = bf16(fxa_value(S_o[k], s_o) * alpha_o[k]); v = x + o; CTA 0 stores
+// resid = bf16(v) and normed = bf16(v * rstd * w); logits[e] = R128
+// dot(bf16(normed), gate[e]) (router_kernel<FUSE>).  One item per CTA: 2
+// experts; warp (e_local = w / 4, q = w % 4) owns R128 partials 32q + lane.
+// The norm weights and this CTA's gate rows were staged before the barrier.
+__device__ __forceinline__ void router_phase(StepShared& S, const StepSmem& M, const StepParams& p,
+                                             const maple_decode_layer& w) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = p.H;
+  const int n_items = (p.E + kRouterExpertsPerItem - 1) / kRouterExpertsPerItem;
+  if ((int)blockIdx.x >= n_items) return;
+  float* vs = M.xr;  // x + o, fp32
+  float* xs = M.xs;  // bf16(normed), fp32 at pidx
+  const int s_o = __ldcg(reinterpret_cast<const int*>(p.meta) + 2);
+  for (int c = tid; c < K / 8; c += kStepThreads) {
+    float a[8];
+    widen_u4<kBF16>(ld_u4(reinterpret_cast<const char*>(p.x) + (size_t)c * 16), a);
+    long long so[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) so[e] = static_cast<long long>(__ldcg(p.o_sum + c * 8 + e));
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int k = c * 8 + e;
+      const float ov = bf16_round(__fmul_rn(fxa_row(so[e], s_o), ldf(w.o_alpha, k, p.alpha_f32)));
+      vs[k] = __fadd_rn(a[e], ov);
+    }
+  }
+  __syncthreads();
+  tmark(S, 1);
+  if (tid < 128) {
+    float ss = 0.0f;
+    for (int k = tid; k < K; k += 128) ss = __fmaf_rn(vs[k], vs[k], ss);
+    S.part[0][tid] = ss;
+  }
+  __syncthreads();
+  const float rstd = rstd_of(r128_smem_finish(S.part[0], lane), K, p.eps);
+  tmark(S, 2);
+  for (int c = tid; c < K / 8; c += kStepThreads) {
+    uint32_t rq[4], nq[4];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int k = c * 8 + e;
+      const float v = vs[k];
+      const float nv = __fmul_rn(__fmul_rn(v, rstd), ldf(M.post_norm, k, p.norm_f32));
+      const uint16_t nb = f32_to_bf16(nv);
+      xs[pidx(k)] = bf16_to_f32(nb);
+      const uint16_t vb = f32_to_bf16(v);
+      if (e & 1) {
+        rq[e >> 1] |= static_cast<uint32_t>(vb) << 16;
+        nq[e >> 1] |= static_cast<uint32_t>(nb) << 16;
+      } else {
+        rq[e >> 1] = vb;
+        nq[e >> 1] = nb;
+      }
+    }
+    if (blockIdx.x == 0) {
+      *reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.resid) + (size_t)c * 16) = make_uint4(rq[0], rq[1], rq[2], rq[3]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.normed) + (size_t)c * 16) = make_uint4(nq[0], nq[1], nq[2], nq[3]);
+    }
+  }
+  __syncthreads();
+  tmark(S, 3);
+  const int el = warp / 4, q = warp % 4;
+  const int e = blockIdx.x * kRouterExpertsPerItem + el;
+  if (e < p.E) {
+    const int j = 32 * q + lane;
+    float pj = 0.0f;
+#pragma unroll 4
+    for (int k = j; k < K; k += 128) pj = __fmaf_rn(xs[pidx(k)], ldf(M.gate, (int64_t)el * K + k, p.gate_f32), pj);
+    S.part[el][j] = pj;
+  }
+  __syncthreads();
+  if (q == 0 && e < p.E) {
+    const float logit = r128_smem_finish(S.part[el], lane);
+    if (lane == 0) p.logits[e] = logit;
+  }
+  tmark(S, 4);
+}
+
+// ------------------------------------------------------------ SwiGLU ----
 // Every CTA: softmax + top-k + renorm of the E logits (router_kernel's
-// last-CTA part).  The order of its repeated argmax (largest first, ties to
-// the lowest index) is each expert's rank, one thread per expert.  Then
-// h[slot, n] = bf16(clamp(u, +-7) * min(g, 7) * sigmoid(min(g, 7))) with u, g
-// the up / gate rows of expert ids[slot] (tgemv2_kernel<kSwiglu>).  Items:
-// (slot, 8*WM outputs); warps wm < WM/2 take up rows, the rest gate rows.
-// The down rows of this CTA's down item go to L2 as soon as the experts are
-// known.
+// last-CTA part; the order of its repeated argmax, largest first and ties to
+// the lowest index, is each expert's rank, one thread per expert).  Then the
+// up|gate rows of the selected experts against bf16(normed), split-K into
+// p.sw_sum[slot][2I]; CTA 0 publishes the shift.  The down rows of this CTA's
+// down item go to L2 once the experts are known; the O accumulators are
+// cleared.
+template <int TPW>
 __device__ __forceinline__ void swiglu_phase(StepShared& S, const StepSmem& M, const StepParams& p,
                                              const maple_decode_layer& w) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
-  const int WM = p.wm_sw, WK = kStepWarps / WM;
-  const int wm = warp % WM, wk = warp / WM;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = p.H, I = p.I, E = p.E;
-  const int nwords = K / 16, iters_total = (nwords + 15) / 16;
-  const int ipw = (iters_total + WK - 1) / WK;
-  const int it0 = wk * ipw, my_iters = max(0, min(ipw, iters_total - it0));
-  const int outs = 8 * WM, nblk = (I + outs - 1) / outs, n_items = p.topk * nblk;
-  const int64_t expert_words = (int64_t)2 * I * nwords;
   const float ninf = __int_as_float(0xff800000);
-  // 1. the normed row (all) and the logits (warp 0) in one round trip
-  const int nch = K / 8;
-  uint4 r[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    if (tid + i * kStepThreads < nch) r[i] = ld_u4(reinterpret_cast<const char*>(p.normed) + (size_t)(tid + i * kStepThreads) * 16);
+  zero_share(p.o_sum, p.H);
+  // 1. the logits (warp 0) -> probabilities
   if (warp == 0) {
     float v[kStepMaxE / 32];
     float m = ninf;
@@ -433,22 +648,25 @@ __device__ __forceinline__ void swiglu_phase(StepShared& S, const StepSmem& M, c
       S.tk_sel_i[lane] = 0x7fffffff;
     }
   }
+  // 2. this CTA's slice of bf16(normed) while warp 0 works
+  const SplitGeom G{TPW, p.sw_nks, p.sw_ipw};
+  const int nwords = K / 16, iters_total = (nwords + 15) / 16;
+  const int rpi = G.rows_per_item();       // code rows per item: rpi/2 up rows + rpi/2 gate rows
+  const int outs = rpi / 2;
+  const int n_ob = (I + outs - 1) / outs;
+  const int n_items = p.topk * n_ob * G.nks;
+  const int item = blockIdx.x;
+  const bool has_item = item < n_items;
+  const int slot = item / (n_ob * G.nks), ob = (item / G.nks) % n_ob, ks = item % G.nks;
+  const int it0 = ks * G.ipw, n_it = max(0, min(G.ipw, iters_total - it0));
+  const int k0 = it0 * 256, n_slice = min(K, (it0 + n_it) * 256) - k0;
   unsigned amax = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c = tid + i * kStepThreads;
-    if (c < nch) {
-      float v[8];
-      widen_u4<kBF16>(r[i], v);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        M.xs[c * 8 + e] = v[e];
-        amax = max(amax, __float_as_uint(v[e]) & 0x7fffffffu);
-      }
-    }
-  }
+  if (has_item)
+    amax = stage_slice(M, K, k0, n_slice, [&](int c, float (&v)[8]) {
+      widen_u4<kBF16>(ld_u4(reinterpret_cast<const char*>(p.normed) + (size_t)c * 16), v);
+    });
   const int s = amax_exchange(S, amax);  // also publishes the probabilities
-  // 2. rank of expert tid (NaN is never picked by the argmax rounds)
+  // 3. rank of expert tid (NaN is never picked by the argmax rounds)
   if (tid < E) {
     const float pi = S.tk_p[tid];
     if (pi == pi) {
@@ -464,6 +682,7 @@ __device__ __forceinline__ void swiglu_phase(StepShared& S, const StepSmem& M, c
       }
     }
   }
+  if (has_item) build_frags(S, M.xs, n_slice, s, n_it, M.frag, tid, kStepThreads);
   __syncthreads();
   float total = 0.0f;
   for (int rr = 0; rr < p.topk; ++rr) total = __fadd_rn(total, S.tk_sel_p[rr]);
@@ -472,272 +691,130 @@ __device__ __forceinline__ void swiglu_phase(StepShared& S, const StepSmem& M, c
     S.ids[tid] = S.tk_sel_i[tid];
     S.wts[tid] = __fmul_rn(S.tk_sel_p[tid], inv);
   }
+  if (blockIdx.x == 0 && tid == 0) reinterpret_cast<int*>(p.meta)[3] = s;
   tmark(S, 1);
-  // 3. this CTA's down rows into L2 (slot = warp, one 128-byte line per lane)
+  // 4. this CTA's down rows into L2: down item = (slot, 128 rows)
   {
-    const int64_t row_bytes = (int64_t)I / 4;
-    const int n_down = (p.H + 15) / 16;
-    if (warp < p.topk && (int)blockIdx.x < n_down) {
-      const int e = S.tk_sel_i[warp];
+    const int n_db = (p.H + 127) / 128;
+    const int ditem = blockIdx.x;
+    if (ditem < p.topk * n_db) {
+      const int dslot = ditem / n_db, r0 = (ditem % n_db) * 128;
+      const int e = S.tk_sel_i[dslot];
       if (e >= 0 && e < E) {
-        const int r0 = blockIdx.x * 16;
-        const int64_t bytes = min(16, p.H - r0) * row_bytes;
+        const int64_t row_bytes = (int64_t)I / 4;
+        const int64_t bytes = min(128, p.H - r0) * row_bytes;
         const char* base = reinterpret_cast<const char*>(w.dn_codes) + ((int64_t)e * p.H + r0) * row_bytes;
-        for (int64_t off = (int64_t)lane * 128; off < bytes; off += 32 * 128) prefetch_l2(base + off);
+        for (int64_t off = (int64_t)tid * 128; off < bytes; off += (int64_t)kStepThreads * 128) prefetch_l2(base + off);
       }
     }
   }
-  // 4. expert rows, then the fragments while they arrive
-  bool first = true;
-  int tot[4] = {0, 0, 0, 0};
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-    const int slot = item / nblk, n0 = (item % nblk) * outs;
-    int e = S.tk_sel_i[slot];
-    const bool bad_id = (e < 0 || e >= E);
-    if (bad_id) e = 0;
-    const uint32_t* codes = w.ug_codes + (int64_t)e * expert_words;
-    const int base = (wm < WM / 2) ? 0 : I;
-    const int tile0 = base + n0 + 16 * ((wm < WM / 2) ? wm : wm - WM / 2);
-    const int row_g = tile0 + g, row_h = row_g + 8;
-    const bool ok_g = row_g < base + I, ok_h = row_h < base + I;
-    uint4 wa[kStepNI], wb[kStepNI];
-    load_tile(codes, row_g, row_h, ok_g, ok_h, nwords, it0, my_iters, t, wa, wb);
-    tmark(S, 2);
-    if (first) {
-      build_frags(S, M.xs, K, s, iters_total, M.frag, tid, kStepThreads);
-      __syncthreads();
-      digit_totals(S, iters_total, tot);
-      first = false;
-    }
-    tmark(S, 3);
-    int acc[4] = {0, 0, 0, 0};
-    contract_tile2<kStepNI>(wa, wb, my_iters, M.frag + (size_t)it0 * 256, lane, acc);
-    if (wk > 0) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) S.red[(wk - 1) * WM + wm][lane][j] = acc[j];
-    }
-    if (WK > 1) __syncthreads();
-    tmark(S, 4);
-    if (wk == 0) {
-      for (int w2 = 1; w2 < WK; ++w2)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[j] += S.red[(w2 - 1) * WM + wm][lane][j];
-      long long Sg, Sh;
-      combine_digits(acc, tot, t, Sg, Sh);
-      if (t == 0) {
-        const bool nan_out = (s == kFxaNonFinite) || bad_id;
-        const void* al = static_cast<const char*>(w.ug_alpha) + (int64_t)e * 2 * I * (p.alpha_f32 ? 4 : 2);
-        auto value = [&](int row, long long Sv) -> float {
-          const float v = nan_out ? __int_as_float(0x7fc00000) : fxa_value(Sv, s);
-          return __fmul_rn(v, ldf(al, row, p.alpha_f32));
-        };
-        S.s_val[16 * wm + g] = ok_g ? value(row_g, Sg) : 0.0f;
-        S.s_val[16 * wm + g + 8] = ok_h ? value(row_h, Sh) : 0.0f;
-      }
-    }
-    __syncthreads();
-    if (tid < outs) {
-      const int n = n0 + tid;
-      if (n < I) {
-        float up = S.s_val[tid], gate = S.s_val[outs + tid];
-        up = fminf(fmaxf(up, -7.0f), 7.0f);
-        gate = fminf(gate, 7.0f);
-        p.hact[(int64_t)slot * I + n] = f32_to_bf16(__fmul_rn(__fmul_rn(up, gate), msigmoid(gate)));
-      }
-    }
-    __syncthreads();
-    tmark(S, 5);
-  }
+  if (!has_item) return;
+  int tot[4];
+  digit_totals(S, n_it, tot);
+  tmark(S, 2);
+  int e = S.tk_sel_i[slot];
+  if (e < 0 || e >= E) e = 0;  // a bad id finishes as NaN in the down phase
+  const uint32_t* codes = w.ug_codes + (int64_t)e * 2 * I * nwords;
+  // warp's local rows [warp * TPW * 16, +TPW*16): the first half of the item's rows are up rows, the rest gate rows
+  const int lbase = warp * TPW * 16;
+  auto code_row = [&](int j) {
+    const int lr = lbase + 16 * j;
+    const int r = lr < outs ? ob * outs + lr : I + ob * outs + (lr - outs);
+    const int lim = lr < outs ? I : 2 * I;
+    return r < lim ? r : -1;
+  };
+  splitk_contract<TPW, 4>(M, codes, nwords, it0, n_it, tot, code_row,
+                          [&](int j) { return slot * 2 * I + code_row(j); }, p.sw_sum);
 }
 
-// ---------------------------------------------------------------- down ----
-// out[n] = bf16(fmaf-chain_slot(w_slot, bf16(alpha_e[n] * S_slot[n])) +
-// residual[n]) (down_sum_kernel MODE 0).  Warp `slot` encodes that slot's
-// activation row itself (no block barrier) and contracts the item's 16 rows
-// of expert ids[slot] against it; the weighted combine adds the slots in
-// order.
+// -------------------------------------------------------------- down ----
+// Item (slot, 128 rows): h = bf16(clamp(u, +-7) * min(g, 7) * sigmoid(min(g,
+// 7))) with u, g the finished up / gate rows of the slot's expert
+// (tgemv2_kernel<kSwiglu>'s epilogue), encoded whole; the item's down rows
+// against it; y[slot][row] = bf16(fxa_value(S, s_h) * alpha) (the expert
+// output the combine reads in the next layer's QKV phase).
 __device__ __forceinline__ void down_phase(StepShared& S, const StepSmem& M, const StepParams& p,
                                            const maple_decode_layer& w) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
   const int K = p.I, N = p.H;
   const int nwords = K / 16, iters_total = (nwords + 15) / 16;
-  const int slot = warp;
-  const int n_items = (N + 15) / 16;
-  const size_t frag_stride = (size_t)iters_total * 256;
-  const bool active = slot < p.topk;
-  int e = active ? S.ids[slot] : 0;
+  const int n_db = (N + 127) / 128;
+  const int item = blockIdx.x;
+  if (item >= p.topk * n_db) return;
+  const int slot = item / n_db, r0 = (item % n_db) * 128;
+  int e = S.ids[slot];
   const bool bad = (e < 0 || e >= p.E);
   if (bad) e = 0;
-  const uint32_t* codes = w.dn_codes + (int64_t)e * N * nwords;
-  const void* al = static_cast<const char*>(w.dn_alpha) + (int64_t)e * N * (p.alpha_f32 ? 4 : 2);
-  bool first = true;
-  int sh = 0;
-  int tot[4] = {0, 0, 0, 0};
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-    const int row_g = item * 16 + g, row_h = row_g + 8;
-    uint4 wa[kStepNI], wb[kStepNI];
-    load_tile(codes, row_g, row_h, active && row_g < N, active && row_h < N, nwords, 0, active ? iters_total : 0, t,
-              wa, wb);
-    tmark(S, 1);
-    if (first && active) {
-      // this warp's slot row: stage, |h| max, fragments, digit sums
-      const char* src = reinterpret_cast<const char*>(p.hact + (int64_t)slot * K);
-      float* xs = M.xs + (size_t)slot * K;
-      const int nch = K / 8;
-      uint4 rr[8];
+  const int row_g = r0 + warp * 16 + g, row_h = row_g + 8;
+  uint4 wa[kStepNI], wb[kStepNI];
+  load_tile<kStepNI>(w.dn_codes + (int64_t)e * N * nwords, row_g, row_h, row_g < N, row_h < N, nwords, 0,
+                     iters_total, t, wa, wb);
+  tmark(S, 1);
+  const int s_sw = __ldcg(reinterpret_cast<const int*>(p.meta) + 3);
+  const unsigned long long* su = p.sw_sum + (int64_t)slot * 2 * K;
+  const void* ua = static_cast<const char*>(w.ug_alpha) + (int64_t)e * 2 * K * (p.alpha_f32 ? 4 : 2);
+  const unsigned amax = stage_slice(M, K, 0, K, [&](int c, float (&v)[8]) {
+    long long Su[8], Sg[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (lane + 32 * i < nch) rr[i] = ld_u4(src + (size_t)(lane + 32 * i) * 16);
-      unsigned amax = 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int c = lane + 32 * i;
-        if (c < nch) {
-          float v[8];
-          widen_u4<kBF16>(rr[i], v);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            xs[c * 8 + q] = v[q];
-            amax = max(amax, __float_as_uint(v[q]) & 0x7fffffffu);
-          }
-        }
-      }
-#pragma unroll
-      for (int m = 16; m >= 1; m >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, m));
-      sh = fxa_shift(amax);
-      __syncwarp();
-      int raws[4] = {0, 0, 0, 0};
-      fxa_build<2>(xs, K, sh, sh == kFxaNonFinite, iters_total, M.frag + slot * frag_stride, lane, 32, raws);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int m = 16; m >= 1; m >>= 1) raws[j] += __shfl_xor_sync(0xffffffffu, raws[j], m);
-        tot[j] = raws[j] - 64 * iters_total * 256;
-      }
-      __syncwarp();
+    for (int q = 0; q < 8; ++q) {
+      Su[q] = static_cast<long long>(__ldcg(su + c * 8 + q));
+      Sg[q] = static_cast<long long>(__ldcg(su + K + c * 8 + q));
     }
-    first = false;
-    tmark(S, 2);
-    if (active) {
-      int acc[4] = {0, 0, 0, 0};
-      contract_tile2<kStepNI>(wa, wb, iters_total, M.frag + slot * frag_stride, lane, acc);
-      long long Sg, Sh;
-      combine_digits(acc, tot, t, Sg, Sh);
-      if (t == 0) {
-        const bool nan_out = bad || sh == kFxaNonFinite;
-        const float nanv = __int_as_float(0x7fc00000);
-        const float vg = nan_out ? nanv : fxa_value(Sg, sh);
-        const float vh = nan_out ? nanv : fxa_value(Sh, sh);
-        const float ag = row_g < N ? ldf(al, row_g, p.alpha_f32) : 0.f;
-        const float ah = row_h < N ? ldf(al, row_h, p.alpha_f32) : 0.f;
-        S.y[slot][g] = bf16_round(__fmul_rn(vg, ag));
-        S.y[slot][g + 8] = bf16_round(__fmul_rn(vh, ah));
-      }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int k = c * 8 + q;
+      const float nanv = __int_as_float(0x7fc00000);
+      float up = bad ? nanv : __fmul_rn(fxa_row(Su[q], s_sw), ldf(ua, k, p.alpha_f32));
+      float gate = bad ? nanv : __fmul_rn(fxa_row(Sg[q], s_sw), ldf(ua, K + k, p.alpha_f32));
+      up = fminf(fmaxf(up, -7.0f), 7.0f);
+      gate = fminf(gate, 7.0f);
+      v[q] = bf16_round(__fmul_rn(__fmul_rn(up, gate), msigmoid(gate)));
     }
-    __syncthreads();
-    tmark(S, 3);
-    if (tid < 16) {
-      const int row = item * 16 + tid;
-      if (row < N) {
-        float acc2 = 0.0f;
-        for (int sl = 0; sl < p.topk; ++sl) acc2 = __fmaf_rn(S.wts[sl], S.y[sl][tid], acc2);
-        acc2 = __fadd_rn(acc2, bf16_to_f32(p.resid[row]));
-        p.x[row] = f32_to_bf16(acc2);
-      }
-    }
-    __syncthreads();
-    tmark(S, 4);
+  });
+  const int sh = amax_exchange(S, amax);
+  build_frags(S, M.xs, K, sh, iters_total, M.frag, tid, kStepThreads);
+  __syncthreads();
+  int tot[4];
+  digit_totals(S, iters_total, tot);
+  tmark(S, 2);
+  int acc[4] = {0, 0, 0, 0};
+  contract_tile2<kStepNI>(wa, wb, iters_total, M.frag, lane, acc);
+  long long Sg, Sh;
+  combine_digits(acc, tot, t, Sg, Sh);
+  if (t == 0) {
+    const void* al = static_cast<const char*>(w.dn_alpha) + (int64_t)e * N * (p.alpha_f32 ? 4 : 2);
+    const bool nan_out = bad || sh == kFxaNonFinite;
+    const float nanv = __int_as_float(0x7fc00000);
+    uint16_t* y = p.ybuf + (int64_t)slot * N;
+    if (row_g < N) y[row_g] = f32_to_bf16(__fmul_rn(nan_out ? nanv : fxa_value(Sg, sh), ldf(al, row_g, p.alpha_f32)));
+    if (row_h < N) y[row_h] = f32_to_bf16(__fmul_rn(nan_out ? nanv : fxa_value(Sh, sh), ldf(al, row_h, p.alpha_f32)));
   }
+  tmark(S, 3);
 }
 
-// -------------------------------------------------------------- router ----
-// v = x + o; CTA 0 stores resid = bf16(v) and normed = bf16(v * rstd * w);
-// logits[e] = R128 dot(bf16(normed), gate[e]) (router_kernel<FUSE>).  One
-// item per CTA: 2 experts; warp (e_local = w / 4, q = w % 4) owns R128
-// partials 32q + lane.  The norm weights and this CTA's gate rows were
-// staged in shared memory before the barrier.
-__device__ __forceinline__ void router_phase(StepShared& S, const StepSmem& M, const StepParams& p) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int K = p.H;
-  const int n_items = (p.E + kRouterExpertsPerItem - 1) / kRouterExpertsPerItem;
-  if ((int)blockIdx.x >= n_items) return;
-  float* vs = M.xr;  // x + o, fp32
-  float* xs = M.xs;  // bf16(normed), fp32
-  const int nch = K / 8;
-  uint4 rx[4], ro[4];
+// Final combine after the last layer: x = bf16(fmaf-chain_s(w_s, y_s) +
+// resid) into p.x (CTA 0), and the SwiGLU accumulators cleared.
+__device__ __forceinline__ void final_phase(StepShared& S, const StepParams& p) {
+  zero_share(p.sw_sum, (int64_t)p.topk * 2 * p.I);
+  if (blockIdx.x != 0) return;
+  for (int c = threadIdx.x; c < p.H / 8; c += kStepThreads) {
+    float rv[8], acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    widen_u4<kBF16>(ld_u4(reinterpret_cast<const char*>(p.resid) + (size_t)c * 16), rv);
+    for (int s = 0; s < p.topk; ++s) {
+      float yv[8];
+      widen_u4<kBF16>(ld_u4(reinterpret_cast<const char*>(p.ybuf + (int64_t)s * p.H) + (size_t)c * 16), yv);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c = tid + i * kStepThreads;
-    if (c < nch) {
-      rx[i] = ld_u4(reinterpret_cast<const char*>(p.x) + (size_t)c * 16);
-      ro[i] = ld_u4(reinterpret_cast<const char*>(p.o) + (size_t)c * 16);
+      for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(S.wts[s], yv[e], acc[e]);
     }
-  }
+    uint32_t q[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c = tid + i * kStepThreads;
-    if (c < nch) {
-      float a[8], b[8];
-      widen_u4<kBF16>(rx[i], a);
-      widen_u4<kBF16>(ro[i], b);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) vs[c * 8 + e] = __fadd_rn(a[e], b[e]);
+    for (int e = 0; e < 8; ++e) {
+      const uint16_t b = f32_to_bf16(__fadd_rn(acc[e], rv[e]));
+      if (e & 1) q[e >> 1] |= static_cast<uint32_t>(b) << 16;
+      else q[e >> 1] = b;
     }
+    *reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.x) + (size_t)c * 16) = make_uint4(q[0], q[1], q[2], q[3]);
   }
-  __syncthreads();
-  tmark(S, 1);
-  if (tid < 128) {
-    float ss = 0.0f;
-    for (int k = tid; k < K; k += 128) ss = __fmaf_rn(vs[k], vs[k], ss);
-    S.part[0][tid] = ss;
-  }
-  __syncthreads();
-  const float rstd = rstd_of(r128_smem_finish(S.part[0], lane), K, p.eps);
-  tmark(S, 2);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c = tid + i * kStepThreads;
-    if (c < nch) {
-      uint32_t rq[4], nq[4];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int k = c * 8 + e;
-        const float v = vs[k];
-        const float nv = __fmul_rn(__fmul_rn(v, rstd), ldf(M.post_norm, k, p.norm_f32));
-        const uint16_t nb = f32_to_bf16(nv);
-        xs[k] = bf16_to_f32(nb);
-        const uint16_t vb = f32_to_bf16(v);
-        if (e & 1) {
-          rq[e >> 1] |= static_cast<uint32_t>(vb) << 16;
-          nq[e >> 1] |= static_cast<uint32_t>(nb) << 16;
-        } else {
-          rq[e >> 1] = vb;
-          nq[e >> 1] = nb;
-        }
-      }
-      if (blockIdx.x == 0) {
-        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.resid) + (size_t)c * 16) = make_uint4(rq[0], rq[1], rq[2], rq[3]);
-        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.normed) + (size_t)c * 16) = make_uint4(nq[0], nq[1], nq[2], nq[3]);
-      }
-    }
-  }
-  __syncthreads();
-  tmark(S, 3);
-  const int el = warp / 4, q = warp % 4;
-  const int e = blockIdx.x * kRouterExpertsPerItem + el;
-  if (e < p.E) {
-    const int j = 32 * q + lane;
-    float pj = 0.0f;
-#pragma unroll 4
-    for (int k = j; k < K; k += 128) pj = __fmaf_rn(xs[k], ldf(M.gate, (int64_t)el * K + k, p.gate_f32), pj);
-    S.part[el][j] = pj;
-  }
-  __syncthreads();
-  if (q == 0 && e < p.E) {
-    const float logit = r128_smem_finish(S.part[el], lane);
-    if (lane == 0) p.logits[e] = logit;
-  }
-  tmark(S, 4);
 }
 
 // ----------------------------------------------------------- attention ----
@@ -844,6 +921,8 @@ __device__ __forceinline__ void attention_phase(StepShared& S, const StepSmem& M
   const float ninf = __int_as_float(0xff800000);
   const int use_rope = (int)w.use_rope;
   const bool store_ok = a.pos >= 0 && a.pos < p.T && a.cb_ok;
+  const int s_qkv = __ldcg(reinterpret_cast<const int*>(p.meta));
+  const float rstd_qkv = __ldcg(p.meta + 1);
   bool first = true;
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
     const int h = item / a.ns, s = item % a.ns;
@@ -853,13 +932,31 @@ __device__ __forceinline__ void attention_phase(StepShared& S, const StepSmem& M
     if (!first && tid == 0) attn_issue<D>(p, a, w, item, M.att, &S.bar_kv);
     first = false;
     const bool has_new = a.pos >= t0 && a.pos < (int64_t)t0 + n && store_ok;
-    // loads first: q head of warp g < G, the new K (warp 0) and V (warp 1) rows
+    // q head of warp g < G, the new K (warp 0) and V (warp 1) rows, finished
+    // from the QKV sums as ternary_gemv does: bf16((fxa(S) * rstd) * alpha)
     uint16_t rq[U], rk[U], rv[U];
+    {
+      long long sq[U], sk[U], sv[U];
+      float aq[U], ak[U], av[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      rq[u] = warp < G ? p.qkv[(h * G + warp) * D + lane + 32 * u] : 0;
-      rk[u] = (warp == 0 && has_new) ? p.qkv[(p.Hq + h) * D + lane + 32 * u] : 0;
-      rv[u] = (warp == 1 && has_new) ? p.qkv[(p.Hq + p.Hkv + h) * D + lane + 32 * u] : 0;
+      for (int u = 0; u < U; ++u) {
+        const int rq_ = (h * G + warp) * D + lane + 32 * u;
+        const int rk_ = (p.Hq + h) * D + lane + 32 * u;
+        const int rv_ = (p.Hq + p.Hkv + h) * D + lane + 32 * u;
+        const bool wq = warp < G, wk = warp == 0 && has_new, wv = warp == 1 && has_new;
+        sq[u] = wq ? static_cast<long long>(__ldcg(p.qkv_sum + rq_)) : 0;
+        sk[u] = wk ? static_cast<long long>(__ldcg(p.qkv_sum + rk_)) : 0;
+        sv[u] = wv ? static_cast<long long>(__ldcg(p.qkv_sum + rv_)) : 0;
+        aq[u] = wq ? ldf(w.qkv_alpha, rq_, p.alpha_f32) : 0.f;
+        ak[u] = wk ? ldf(w.qkv_alpha, rk_, p.alpha_f32) : 0.f;
+        av[u] = wv ? ldf(w.qkv_alpha, rv_, p.alpha_f32) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        rq[u] = f32_to_bf16(__fmul_rn(__fmul_rn(fxa_row(sq[u], s_qkv), rstd_qkv), aq[u]));
+        rk[u] = f32_to_bf16(__fmul_rn(__fmul_rn(fxa_row(sk[u], s_qkv), rstd_qkv), ak[u]));
+        rv[u] = f32_to_bf16(__fmul_rn(__fmul_rn(fxa_row(sv[u], s_qkv), rstd_qkv), av[u]));
+      }
     }
     if (warp < G) {
       norm_rope_head<D>(rq, M.q_norm, p.norm_f32, M.cos, M.sin, p.cs_f32, use_rope, p.R, p.eps, qs + warp * D);
@@ -1130,6 +1227,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_layers_kernel(StepPara
   // every layer descriptor into shared memory (plain loads: a few KB)
   for (int i = tid; i < p.n_layers * (int)(sizeof(maple_decode_layer) / 8); i += kStepThreads)
     reinterpret_cast<uint64_t*>(M.layers)[i] = reinterpret_cast<const uint64_t*>(p.layers)[i];
+  // the fragments' zero halves (B columns 4-7): written here only
+  for (int i = tid; i < p.frag_entries; i += kStepThreads) M.frag[i] = make_uint2(0u, 0u);
   __syncthreads();
   unsigned ph_kv = 0, ph_st = 0, ph_in = 0, ph_rope = 0;
   if (tid == kLast) stage_layer<D>(S, p, M, L[0], attn_geom(p, (int)L[0].window));
@@ -1156,11 +1255,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_layers_kernel(StepPara
     const AttnGeom ag = attn_geom(p, (int)w.window);
     // a position outside the cache (or a bad cache row) stores no K/V, as in qk_norm_rope_store_kernel
     if (blockIdx.x == 0 && tid == 0 && (ag.pos < 0 || ag.pos >= p.T || !ag.cb_ok)) atomicOr(p.err, kErrFlagBounds);
-    // 1: RMSNorm -> QKV
+    // 1: combine the previous layer's experts -> x; RMSNorm -> QKV (split-K)
     phase_marks(l, 0);
     wait_stage(p, &S.bar_in, ph_in);
-    dense_gemv<4>(S, M, p.x, M.in_norm, p.norm_f32, p.eps, w.qkv_codes, w.qkv_alpha, p.alpha_f32, p.qkv,
-               (p.Hq + 2 * p.Hkv) * D, p.H, p.wm_qkv);
+    if (l > 0) zero_share(p.sw_sum, (int64_t)p.topk * 2 * p.I);
+    qkv_phase<kQkvTpw>(S, M, p, w, l == 0);
     tmark(S, 7);
     if (!grid_barrier(p, epoch, &S.ok, next_tr())) break;
     // 2: attention (first item's final rows are in flight since the previous layer)
@@ -1169,31 +1268,31 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_layers_kernel(StepPara
     attention_phase<D>(S, M, p, w, ag, ph_kv);
     tmark(S, 7);
     if (!grid_barrier(p, epoch, &S.ok, next_tr())) break;
-    // 3: O projection
+    // 3: O projection (split-K)
     phase_marks(l, 2);
-    dense_gemv<4>(S, M, p.attn, nullptr, p.norm_f32, 0.0f, w.o_codes, w.o_alpha, p.alpha_f32, p.o, p.H, p.Hq * D,
-               p.wm_o);
+    o_phase<kOTpw>(S, M, p, w);
     tmark(S, 7);
     if (!grid_barrier(p, epoch, &S.ok, next_tr())) break;
     // 4: residual add + RMSNorm + router logits; the next layer's dense
     // weights into L2 once this CTA is done
     phase_marks(l, 3);
-    router_phase(S, M, p);
+    router_phase(S, M, p, w);
     if (l + 1 < p.n_layers) prefetch_layer_dense(p, L[l + 1]);
     tmark(S, 7);
     if (!grid_barrier(p, epoch, &S.ok, next_tr())) break;
-    // 5: top-k (every CTA), down rows of the selected experts into L2, SwiGLU
+    // 5: top-k (every CTA), up|gate of the selected experts (split-K)
     phase_marks(l, 4);
-    swiglu_phase(S, M, p, w);
+    swiglu_phase<kSwTpw>(S, M, p, w);
     tmark(S, 7);
     if (!grid_barrier(p, epoch, &S.ok, next_tr())) break;
-    // 6: down + combine + residual -> x; then the next layer's staging copies
+    // 6: SwiGLU + down per (slot, rows); then the next layer's staging copies
     phase_marks(l, 5);
     down_phase(S, M, p, w);
     if (l + 1 < p.n_layers && tid == kLast) stage_layer<D>(S, p, M, L[l + 1], attn_geom(p, (int)L[l + 1].window));
     tmark(S, 7);
-    if (l + 1 < p.n_layers && !grid_barrier(p, epoch, &S.ok, next_tr())) break;
+    if (!grid_barrier(p, epoch, &S.ok, next_tr())) break;
   }
+  if (S.ok) final_phase(S, p);
   // a layer that stopped early (timeout) leaves no staging copy in flight
   if (tid == 0 && S.ok == 0) {
     mbar_wait_bounded(&S.bar_in, ph_in);
@@ -1215,7 +1314,7 @@ constexpr int64_t kStepTraceBytes = 1 << 20;  // barrier timestamps, written onl
 int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
 struct StepLayout {
-  int64_t qkv, attn, o, resid, normed, hact, logits, acc, ml, trace, total;
+  int64_t qkv_sum, o_sum, sw_sum, ybuf, meta, attn, resid, normed, logits, acc, ml, trace, total;
   int off_frag, off_xs, off_xr, off_att, off_layers, off_in, off_post, off_qn, off_kn, off_cos, off_sin, off_gate, smem;
 };
 
@@ -1223,12 +1322,14 @@ StepLayout step_layout(int64_t H, int64_t Hq, int64_t Hkv, int64_t D, int64_t E,
                        int64_t NS, int64_t P, int64_t R, int64_t n_layers) {
   StepLayout L{};
   int64_t off = kStepSyncBytes;
-  L.qkv = off; off = align256(off + (Hq + 2 * Hkv) * D * 2);
+  L.qkv_sum = off; off = align256(off + (Hq + 2 * Hkv) * D * 8);
+  L.o_sum = off; off = align256(off + H * 8);
+  L.sw_sum = off; off = align256(off + topk * 2 * I * 8);
+  L.ybuf = off; off = align256(off + topk * H * 2);
+  L.meta = off; off = align256(off + 64);
   L.attn = off; off = align256(off + Hq * D * 2);
-  L.o = off; off = align256(off + H * 2);
   L.resid = off; off = align256(off + H * 2);
   L.normed = off; off = align256(off + H * 2);
-  L.hact = off; off = align256(off + topk * I * 2);
   L.logits = off; off = align256(off + E * 4);
   L.acc = off; off = align256(off + Hq * NS * D * 4);
   L.ml = off; off = align256(off + Hq * NS * 2 * 4);
@@ -1236,9 +1337,11 @@ StepLayout step_layout(int64_t H, int64_t Hq, int64_t Hkv, int64_t D, int64_t E,
   L.total = off;
   auto iters = [](int64_t K) { return (K / 16 + 15) / 16; };
   auto a128 = [](int64_t v) { return (v + 127) & ~int64_t(127); };
-  const int64_t frag = std::max(std::max(iters(H), iters(Hq * D)) * 2048, topk * iters(I) * 2048);
-  const int64_t xs = std::max(std::max(H, Hq * D), topk * I);
-  const int64_t xr = std::max(H, Hq * D);
+  // fragments: a split-K slice (<= 4 iterations) or the down phase's whole K
+  const int64_t frag = std::max<int64_t>(4, iters(I)) * 2048;
+  // xs: a split-K slice (<= 4 iterations), the down phase's whole K, or the router's normed row
+  const int64_t xs = std::max<int64_t>(std::max<int64_t>(padded_len(4 * 256), padded_len((int)I)), padded_len((int)H));
+  const int64_t xr = H;
   int64_t s = 0;
   L.off_frag = (int)s; s += a128(frag);
   L.off_xs = (int)s; s += a128(xs * 4);
@@ -1256,20 +1359,15 @@ StepLayout step_layout(int64_t H, int64_t Hq, int64_t Hkv, int64_t D, int64_t E,
   return L;
 }
 
-// Row tiles per item: the fewest that cover N within one wave of CTAs while
-// each warp's K slice stays within max_ni register iterations.
-int pick_wm(int64_t N, int64_t K, int grid, int min_wm, int rows_per_tile, int max_ni) {
+// Split-K geometry: the fewest iterations per slice (<= 4) whose items
+// (row blocks x slices) fit one wave of CTAs; -1 when none does.
+int pick_ipw(int64_t row_blocks, int64_t K, int grid) {
   const int64_t it = (K / 16 + 15) / 16;
-  int best = -1;
-  for (int wm = min_wm; wm <= kStepWarps; wm *= 2) {
-    const int wk = kStepWarps / wm;
-    if ((it + wk - 1) / wk > max_ni) continue;
-    if (best < 0) best = wm;
-    const int64_t items = (N + (int64_t)rows_per_tile * wm - 1) / ((int64_t)rows_per_tile * wm);
-    if (items <= grid) return wm;
-    best = wm;
+  for (int ipw = 1; ipw <= 4; ++ipw) {
+    const int64_t nks = (it + ipw - 1) / ipw;
+    if (row_blocks * nks <= grid) return ipw;
   }
-  return best;
+  return -1;
 }
 
 }  // namespace
@@ -1337,23 +1435,35 @@ extern "C" int maple_decode_layers(const maple_decode_layer* layers, int64_t n_l
   p.E = (int)n_experts; p.topk = (int)topk; p.I = (int)inter; p.T = (int)max_len; p.Bc = (int)cache_batch;
   p.P = (int)split_len; p.NS = (int)NS; p.kc_sb = cache_sb; p.kc_sh = cache_sh;
   p.eps = eps; p.scale = scale;
-  p.wm_qkv = pick_wm((num_heads + 2 * num_kv_heads) * head_dim, hidden, grid, 1, 16, 4);
-  p.wm_o = pick_wm(hidden, num_heads * head_dim, grid, 1, 16, 4);
-  p.wm_sw = pick_wm(topk * inter, hidden, grid, 2, 8, kStepNI);
-  if (p.wm_qkv < 0 || p.wm_o < 0 || p.wm_sw < 0) return kErrShape;
+  auto iters = [](int64_t K) { return (int)((K / 16 + 15) / 16); };
+  const int64_t qkv_rows = (num_heads + 2 * num_kv_heads) * head_dim;
+  const int64_t qkv_rb = (qkv_rows + kStepWarps * kQkvTpw * 16 - 1) / (kStepWarps * kQkvTpw * 16);
+  const int64_t o_rb = (hidden + kStepWarps * kOTpw * 16 - 1) / (kStepWarps * kOTpw * 16);
+  const int64_t sw_outs = kStepWarps * kSwTpw * 16 / 2;
+  const int64_t sw_rb = topk * ((inter + sw_outs - 1) / sw_outs);
+  p.qkv_ipw = pick_ipw(qkv_rb, hidden, grid);
+  p.o_ipw = pick_ipw(o_rb, num_heads * head_dim, grid);
+  p.sw_ipw = pick_ipw(sw_rb, hidden, grid);
+  if (p.qkv_ipw < 0 || p.o_ipw < 0 || p.sw_ipw < 0) return kErrShape;
+  p.qkv_nks = (iters(hidden) + p.qkv_ipw - 1) / p.qkv_ipw;
+  p.o_nks = (iters(num_heads * head_dim) + p.o_ipw - 1) / p.o_ipw;
+  p.sw_nks = (iters(hidden) + p.sw_ipw - 1) / p.sw_ipw;
+  if (topk * ((hidden + 127) / 128) > grid) return kErrShape;  // down items: (slot, 128 rows)
   char* ws = static_cast<char*>(workspace);
-  p.qkv = reinterpret_cast<uint16_t*>(ws + L.qkv);
+  p.qkv_sum = reinterpret_cast<unsigned long long*>(ws + L.qkv_sum);
+  p.o_sum = reinterpret_cast<unsigned long long*>(ws + L.o_sum);
+  p.sw_sum = reinterpret_cast<unsigned long long*>(ws + L.sw_sum);
+  p.ybuf = reinterpret_cast<uint16_t*>(ws + L.ybuf);
+  p.meta = reinterpret_cast<float*>(ws + L.meta);
   p.attn = reinterpret_cast<uint16_t*>(ws + L.attn);
-  p.o = reinterpret_cast<uint16_t*>(ws + L.o);
   p.resid = reinterpret_cast<uint16_t*>(ws + L.resid);
   p.normed = reinterpret_cast<uint16_t*>(ws + L.normed);
-  p.hact = reinterpret_cast<uint16_t*>(ws + L.hact);
   p.logits = reinterpret_cast<float*>(ws + L.logits);
   p.att_acc = reinterpret_cast<float*>(ws + L.acc);
   p.att_ml = reinterpret_cast<float*>(ws + L.ml);
   p.sync = reinterpret_cast<unsigned*>(ws);
   // timestamps of every barrier (opt-in through sync word 2) when they fit
-  p.trace = (n_layers * 6 * 2 * (int64_t)grid * 8 <= kStepTraceBytes) ? reinterpret_cast<int64_t*>(ws + L.trace)
+  p.trace = ((n_layers * 6 + 1) * 2 * (int64_t)grid * 8 <= kStepTraceBytes) ? reinterpret_cast<int64_t*>(ws + L.trace)
                                                                       : nullptr;
   p.trace_bytes = kStepTraceBytes;
   p.att_tickets = reinterpret_cast<unsigned*>(ws + 256);
@@ -1361,6 +1471,7 @@ extern "C" int maple_decode_layers(const maple_decode_layer* layers, int64_t n_l
   p.off_frag = L.off_frag; p.off_xs = L.off_xs; p.off_xr = L.off_xr; p.off_att = L.off_att;
   p.off_layers = L.off_layers; p.off_in = L.off_in; p.off_post = L.off_post; p.off_qn = L.off_qn;
   p.off_kn = L.off_kn; p.off_cos = L.off_cos; p.off_sin = L.off_sin; p.off_gate = L.off_gate;
+  p.frag_entries = (L.off_xs - L.off_frag) / (int)sizeof(uint2);
   if ((n_experts + kRouterExpertsPerItem - 1) / kRouterExpertsPerItem > grid) return kErrShape;
   if (num_kv_heads * 4 > kStepSyncBytes - 256) return kErrShape;
 

@@ -121,9 +121,9 @@ class FusedDecodePlan:
 
     def read_trace(self, model) -> torch.Tensor:
         """Barrier timestamps of the last launch, ``[n_barriers, 2, grid]`` ns
-        (arrival, release); ``n_barriers = 6 * n_layers - 1``."""
+        (arrival, release); ``n_barriers = 6 * n_layers``."""
         grid = torch.cuda.get_device_properties(self.ws.device).multi_processor_count
-        nb = 6 * model.num_layers - 1
+        nb = 6 * model.num_layers
         off = self.ws.numel() - self.TRACE_BYTES
         raw = self.ws[off:off + nb * 2 * grid * 8].view(torch.int64)
         return raw.reshape(nb, 2, grid).cpu()
