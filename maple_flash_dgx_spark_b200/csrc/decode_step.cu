@@ -56,7 +56,7 @@ namespace mb {
 constexpr int kStepThreads = 256;
 constexpr int kStepWarps = kStepThreads / 32;
 constexpr int kStepNI = 8;         // K iterations per warp held in registers (down phase)
-constexpr int kQkvTpw = 2, kOTpw = 1, kSwTpw = 2;  // 16-row tiles per warp in the split-K phases
+constexpr int kQkvTpw = 1, kOTpw = 1, kSwTpw = 2;  // 16-row tiles per warp in the split-K phases
 constexpr int kStepMaxTopk = 8;
 constexpr int kStepMaxG = 8;       // query heads per KV head
 constexpr int kStepMaxE = 256;
@@ -103,6 +103,10 @@ __device__ __forceinline__ float ldf(const void* p, int64_t i, int f32) {
 }
 
 __device__ __forceinline__ float bf16_round(float v) { return bf16_to_f32(f32_to_bf16(v)); }
+
+// mexp / msigmoid (common.cuh) as single shared copies for the persistent kernel.
+__device__ __noinline__ float mexp_call(float x) { return mexp(x); }
+__device__ __noinline__ float msigmoid_call(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, mexp(-x))); }
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
   unsigned v;
@@ -250,8 +254,20 @@ __host__ __device__ constexpr int padded_len(int n) { return n + (n >> 5) + 1; }
 // in an order rotated by m & 3 so a warp's 8-byte stores spread over the
 // banks.  Only the digit half of an entry is written: the zero half (B
 // columns 4-7) is cleared once per launch and never written again.
+__device__ __noinline__ int4 build_frag2_call(const float* xs, int n, int s, bool bad, int iters, uint2* frag,
+                                              int t_local, int nt);
+
 __device__ __forceinline__ void build_frag2(const float* xs, int n, int s, bool bad, int iters, uint2* frag,
                                             int t_local, int nt, int (&raws)[4]) {
+  const int4 r = build_frag2_call(xs, n, s, bad, iters, frag, t_local, nt);
+  raws[0] += r.x; raws[1] += r.y; raws[2] += r.z; raws[3] += r.w;
+}
+
+// One shared copy of the builder: the persistent kernel runs it in four
+// phases of every layer, and inlined copies crowd the instruction cache.
+__device__ __noinline__ int4 build_frag2_call(const float* xs, int n, int s, bool bad, int iters, uint2* frag,
+                                              int t_local, int nt) {
+  int raws[4] = {0, 0, 0, 0};
   constexpr int off[8] = {0, 4, 8, 12, 1, 5, 9, 13};
   for (int c = t_local; c < iters * 32; c += nt) {
     const int it = c >> 5, r = c & 31;
@@ -279,6 +295,7 @@ __device__ __forceinline__ void build_frag2(const float* xs, int n, int s, bool 
       dst[4 * j] = make_uint2(signed_digits(w0), signed_digits(w1));
     }
   }
+  return make_int4(raws[0], raws[1], raws[2], raws[3]);
 }
 
 // Fragments of codes [0, iters*256) of xs (n values at pidx) by threads
@@ -361,23 +378,35 @@ __device__ __forceinline__ unsigned stage_slice(const StepSmem& M, int K, int k0
   return amax;
 }
 
-// Contract this warp's TPW row tiles (code rows row_of(j) + g, + 8) over the
-// slice's fragments and add the exact partial sums to sums[out_row(j) + ...].
-template <int TPW, int NI, typename RowOf, typename OutOf>
-__device__ __forceinline__ void splitk_contract(const StepSmem& M, const uint32_t* codes, int nwords, int it0,
-                                                int n_it, const int (&tot)[4], RowOf row_of, OutOf out_of,
-                                                unsigned long long* sums) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+// This warp's TPW row tiles (code rows row_of(j) + g, + 8) of the slice,
+// loaded into registers (issued before the activation is staged).
+template <int TPW, int NI>
+struct SplitTiles {
   uint4 wa[TPW][NI], wb[TPW][NI];
+};
+
+template <int TPW, int NI, typename RowOf>
+__device__ __forceinline__ void splitk_load(SplitTiles<TPW, NI>& T, const uint32_t* codes, int nwords, int it0,
+                                            int n_it, RowOf row_of) {
+  const int t = threadIdx.x & 3, g = (threadIdx.x & 31) >> 2;
 #pragma unroll
   for (int j = 0; j < TPW; ++j) {
     const int r = row_of(j);
-    load_tile<NI>(codes, r + g, r + g + 8, r >= 0, r >= 0, nwords, it0, n_it, t, wa[j], wb[j]);
+    load_tile<NI>(codes, r + g, r + g + 8, r >= 0, r >= 0, nwords, it0, n_it, t, T.wa[j], T.wb[j]);
   }
+}
+
+// Contract the loaded tiles against the slice's fragments and add the exact
+// partial sums to sums[out_of(j) + g (+ 8)].
+template <int TPW, int NI, typename RowOf, typename OutOf>
+__device__ __forceinline__ void splitk_finish(const SplitTiles<TPW, NI>& T, const StepSmem& M, int n_it,
+                                              const int (&tot)[4], RowOf row_of, OutOf out_of,
+                                              unsigned long long* sums) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
 #pragma unroll
   for (int j = 0; j < TPW; ++j) {
     int acc[4] = {0, 0, 0, 0};
-    contract_tile2<NI>(wa[j], wb[j], n_it, M.frag, lane, acc);
+    contract_tile2<NI>(T.wa[j], T.wb[j], n_it, M.frag, lane, acc);
     long long Sg, Sh;
     combine_digits(acc, tot, t, Sg, Sh);
     const int o = out_of(j);
@@ -420,6 +449,10 @@ __device__ __forceinline__ void qkv_phase(StepShared& S, const StepSmem& M, cons
   const int it0 = ks * G.ipw, n_it = max(0, min(G.ipw, iters_total - it0));
   const int k0 = it0 * 256, n_slice = min(K, (it0 + n_it) * 256) - k0;
   if (!has_item && blockIdx.x != 0) return;
+  const int base = rb * G.rows_per_item() + warp * TPW * 16;
+  auto row_of = [&](int j) { const int r = base + 16 * j; return (has_item && r < N) ? r : -1; };
+  SplitTiles<TPW, 4> T;
+  splitk_load(T, w.qkv_codes, nwords, it0, n_it, row_of);
   // x, x_hat = x * w_in; raw x to xr for the RMS partials
   auto fetch = [&](int c, float (&v)[8]) {
     float xv[8];
@@ -480,10 +513,7 @@ __device__ __forceinline__ void qkv_phase(StepShared& S, const StepSmem& M, cons
     }
   }
   tmark(S, 2);
-  const int base = rb * G.rows_per_item() + warp * TPW * 16;
-  splitk_contract<TPW, 4>(M, w.qkv_codes, nwords, it0, n_it, tot,
-                          [&](int j) { const int r = base + 16 * j; return r < N ? r : -1; },
-                          [&](int j) { return base + 16 * j; }, p.qkv_sum);
+  splitk_finish(T, M, n_it, tot, row_of, [&](int j) { return base + 16 * j; }, p.qkv_sum);
 }
 
 // ---------------------------------------------------------------- O ----
@@ -504,6 +534,10 @@ __device__ __forceinline__ void o_phase(StepShared& S, const StepSmem& M, const 
   const int rb = item / G.nks, ks = item % G.nks;
   const int it0 = ks * G.ipw, n_it = max(0, min(G.ipw, iters_total - it0));
   const int k0 = it0 * 256, n_slice = min(K, (it0 + n_it) * 256) - k0;
+  const int base = rb * G.rows_per_item() + warp * TPW * 16;
+  auto row_of = [&](int j) { const int r = base + 16 * j; return r < N ? r : -1; };
+  SplitTiles<TPW, 4> T;
+  splitk_load(T, w.o_codes, nwords, it0, n_it, row_of);
   const unsigned amax = stage_slice(M, K, k0, n_slice, [&](int c, float (&v)[8]) {
     widen_u4<kBF16>(ld_u4(reinterpret_cast<const char*>(p.attn) + (size_t)c * 16), v);
   });
@@ -514,10 +548,7 @@ __device__ __forceinline__ void o_phase(StepShared& S, const StepSmem& M, const 
   digit_totals(S, n_it, tot);
   if (blockIdx.x == 0 && tid == 0) reinterpret_cast<int*>(p.meta)[2] = s;
   tmark(S, 2);
-  const int base = rb * G.rows_per_item() + warp * TPW * 16;
-  splitk_contract<TPW, 4>(M, w.o_codes, nwords, it0, n_it, tot,
-                          [&](int j) { const int r = base + 16 * j; return r < N ? r : -1; },
-                          [&](int j) { return base + 16 * j; }, p.o_sum);
+  splitk_finish(T, M, n_it, tot, row_of, [&](int j) { return base + 16 * j; }, p.o_sum);
 }
 
 // ----------------------------------------------------------- router ----
@@ -630,7 +661,7 @@ __device__ __forceinline__ void swiglu_phase(StepShared& S, const StepSmem& M, c
 #pragma unroll
     for (int i = 0; i < kStepMaxE / 32; ++i) {
       const int ee = lane + 32 * i;
-      v[i] = ee < E ? mexp(__fsub_rn(v[i], m)) : 0.0f;
+      v[i] = ee < E ? mexp_call(__fsub_rn(v[i], m)) : 0.0f;
       const int j = (i & 3);
       if (j == 0) q0 = __fadd_rn(q0, v[i]);
       if (j == 1) q1 = __fadd_rn(q1, v[i]);
@@ -682,8 +713,21 @@ __device__ __forceinline__ void swiglu_phase(StepShared& S, const StepSmem& M, c
       }
     }
   }
-  if (has_item) build_frags(S, M.xs, n_slice, s, n_it, M.frag, tid, kStepThreads);
   __syncthreads();
+  // 4. the selected expert's rows of this item, then the fragments while they arrive
+  int e_item = has_item ? S.tk_sel_i[slot] : 0;
+  if (e_item < 0 || e_item >= E) e_item = 0;  // a bad id finishes as NaN in the down phase
+  const uint32_t* codes = w.ug_codes + (int64_t)e_item * 2 * I * nwords;
+  const int lbase = warp * TPW * 16;
+  auto code_row = [&](int j) {
+    const int lr = lbase + 16 * j;
+    const int r = lr < outs ? ob * outs + lr : I + ob * outs + (lr - outs);
+    const int lim = lr < outs ? I : 2 * I;
+    return (has_item && r < lim) ? r : -1;
+  };
+  SplitTiles<TPW, 4> T;
+  splitk_load(T, codes, nwords, it0, n_it, code_row);
+  if (has_item) build_frags(S, M.xs, n_slice, s, n_it, M.frag, tid, kStepThreads);
   float total = 0.0f;
   for (int rr = 0; rr < p.topk; ++rr) total = __fadd_rn(total, S.tk_sel_p[rr]);
   const float inv = __fdiv_rn(1.0f, __fadd_rn(total, 1e-20f));
@@ -708,23 +752,13 @@ __device__ __forceinline__ void swiglu_phase(StepShared& S, const StepSmem& M, c
       }
     }
   }
+  __syncthreads();
   if (!has_item) return;
   int tot[4];
   digit_totals(S, n_it, tot);
   tmark(S, 2);
-  int e = S.tk_sel_i[slot];
-  if (e < 0 || e >= E) e = 0;  // a bad id finishes as NaN in the down phase
-  const uint32_t* codes = w.ug_codes + (int64_t)e * 2 * I * nwords;
   // warp's local rows [warp * TPW * 16, +TPW*16): the first half of the item's rows are up rows, the rest gate rows
-  const int lbase = warp * TPW * 16;
-  auto code_row = [&](int j) {
-    const int lr = lbase + 16 * j;
-    const int r = lr < outs ? ob * outs + lr : I + ob * outs + (lr - outs);
-    const int lim = lr < outs ? I : 2 * I;
-    return r < lim ? r : -1;
-  };
-  splitk_contract<TPW, 4>(M, codes, nwords, it0, n_it, tot, code_row,
-                          [&](int j) { return slot * 2 * I + code_row(j); }, p.sw_sum);
+  splitk_finish(T, M, n_it, tot, code_row, [&](int j) { return slot * 2 * I + code_row(j); }, p.sw_sum);
 }
 
 // -------------------------------------------------------------- down ----
@@ -749,6 +783,9 @@ __device__ __forceinline__ void down_phase(StepShared& S, const StepSmem& M, con
   uint4 wa[kStepNI], wb[kStepNI];
   load_tile<kStepNI>(w.dn_codes + (int64_t)e * N * nwords, row_g, row_h, row_g < N, row_h < N, nwords, 0,
                      iters_total, t, wa, wb);
+  const void* al = static_cast<const char*>(w.dn_alpha) + (int64_t)e * N * (p.alpha_f32 ? 4 : 2);
+  const float ag = row_g < N ? ldf(al, row_g, p.alpha_f32) : 0.f;
+  const float ah = row_h < N ? ldf(al, row_h, p.alpha_f32) : 0.f;
   tmark(S, 1);
   const int s_sw = __ldcg(reinterpret_cast<const int*>(p.meta) + 3);
   const unsigned long long* su = p.sw_sum + (int64_t)slot * 2 * K;
@@ -768,7 +805,7 @@ __device__ __forceinline__ void down_phase(StepShared& S, const StepSmem& M, con
       float gate = bad ? nanv : __fmul_rn(fxa_row(Sg[q], s_sw), ldf(ua, K + k, p.alpha_f32));
       up = fminf(fmaxf(up, -7.0f), 7.0f);
       gate = fminf(gate, 7.0f);
-      v[q] = bf16_round(__fmul_rn(__fmul_rn(up, gate), msigmoid(gate)));
+      v[q] = bf16_round(__fmul_rn(__fmul_rn(up, gate), msigmoid_call(gate)));
     }
   });
   const int sh = amax_exchange(S, amax);
@@ -782,12 +819,11 @@ __device__ __forceinline__ void down_phase(StepShared& S, const StepSmem& M, con
   long long Sg, Sh;
   combine_digits(acc, tot, t, Sg, Sh);
   if (t == 0) {
-    const void* al = static_cast<const char*>(w.dn_alpha) + (int64_t)e * N * (p.alpha_f32 ? 4 : 2);
     const bool nan_out = bad || sh == kFxaNonFinite;
     const float nanv = __int_as_float(0x7fc00000);
     uint16_t* y = p.ybuf + (int64_t)slot * N;
-    if (row_g < N) y[row_g] = f32_to_bf16(__fmul_rn(nan_out ? nanv : fxa_value(Sg, sh), ldf(al, row_g, p.alpha_f32)));
-    if (row_h < N) y[row_h] = f32_to_bf16(__fmul_rn(nan_out ? nanv : fxa_value(Sh, sh), ldf(al, row_h, p.alpha_f32)));
+    if (row_g < N) y[row_g] = f32_to_bf16(__fmul_rn(nan_out ? nanv : fxa_value(Sg, sh), ag));
+    if (row_h < N) y[row_h] = f32_to_bf16(__fmul_rn(nan_out ? nanv : fxa_value(Sh, sh), ah));
   }
   tmark(S, 3);
 }
@@ -860,10 +896,31 @@ __device__ __forceinline__ int attn_issue(const StepParams& p, const AttnGeom& a
 // (qk_norm_rope_store_kernel); dst (D floats, shared) ends with the bf16
 // values as fp32.
 template <int D>
+__device__ __noinline__ void norm_rope_head_call(uint2 packed, const void* nw, int norm_f32, const void* cs,
+                                                 const void* sn, int cs_f32, int use_rope, int R, float eps,
+                                                 float* dst);
+
+template <int D>
 __device__ __forceinline__ void norm_rope_head(const uint16_t (&raw)[D / 32], const void* nw, int norm_f32,
                                                const void* cs, const void* sn, int cs_f32, int use_rope, int R,
                                                float eps, float* dst) {
   constexpr int U = D / 32;
+  uint32_t w4[2] = {0u, 0u};
+#pragma unroll
+  for (int u = 0; u < U; ++u) w4[u >> 1] |= static_cast<uint32_t>(raw[u]) << (16 * (u & 1));
+  norm_rope_head_call<D>(make_uint2(w4[0], w4[1]), nw, norm_f32, cs, sn, cs_f32, use_rope, R, eps, dst);
+}
+
+// One shared copy (q heads and the new K row of every layer).
+template <int D>
+__device__ __noinline__ void norm_rope_head_call(uint2 packed, const void* nw, int norm_f32, const void* cs,
+                                                 const void* sn, int cs_f32, int use_rope, int R, float eps,
+                                                 float* dst) {
+  constexpr int U = D / 32;
+  uint16_t raw[U];
+  const uint32_t w4[2] = {packed.x, packed.y};
+#pragma unroll
+  for (int u = 0; u < U; ++u) raw[u] = static_cast<uint16_t>(w4[u >> 1] >> (16 * (u & 1)));
   const int lane = threadIdx.x & 31;
   const int half = R / 2;
   float xv[U];
@@ -912,7 +969,6 @@ __device__ __forceinline__ void attention_phase(StepShared& S, const StepSmem& M
   unsigned char* ktile = M.att;
   unsigned char* vtile = M.att + (size_t)P * D * 2;
   const uint16_t* kt16 = reinterpret_cast<const uint16_t*>(ktile);
-  const uint16_t* vt16 = reinterpret_cast<const uint16_t*>(vtile);
   float* scores = reinterpret_cast<float*>(M.att + 2 * (size_t)P * D * 2);  // [8][P]
   float* pb = scores + 8 * P;                                                 // [8][P]
   float* qs = pb + 8 * P;                                                     // [8][D]
@@ -996,7 +1052,13 @@ __device__ __forceinline__ void attention_phase(StepShared& S, const StepSmem& M
       ph_kv ^= 1u;
     }
     tmark(S, 2);
-    // scores: warp w takes position groups of 4 (gqa_cluster_kernel)
+    // scores: warp w takes position groups of 4 (gqa_cluster_kernel); the
+    // group's q values stay in registers
+    float qv[8][U];
+#pragma unroll
+    for (int gg = 0; gg < 8; ++gg)
+#pragma unroll
+      for (int u = 0; u < U; ++u) qv[gg][u] = qs[gg * D + lane + 32 * u];
     if (ok) {
       for (int grp = warp; grp * 4 < n; grp += kStepWarps) {
         float v[32];
@@ -1010,7 +1072,7 @@ __device__ __forceinline__ void attention_phase(StepShared& S, const StepSmem& M
           for (int gg = 0; gg < 8; ++gg) {
             float pj[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int u = 0; u < U; ++u) pj[u & 3] = __fmaf_rn(qs[gg * D + lane + 32 * u], kk[u], pj[u & 3]);
+            for (int u = 0; u < U; ++u) pj[u & 3] = __fmaf_rn(qv[gg][u], kk[u], pj[u & 3]);
             v[i * 8 + gg] = __fadd_rn(__fadd_rn(__fadd_rn(pj[0], pj[1]), pj[2]), pj[3]);
           }
         }
@@ -1045,41 +1107,56 @@ __device__ __forceinline__ void attention_phase(StepShared& S, const StepSmem& M
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int tt = lane + 32 * u;
-        pp[u] = (tt < n) ? mexp(__fsub_rn(sv[u], m)) : 0.0f;
+        pp[u] = (tt < n) ? mexp_call(__fsub_rn(sv[u], m)) : 0.0f;
         if (tt < P) pb[gg * P + tt] = (tt < n) ? bf16_round(pp[u]) : 0.0f;
       }
       const float l = r128_lane_finish(pp[0], pp[1], pp[2], pp[3]);
       __syncwarp();
+      // P.V: lane owns dims dv(u) = 64 (u / 2) + 2 lane + u % 2 (bf16 pairs);
+      // each dim is a sequential fmaf chain over the positions
       float acc[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) acc[u] = 0.0f;
+      const uint32_t* vt32 = reinterpret_cast<const uint32_t*>(vtile);
       int tt = 0;
       for (; tt + 4 <= n; tt += 4) {
-        float pq[4], vv[4][U];
+        float pq[4];
+        uint32_t vv[4][U / 2];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           pq[i] = pb[gg * P + tt + i];
 #pragma unroll
-          for (int u = 0; u < U; ++u) vv[i][u] = bf16_to_f32(vt16[(size_t)(tt + i) * D + lane + 32 * u]);
+          for (int h2 = 0; h2 < U / 2; ++h2) vv[i][h2] = vt32[((size_t)(tt + i) * D + 64 * h2 + 2 * lane) >> 1];
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int u = 0; u < U; ++u) acc[u] = __fmaf_rn(pq[i], vv[i][u], acc[u]);
+          for (int h2 = 0; h2 < U / 2; ++h2) {
+            acc[2 * h2] = __fmaf_rn(pq[i], __uint_as_float(vv[i][h2] << 16), acc[2 * h2]);
+            acc[2 * h2 + 1] = __fmaf_rn(pq[i], __uint_as_float(vv[i][h2] & 0xffff0000u), acc[2 * h2 + 1]);
+          }
       }
       for (; tt < n; ++tt) {
         const float pt = pb[gg * P + tt];
 #pragma unroll
-        for (int u = 0; u < U; ++u) acc[u] = __fmaf_rn(pt, bf16_to_f32(vt16[(size_t)tt * D + lane + 32 * u]), acc[u]);
+        for (int h2 = 0; h2 < U / 2; ++h2) {
+          const uint32_t vv = vt32[((size_t)tt * D + 64 * h2 + 2 * lane) >> 1];
+          acc[2 * h2] = __fmaf_rn(pt, __uint_as_float(vv << 16), acc[2 * h2]);
+          acc[2 * h2 + 1] = __fmaf_rn(pt, __uint_as_float(vv & 0xffff0000u), acc[2 * h2 + 1]);
+        }
       }
       const int hq = h * G + gg;
       if (a.ns == 1) {
 #pragma unroll
-        for (int u = 0; u < U; ++u) p.attn[hq * D + lane + 32 * u] = f32_to_bf16(__fdiv_rn(acc[u], l));
+        for (int h2 = 0; h2 < U / 2; ++h2) {
+          const uint32_t lo = f32_to_bf16(__fdiv_rn(acc[2 * h2], l)), hi = f32_to_bf16(__fdiv_rn(acc[2 * h2 + 1], l));
+          reinterpret_cast<uint32_t*>(p.attn + hq * D + 64 * h2)[lane] = lo | (hi << 16);
+        }
       } else {
         float* wa = p.att_acc + ((int64_t)hq * p.NS + s) * D;
 #pragma unroll
-        for (int u = 0; u < U; ++u) wa[lane + 32 * u] = acc[u];
+        for (int h2 = 0; h2 < U / 2; ++h2)
+          reinterpret_cast<float2*>(wa + 64 * h2)[lane] = make_float2(acc[2 * h2], acc[2 * h2 + 1]);
         if (lane == 0) {
           float* wml = p.att_ml + ((int64_t)hq * p.NS + s) * 2;
           wml[0] = m;
@@ -1101,6 +1178,9 @@ __device__ __forceinline__ void attention_phase(StepShared& S, const StepSmem& M
       __syncthreads();
       tmark(S, 5);
       if (S.last && warp < G) {
+        // M = max_j m_j, w_j = exp(m_j - M), den / num as fmaf chains in split
+        // order (the workspace merge of gqa_decode_kernel), 8 splits per
+        // round of loads
         const int hq = h * G + warp;
         const float* ml = p.att_ml + (int64_t)hq * p.NS * 2;
         const float* ac = p.att_acc + (int64_t)hq * p.NS * D;
@@ -1112,7 +1192,8 @@ __device__ __forceinline__ void attention_phase(StepShared& S, const StepSmem& M
         for (int u = 0; u < U; ++u) num[u] = 0.0f;
         float den = 0.0f;
         for (int j0 = 0; j0 < a.ns; j0 += 8) {
-          float mj[8], lj[8], aj[8][U];
+          float mj[8], lj[8];
+          float2 aj[8][U / 2];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int j = j0 + i;
@@ -1120,21 +1201,28 @@ __device__ __forceinline__ void attention_phase(StepShared& S, const StepSmem& M
               mj[i] = __ldcg(ml + 2 * j);
               lj[i] = __ldcg(ml + 2 * j + 1);
 #pragma unroll
-              for (int u = 0; u < U; ++u) aj[i][u] = __ldcg(ac + (int64_t)j * D + lane + 32 * u);
+              for (int h2 = 0; h2 < U / 2; ++h2)
+                aj[i][h2] = __ldcg(reinterpret_cast<const float2*>(ac + (int64_t)j * D + 64 * h2) + lane);
             }
           }
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             if (j0 + i < a.ns) {
-              const float wgt = mexp(__fsub_rn(mj[i], M2));
+              const float wgt = mexp_call(__fsub_rn(mj[i], M2));
               den = __fmaf_rn(wgt, lj[i], den);
 #pragma unroll
-              for (int u = 0; u < U; ++u) num[u] = __fmaf_rn(wgt, aj[i][u], num[u]);
+              for (int h2 = 0; h2 < U / 2; ++h2) {
+                num[2 * h2] = __fmaf_rn(wgt, aj[i][h2].x, num[2 * h2]);
+                num[2 * h2 + 1] = __fmaf_rn(wgt, aj[i][h2].y, num[2 * h2 + 1]);
+              }
             }
           }
         }
 #pragma unroll
-        for (int u = 0; u < U; ++u) p.attn[hq * D + lane + 32 * u] = f32_to_bf16(__fdiv_rn(num[u], den));
+        for (int h2 = 0; h2 < U / 2; ++h2) {
+          const uint32_t lo = f32_to_bf16(__fdiv_rn(num[2 * h2], den)), hi = f32_to_bf16(__fdiv_rn(num[2 * h2 + 1], den));
+          reinterpret_cast<uint32_t*>(p.attn + hq * D + 64 * h2)[lane] = lo | (hi << 16);
+        }
       }
     }
     __syncthreads();
