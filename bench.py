@@ -293,7 +293,7 @@ def main():
                      "frac": swiglu_bytes / (launch_us * 1e-6) / 1e9 / peak, "traffic": traffic,
                      "algorithmic_bytes": swiglu_bytes, "launch_us": launch_us, "peak_kind": f"{peak_kind} hbm_gbs"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
-        "gpu_launches": Kst * (8 * cfg["num_hidden_layers"] + 4),
+        "gpu_launches": Kst * _step_launches(cfg["num_hidden_layers"]),
         "clocks": clocks.summary(),
     }
     if args.breakdown:
@@ -498,7 +498,7 @@ def run_bs64(args):
                      "frac": kv_per_launch / (att_us * 1e-6) / 1e9 / peak, "traffic": None,
                      "algorithmic_bytes": kv_per_launch, "launch_us": att_us, "peak_kind": f"{peak_kind} hbm_gbs"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * T, "d2h_bytes_per_step": 8 * T},
-        "gpu_launches": Kst * (15 * cfg["num_hidden_layers"] + 4),
+        "gpu_launches": Kst * ((12 + _attn_launches()) * cfg["num_hidden_layers"] + 4),
         "clocks": clocks.summary(),
     }
     if rank == 0:
@@ -667,7 +667,7 @@ def run_long(args):
                      "frac": kv_per_launch / (att_us * 1e-6) / 1e9 / peak, "traffic": None,
                      "algorithmic_bytes": kv_per_launch, "launch_us": att_us, "peak_kind": f"{peak_kind} hbm_gbs"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 8 * B},
-        "gpu_launches": Kst * (8 * cfg["num_hidden_layers"] + 8),
+        "gpu_launches": Kst * ((5 + _attn_launches()) * cfg["num_hidden_layers"] + 8),
         "clocks": clocks.summary(),
     }
     if flash:
@@ -712,48 +712,66 @@ def swiglu_roofline(model, prompt, dev):
     return us, nbytes
 
 
+def _step_launches(n_layers: int) -> int:
+    """This engine's kernel launches in one batch-1 decode step: per layer QKV,
+    attention with QK-norm / RoPE / K-V store, O, add-norm + router, SwiGLU,
+    down (seven with the QK-norm as its own launch), or one persistent launch
+    for all layers under MAPLE_FUSED_DECODE=1; plus embedding, final norm,
+    head and argmax."""
+    from maple_flash_dgx_spark_b200.fused_decode import fused_decode_enabled
+
+    if fused_decode_enabled():
+        return 1 + 4
+    return _attn_launches() * n_layers + 4 * n_layers + 4
+
+
+def _attn_launches() -> int:
+    """Launches of the attention block of a decode layer besides O: QKV + the
+    fused attention, or QKV + QK-norm + attention."""
+    from maple_flash_dgx_spark_b200.model import _fused_qk_attention
+
+    return 2 if _fused_qk_attention() else 3
+
+
 def op_breakdown(model, cache, dev):
-    """Warm in-graph time of each decode operator: run one decode step layer by
-    layer keeping every intermediate, then replay each operator over the 48
-    layers in its own CUDA graph (launched like the decode step, with PDL)."""
+    """Warm in-graph time of each operator of the batch-1 decode step: run one
+    step layer by layer keeping every intermediate, then replay each operator
+    over the 48 layers in its own CUDA graph (launched like the decode step,
+    with PDL).  The attention replays re-store the same K/V row."""
     import torch
 
     from maple_flash_dgx_spark_b200 import kernels as K
 
     pos = torch.full((1,), int(cache.seen[0]) - 1, dtype=torch.int64, device=dev)
     rot = model.rotary
-    steps = {name: [] for name in ("qkv_gemv", "qk_norm_rope_store", "attention", "o_gemv", "add_rms_norm",
-                                   "router_topk", "expert_swiglu", "expert_down_reduce")}
+    steps = {name: [] for name in ("qkv_gemv", "attention_qk", "o_gemv", "add_norm_router", "expert_swiglu",
+                                   "expert_down_reduce")}
     h = model.embed(torch.ones(1, dtype=torch.long, device=dev))
     with torch.inference_mode():
         for i, lay in enumerate(model.layers):
             at, mlp = lay.self_attn, lay.mlp
             kc, vc = cache.k[i][:1], cache.v[i][:1]
+            pl = lay.post_attention_layernorm.weight
+
+            def attn_qk(at=at, kc=kc, vc=vc, qkv=None):
+                return K.decode_gqa_attn_qk(qkv, at.q_norm.weight, at.k_norm.weight, rot.cos_table, rot.sin_table,
+                                            kc, vc, pos, num_heads=at.num_heads, num_kv_heads=at.num_kv_heads,
+                                            head_dim=at.head_dim, rotary_dim=rot.rotary_dim, use_rope=at.use_rope,
+                                            eps=model.rms_eps, scale=at.scale, window=None,
+                                            split_len=cache.split_len)
+
             qkv = at.qkv_proj(h, rms_weight=lay.input_layernorm.weight, rms_eps=model.rms_eps)
-            q = K.apply_qkv_decode(qkv, at.q_norm.weight, at.k_norm.weight, rot.cos_table, rot.sin_table, kc, vc, pos,
-                                   num_heads=at.num_heads, num_kv_heads=at.num_kv_heads, head_dim=at.head_dim,
-                                   rotary_dim=rot.rotary_dim, use_rope=at.use_rope, use_qk_norm=True,
-                                   eps=model.rms_eps, rope_table=True)
-            attn = K.decode_gqa_attn(q, kc, vc, pos, scale=at.scale, window=None, split_len=cache.split_len)
+            attn = attn_qk(qkv=qkv)
             o = at.o_proj(attn.reshape(1, -1))
-            res, normed = K.add_rms_norm(h, o, lay.post_attention_layernorm.weight, model.rms_eps)
-            idx, wt = K.router_topk(normed, mlp.gate_weight, mlp.top_k)
+            res, normed, idx, wt = K.add_rms_norm_router_topk(h, o, pl, model.rms_eps, mlp.gate_weight, mlp.top_k)
             hs = mlp.up_gate.swiglu(normed, idx)
             h2 = mlp.down.down_reduce(hs, idx, wt, residual=res)
-            pl = lay.post_attention_layernorm.weight
             steps["qkv_gemv"].append(lambda at=at, h=h, lay=lay: at.qkv_proj(
                 h, rms_weight=lay.input_layernorm.weight, rms_eps=model.rms_eps))
-            steps["qk_norm_rope_store"].append(lambda at=at, qkv=qkv, kc=kc, vc=vc: K.apply_qkv_decode(
-                qkv, at.q_norm.weight, at.k_norm.weight, rot.cos_table, rot.sin_table, kc, vc, pos,
-                num_heads=at.num_heads, num_kv_heads=at.num_kv_heads, head_dim=at.head_dim,
-                rotary_dim=rot.rotary_dim, use_rope=at.use_rope, use_qk_norm=True, eps=model.rms_eps,
-                rope_table=True))
-            steps["attention"].append(lambda at=at, q=q, kc=kc, vc=vc: K.decode_gqa_attn(
-                q, kc, vc, pos, scale=at.scale, window=None, split_len=cache.split_len))
+            steps["attention_qk"].append(lambda f=attn_qk, qkv=qkv: f(qkv=qkv))
             steps["o_gemv"].append(lambda at=at, attn=attn: at.o_proj(attn.reshape(1, -1)))
-            steps["add_rms_norm"].append(lambda h=h, o=o, pl=pl: K.add_rms_norm(h, o, pl, model.rms_eps))
-            steps["router_topk"].append(lambda mlp=mlp, normed=normed: K.router_topk(normed, mlp.gate_weight,
-                                                                                      mlp.top_k))
+            steps["add_norm_router"].append(lambda h=h, o=o, pl=pl, mlp=mlp: K.add_rms_norm_router_topk(
+                h, o, pl, model.rms_eps, mlp.gate_weight, mlp.top_k))
             steps["expert_swiglu"].append(lambda mlp=mlp, normed=normed, idx=idx: mlp.up_gate.swiglu(normed, idx))
             steps["expert_down_reduce"].append(lambda mlp=mlp, hs=hs, idx=idx, wt=wt, res=res: mlp.down.down_reduce(
                 hs, idx, wt, residual=res))

@@ -258,6 +258,27 @@ int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, int64_t num
                           int64_t window, int64_t split_len, int kv_final, void* out, int64_t o_sb, int64_t o_sh,
                           void* workspace, int64_t workspace_bytes, int* err, void* stream);
 
+/* maple_apply_qkv_decode followed by maple_decode_gqa_attn in one launch, for
+ * decode rows (K/V at positions < seqlen[b] final before the call): replaces
+ * kernels/decode_attn.py:362-439 apply_qkv_decode + :470-592 decode_gqa_attn
+ * as MapleAttention's decode branch calls them (model.py:368-414).  Each
+ * attention CTA forms its group's q heads (QK RMSNorm + RoPE from the QKV
+ * rows, rope tables read at clamp(seqlen[b])); the split holding seqlen[b]
+ * forms the new K row and copies the V row into the caches.  Results (out
+ * and the cache contents) are bit-identical to the two calls.  qkv: [batch,
+ * (num_heads + 2 num_kv_heads) head_dim] in x_dtype, row stride
+ * qkv_row_stride; q/k weights [head_dim] (w_dtype); the other arguments as
+ * in maple_apply_qkv_decode / maple_decode_gqa_attn. */
+int maple_decode_gqa_attn_qk(const void* qkv, int x_dtype, int64_t batch, int64_t qkv_row_stride,
+                             const void* q_weight, const void* k_weight, int w_dtype, const void* cos,
+                             const void* sin, int cs_dtype, int64_t cs_row_stride, int64_t cs_table_len,
+                             int64_t rotary_dim, int use_rope, float eps, int64_t num_heads, const void* k_cache,
+                             const void* v_cache, int64_t cache_batch, int64_t num_kv_heads, int64_t cache_sb,
+                             int64_t cache_sh, int64_t max_len, int64_t head_dim, const int64_t* seqlen,
+                             const int32_t* row_map, float scale, int64_t window, int64_t split_len, void* out,
+                             int64_t o_sb, int64_t o_sh, void* workspace, int64_t workspace_bytes, int* err,
+                             void* stream);
+
 /* RTN-4 GEMV y = x . (scale*code + bias)^T per group.  Replaces
  * kernels/rtn4.py:285 rtn4_gemv and linear.py:72 PackedRTN4Linear.  codes
  * uint32 [n, k/8] (8 LSB-first 4-bit codes per word); scales/biases

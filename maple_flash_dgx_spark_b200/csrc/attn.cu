@@ -132,9 +132,113 @@ struct AttnParams {
   int kv_final;           // 1: K/V at positions < seqlen[b] were final before the previous launch
   int defer_merge;        // 1: leave the split partials for gqa_merge_kernel (long contexts)
   float scale;
+  // Fused QK RMSNorm + RoPE + K/V store (kernels with QK = true, decode rows
+  // only): q heads and the new K/V row come from the QKV projection rows.
+  const void* qkv;        // [B, (Hq + 2 Hkv) D]
+  int64_t qkv_sb;
+  const void* q_w;        // [D]
+  const void* k_w;        // [D]
+  const void* cos;        // [cs_len, R] tables read at clamp(seqlen[b])
+  const void* sin;
+  int64_t cs_sb, cs_len;
+  int w_f32, cs_f32, R, use_rope;
+  float eps;
 };
 
+__device__ __forceinline__ float ldf_rt(const void* p, int64_t i, int f32) {
+  return f32 ? static_cast<const float*>(p)[i] : bf16_to_f32(static_cast<const uint16_t*>(p)[i]);
+}
+
+// One warp: RMSNorm (R128 over D) * w, then RoPE of head `base` of a QKV row
+// (the arithmetic of qk_norm_rope_store_kernel); o[u] is the value of dim
+// lane + 32u before its bf16 store.  xh: D floats of warp-private shared memory.
 template <int XT, int D>
+__device__ __forceinline__ void qk_norm_rope_warp(const AttnParams& p, const char* row, int base, const void* w,
+                                                  int64_t pos, float* xh, float (&o)[D / 32]) {
+  constexpr int U = D / 32;
+  const int lane = threadIdx.x & 31;
+  float xv[U];
+  float part[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    xv[u] = load_f<XT>(row, base + lane + 32 * u);
+    part[u & 3] = __fmaf_rn(xv[u], xv[u], part[u & 3]);
+  }
+  const float rstd = rstd_of(r128_lane_finish(part[0], part[1], part[2], part[3]), D, p.eps);
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int d = lane + 32 * u;
+    xh[d] = __fmul_rn(__fmul_rn(xv[u], rstd), ldf_rt(w, d, p.w_f32));
+  }
+  __syncwarp();
+  const int64_t cs_row = pos < 0 ? 0 : (pos >= p.cs_len ? p.cs_len - 1 : pos);
+  const char* cs = static_cast<const char*>(p.cos) + cs_row * p.cs_sb * (p.cs_f32 ? 4 : 2);
+  const char* sn = static_cast<const char*>(p.sin) + cs_row * p.cs_sb * (p.cs_f32 ? 4 : 2);
+  const int half = p.R / 2;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int d = lane + 32 * u;
+    float v = xh[d];
+    if (p.use_rope && d < p.R) {
+      if (d < half)
+        v = __fadd_rn(__fmul_rn(xh[d], ldf_rt(cs, d, p.cs_f32)), __fmul_rn(-xh[d + half], ldf_rt(sn, d, p.cs_f32)));
+      else
+        v = __fadd_rn(__fmul_rn(xh[d], ldf_rt(cs, d, p.cs_f32)), __fmul_rn(xh[d - half], ldf_rt(sn, d, p.cs_f32)));
+    }
+    o[u] = v;
+  }
+  __syncwarp();
+}
+
+// QK mode: the split's q heads into qsm ([8][D], bf16-rounded values; zero
+// rows beyond G) and, in the split that holds position pos, the new K/V row
+// into the cache and the tiles.  Warp w takes q heads w, w + nwarps, ...;
+// warps 0 / 1 then take the new K / V row.  Ends synchronised.
+template <int XT, int D>
+__device__ __forceinline__ void qk_fused_rows(const AttnParams& p, int b, int h, int cb, int64_t pos, int t0,
+                                              int n, bool active, bool cb_ok, unsigned char* ktile,
+                                              unsigned char* vtile, float* qsm, float* kscr, int nwarps) {
+  constexpr int U = D / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int es = XT == kBF16 ? 2 : 4;
+  const char* row = static_cast<const char*>(p.qkv) + b * p.qkv_sb * es;
+  for (int g = warp; g < 8; g += nwarps) {
+    if (g < p.G && active) {
+      float o[U];
+      qk_norm_rope_warp<XT, D>(p, row, (h * p.G + g) * D, p.q_w, pos, qsm + g * D, o);
+#pragma unroll
+      for (int u = 0; u < U; ++u) qsm[g * D + lane + 32 * u] = XT == kBF16 ? bf16_to_f32(f32_to_bf16(o[u])) : o[u];
+    } else {
+#pragma unroll
+      for (int u = 0; u < U; ++u) qsm[g * D + lane + 32 * u] = 0.0f;
+    }
+  }
+  const bool has_new = active && pos >= t0 && pos < (int64_t)t0 + n && pos < p.T && cb_ok;
+  if (has_new && warp == 0) {
+    float o[U];
+    qk_norm_rope_warp<XT, D>(p, row, p.Hq * D + h * D, p.k_w, pos, kscr, o);
+    char* dst = static_cast<char*>(const_cast<void*>(p.kc)) + (cb * p.kc_sb + h * p.kc_sh + pos * D) * es;
+    unsigned char* tt = ktile + (size_t)(pos - t0) * D * es;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      store_f<XT>(dst, lane + 32 * u, o[u]);
+      store_f<XT>(tt, lane + 32 * u, o[u]);
+    }
+  } else if (has_new && warp == 1) {
+    const int vb = (p.Hq + p.Hkv) * D + h * D;
+    char* dst = static_cast<char*>(const_cast<void*>(p.vc)) + (cb * p.vc_sb + h * p.vc_sh + pos * D) * es;
+    unsigned char* tt = vtile + (size_t)(pos - t0) * D * es;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float v = load_f<XT>(row, vb + lane + 32 * u);
+      store_f<XT>(dst, lane + 32 * u, v);
+      store_f<XT>(tt, lane + 32 * u, v);
+    }
+  }
+  __syncthreads();
+}
+
+template <int XT, int D, bool QK>
 __global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
   constexpr int U = D / 32;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -157,7 +261,8 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
   const int n = min(P, kv_len - t0);
   int cb = b;
   if (p.row_map != nullptr) cb = p.row_map[b];
-  if (cb < 0 || cb >= p.Bc) {
+  const bool cb_ok = cb >= 0 && cb < p.Bc;
+  if (!cb_ok) {
     if (tid == 0) atomicOr(p.err, kErrFlagBounds);
     cb = 0;
   }
@@ -166,25 +271,38 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
   unsigned char* vtile = smem + (size_t)P * D * es;
   float* scores = reinterpret_cast<float*>(smem + 2 * (size_t)P * D * es);  // [8][P]
   float* pb = scores + 8 * P;                                                 // [8][P]
+  float* qsm = pb + 8 * P;                                                    // QK: [8][D] q, then [D] K scratch
 
+  // QK: only the rows before pos are in the cache; the newest is formed here
+  const int n_copy = QK ? max(0, (int)min((int64_t)n, pos - t0)) : n;
   if (tid == 0) {
     mbar_init(&bar, 1);
-    const unsigned bytes = (unsigned)(n * D * es);
+    const unsigned bytes = (unsigned)(n_copy * D * es);
     mbar_expect_tx(&bar, 2 * bytes);
     const char* ksrc = static_cast<const char*>(p.kc) + (cb * p.kc_sb + h * p.kc_sh + (int64_t)t0 * D) * es;
     const char* vsrc = static_cast<const char*>(p.vc) + (cb * p.vc_sb + h * p.vc_sh + (int64_t)t0 * D) * es;
-    bulk_g2s(ktile, ksrc, bytes, &bar);
-    bulk_g2s(vtile, vsrc, bytes, &bar);
+    if (bytes > 0) {
+      bulk_g2s(ktile, ksrc, bytes, &bar);
+      bulk_g2s(vtile, vsrc, bytes, &bar);
+    }
   }
   // q of the group's heads while the copies are in flight.
   float qv[8][U];
+  if constexpr (QK) {
+    qk_fused_rows<XT, D>(p, b, h, cb, pos, t0, n, true, cb_ok, ktile, vtile, qsm, qsm + 8 * D, 4);
 #pragma unroll
-  for (int g = 0; g < 8; ++g)
+    for (int g = 0; g < 8; ++g)
 #pragma unroll
-    for (int u = 0; u < U; ++u)
-      qv[g][u] = g < G ? load_f<XT>(static_cast<const char*>(p.q) + (b * p.q_sb + (h * G + g) * p.q_sh) * es,
-                                    lane + 32 * u)
-                       : 0.0f;
+      for (int u = 0; u < U; ++u) qv[g][u] = qsm[g * D + lane + 32 * u];
+  } else {
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        qv[g][u] = g < G ? load_f<XT>(static_cast<const char*>(p.q) + (b * p.q_sb + (h * G + g) * p.q_sh) * es,
+                                      lane + 32 * u)
+                         : 0.0f;
+  }
   __syncthreads();  // barrier initialised before anyone waits on it
   bool ready = false;
   for (int i = 0; i < kWaitSpins && !ready; ++i) ready = mbar_try_wait(&bar, 0);
@@ -340,7 +458,7 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
 // order through distributed shared memory (same arithmetic as the workspace
 // merge).  With kv_final, K/V rows of positions before seqlen[b] are copied
 // before the PDL wait; only the newest position waits for the previous launch.
-template <int XT, int D>
+template <int XT, int D, bool QK>
 __global__ void __launch_bounds__(256) gqa_cluster_kernel(AttnParams p) {
   constexpr int U = D / 32;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -357,6 +475,7 @@ __global__ void __launch_bounds__(256) gqa_cluster_kernel(AttnParams p) {
   float* part = pb + 8 * P;                                                   // [8][D] acc, then m[8], l[8]
   float* part_m = part + 8 * D;
   float* part_l = part_m + 8;
+  float* kscr = part_l + 8;                                                   // QK: [D] K scratch
 
   const int64_t pos = p.seqlen[b];
   const int kv_len = (int)min(pos + 1, (int64_t)p.T);
@@ -386,7 +505,7 @@ __global__ void __launch_bounds__(256) gqa_cluster_kernel(AttnParams p) {
   pdl_trigger();
   if (tid == 0) {
     if (!cb_ok) atomicOr(p.err, kErrFlagBounds);
-    if (n > n_pre) {
+    if (!QK && n > n_pre) {
       const unsigned off = (unsigned)(n_pre * D * es), bytes = (unsigned)((n - n_pre) * D * es);
       mbar_expect_tx(&bar[1], 2u * bytes);
       bulk_g2s(ktile + off, ksrc + off, bytes, &bar[1]);
@@ -394,17 +513,26 @@ __global__ void __launch_bounds__(256) gqa_cluster_kernel(AttnParams p) {
     }
   }
   float qv[8][U];
+  if constexpr (QK) {
+    // q heads and the newest K/V row from the QKV rows (the merge area holds q until P.V)
+    qk_fused_rows<XT, D>(p, b, h, cb, pos, t0, n, active, cb_ok, ktile, vtile, part, kscr, 8);
 #pragma unroll
-  for (int g = 0; g < 8; ++g)
+    for (int g = 0; g < 8; ++g)
 #pragma unroll
-    for (int u = 0; u < U; ++u)
-      qv[g][u] = (g < G && active) ? load_f<XT>(static_cast<const char*>(p.q) + (b * p.q_sb + (h * G + g) * p.q_sh) * es,
-                                                lane + 32 * u)
-                                   : 0.0f;
-  __syncthreads();  // barriers initialised before anyone waits
+      for (int u = 0; u < U; ++u) qv[g][u] = part[g * D + lane + 32 * u];
+  } else {
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        qv[g][u] = (g < G && active) ? load_f<XT>(static_cast<const char*>(p.q) + (b * p.q_sb + (h * G + g) * p.q_sh) * es,
+                                                  lane + 32 * u)
+                                     : 0.0f;
+  }
+  __syncthreads();  // barriers initialised before anyone waits; q read from shared memory
   bool ok = true;
   for (int k = 0; k < 2; ++k) {
-    const bool need = (k == 0) ? n_pre > 0 : n > n_pre;
+    const bool need = (k == 0) ? n_pre > 0 : (!QK && n > n_pre);
     if (need) {
       bool ready = false;
       for (int i = 0; i < kWaitSpins && !ready; ++i) ready = mbar_try_wait(&bar[k], 0);
@@ -629,21 +757,19 @@ extern "C" int64_t maple_decode_gqa_workspace_bytes(int64_t batch, int64_t num_h
   return kAttnTicketBytes + batch * num_heads * ns * (head_dim + 2) * (int64_t)sizeof(float);
 }
 
-extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, int64_t num_heads,
-                                     int64_t q_sb, int64_t q_sh, const void* k_cache, const void* v_cache,
-                                     int64_t cache_batch, int64_t num_kv_heads, int64_t cache_sb,
-                                     int64_t cache_sh, int64_t max_len, int64_t head_dim,
-                                     const int64_t* seqlen, const int32_t* row_map, float scale,
-                                     int64_t window, int64_t split_len, int kv_final, void* out,
-                                     int64_t o_sb, int64_t o_sh, void* workspace, int64_t workspace_bytes,
-                                     int* err, void* stream) {
+static int gqa_common(const void* q, int x_dtype, int64_t batch, int64_t num_heads, int64_t q_sb, int64_t q_sh,
+                      const void* k_cache, const void* v_cache, int64_t cache_batch, int64_t num_kv_heads,
+                      int64_t cache_sb, int64_t cache_sh, int64_t max_len, int64_t head_dim,
+                      const int64_t* seqlen, const int32_t* row_map, float scale, int64_t window,
+                      int64_t split_len, int kv_final, void* out, int64_t o_sb, int64_t o_sh, void* workspace,
+                      int64_t workspace_bytes, int* err, void* stream, const AttnParams* qk) {
   if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_len <= 0) return kErrShape;
   if (batch == 0) return kOk;
   if (num_heads % num_kv_heads != 0 || num_heads / num_kv_heads > 8) return kErrShape;
   if (head_dim != 64 && head_dim != 128 && head_dim != 256) return kErrShape;
   if (split_len != 32 && split_len != 64 && split_len != 128) return kErrShape;
   if (x_dtype != kF32 && x_dtype != kBF16) return kErrDtype;
-  if (!q || !k_cache || !v_cache || !seqlen || !out || !err) return kErrShape;
+  if ((!q && !qk) || !k_cache || !v_cache || !seqlen || !out || !err) return kErrShape;
   const int es = x_dtype == kBF16 ? 2 : 4;
   if ((reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15) ||
       ((cache_sb * es) & 15) || ((cache_sh * es) & 15))
@@ -654,7 +780,7 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
   if (ns > 16 && (!workspace || workspace_bytes < maple_decode_gqa_workspace_bytes(batch, num_heads, head_dim,
                                                                                    max_len, split_len)))
     return kErrWorkspace;
-  AttnParams p{};
+  AttnParams p = qk ? *qk : AttnParams{};
   p.q = q; p.kc = k_cache; p.vc = v_cache; p.seqlen = seqlen; p.row_map = row_map; p.out = out; p.err = err;
   p.tickets = static_cast<unsigned*>(workspace);
   p.ws_acc = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kAttnTicketBytes) : nullptr;
@@ -670,7 +796,7 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
     int cl = 1;
     while (cl < ns) cl *= 2;
     const size_t smem = 2 * (size_t)split_len * head_dim * es + 2 * 8 * (size_t)split_len * sizeof(float) +
-                        (8 * (size_t)head_dim + 16) * sizeof(float);
+                        (8 * (size_t)head_dim + 16) * sizeof(float) + (qk ? (size_t)head_dim * sizeof(float) : 0);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)cl, (unsigned)num_kv_heads, (unsigned)batch);
     cfg.blockDim = dim3(256);
@@ -688,7 +814,7 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
     cudaError_t e = cudaSuccess;
 #define MB_ATTC(XT, DD)                                                                                       \
   do {                                                                                                        \
-    auto kern = gqa_cluster_kernel<XT, DD>;                                                                   \
+    auto kern = qk ? gqa_cluster_kernel<XT, DD, true> : gqa_cluster_kernel<XT, DD, false>;                    \
     if (cl > 8) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);            \
     if (e == cudaSuccess && smem > 32 * 1024)                                                                 \
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                 \
@@ -702,7 +828,8 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
 #undef MB_ATTC
     return e == cudaSuccess ? kOk : kErrCuda;
   }
-  const size_t smem = 2 * (size_t)split_len * head_dim * es + 2 * 8 * (size_t)split_len * sizeof(float);
+  const size_t smem = 2 * (size_t)split_len * head_dim * es + 2 * 8 * (size_t)split_len * sizeof(float) +
+                      (qk ? 9 * (size_t)head_dim * sizeof(float) : 0);
   dim3 grid((unsigned)ns, (unsigned)num_kv_heads, (unsigned)batch);
   cudaError_t e = cudaSuccess;
   // Long contexts: the splits' merge gets its own launch spread over
@@ -710,7 +837,7 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
   p.defer_merge = ns >= 128 ? 1 : 0;
 #define MB_ATT(XT, DD)                                                                        \
   do {                                                                                        \
-    auto kern = gqa_decode_kernel<XT, DD>;                                                    \
+    auto kern = qk ? gqa_decode_kernel<XT, DD, true> : gqa_decode_kernel<XT, DD, false>;       \
     if (smem > 32 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
     if (e == cudaSuccess) e = launch_k(kern, dim3(grid), dim3(128), smem, st, p);                               \
     if (e == cudaSuccess && p.defer_merge)                                                    \
@@ -724,4 +851,40 @@ extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, 
 #undef MB_ATT
   if (e != cudaSuccess) return kErrCuda;
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+extern "C" int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, int64_t num_heads,
+                                     int64_t q_sb, int64_t q_sh, const void* k_cache, const void* v_cache,
+                                     int64_t cache_batch, int64_t num_kv_heads, int64_t cache_sb,
+                                     int64_t cache_sh, int64_t max_len, int64_t head_dim,
+                                     const int64_t* seqlen, const int32_t* row_map, float scale,
+                                     int64_t window, int64_t split_len, int kv_final, void* out,
+                                     int64_t o_sb, int64_t o_sh, void* workspace, int64_t workspace_bytes,
+                                     int* err, void* stream) {
+  return gqa_common(q, x_dtype, batch, num_heads, q_sb, q_sh, k_cache, v_cache, cache_batch, num_kv_heads, cache_sb,
+                    cache_sh, max_len, head_dim, seqlen, row_map, scale, window, split_len, kv_final, out, o_sb, o_sh,
+                    workspace, workspace_bytes, err, stream, nullptr);
+}
+
+extern "C" int maple_decode_gqa_attn_qk(const void* qkv, int x_dtype, int64_t batch, int64_t qkv_row_stride,
+                                        const void* q_weight, const void* k_weight, int w_dtype, const void* cos,
+                                        const void* sin, int cs_dtype, int64_t cs_row_stride, int64_t cs_table_len,
+                                        int64_t rotary_dim, int use_rope, float eps, int64_t num_heads,
+                                        const void* k_cache, const void* v_cache, int64_t cache_batch,
+                                        int64_t num_kv_heads, int64_t cache_sb, int64_t cache_sh, int64_t max_len,
+                                        int64_t head_dim, const int64_t* seqlen, const int32_t* row_map,
+                                        float scale, int64_t window, int64_t split_len, void* out, int64_t o_sb,
+                                        int64_t o_sh, void* workspace, int64_t workspace_bytes, int* err,
+                                        void* stream) {
+  if (!qkv || !q_weight || !k_weight) return kErrShape;
+  if ((w_dtype != kF32 && w_dtype != kBF16) || (cs_dtype != kF32 && cs_dtype != kBF16)) return kErrDtype;
+  if (rotary_dim < 0 || rotary_dim > head_dim || (rotary_dim & 1)) return kErrShape;
+  if (use_rope && (!cos || !sin || cs_table_len <= 0)) return kErrShape;
+  AttnParams qk{};
+  qk.qkv = qkv; qk.qkv_sb = qkv_row_stride; qk.q_w = q_weight; qk.k_w = k_weight; qk.w_f32 = w_dtype == kF32;
+  qk.cos = cos; qk.sin = sin; qk.cs_f32 = cs_dtype == kF32; qk.cs_sb = cs_row_stride; qk.cs_len = cs_table_len;
+  qk.R = (int)rotary_dim; qk.use_rope = use_rope; qk.eps = eps;
+  return gqa_common(nullptr, x_dtype, batch, num_heads, 0, 0, k_cache, v_cache, cache_batch, num_kv_heads, cache_sb,
+                    cache_sh, max_len, head_dim, seqlen, row_map, scale, window, split_len, 1, out, o_sb, o_sh,
+                    workspace, workspace_bytes, err, stream, &qk);
 }

@@ -569,6 +569,54 @@ def decode_gqa_attn(q, k_cache, v_cache, seqlen, *, row_map=None, scale: float, 
     return out
 
 
+def decode_gqa_attn_qk(qkv, q_weight, k_weight, cos, sin, k_cache, v_cache, seqlen, *, row_map=None, num_heads,
+                       num_kv_heads, head_dim, rotary_dim, use_rope, eps, scale: float, window: int | None,
+                       split_len: int | None = None):
+    """:func:`apply_qkv_decode` (RoPE tables read at ``clamp(seqlen[b])``)
+    followed by :func:`decode_gqa_attn` with ``kv_final`` in one launch: the
+    decode branch of reference model.py:368-414 over kernels/decode_attn.py
+    :362-439 and :470-592.  Every K/V position before ``seqlen[b]`` must be
+    final (decode rows, not a prompt's rows).  Returns ``[B, H, 1, D]``; the
+    new K/V rows are written to the caches as apply_qkv_decode writes them."""
+    op = "decode_gqa_attn_qk"
+    if qkv.ndim != 2 or qkv.stride(1) != 1:
+        raise ValueError(f"decode_gqa_attn_qk expects a row-contiguous [B, qkv], got {tuple(qkv.shape)}.")
+    require_cuda(op, qkv, k_cache, v_cache, seqlen)
+    bsz = qkv.shape[0]
+    if row_map is None and (k_cache.shape[0] != bsz or v_cache.shape[0] != bsz):
+        raise ValueError(f"KV cache batch {k_cache.shape[0]} != qkv batch {bsz}.")
+    if seqlen.numel() != bsz:
+        raise ValueError(f"seqlen has {seqlen.numel()} entries, expected {bsz}.")
+    if k_cache.stride(3) != 1 or k_cache.stride(2) != head_dim or k_cache.stride() != v_cache.stride():
+        raise ValueError("KV caches must be [B, n_kv, T, D] with contiguous (T, D).")
+    if k_cache.dtype != qkv.dtype or v_cache.dtype != qkv.dtype:
+        raise TypeError("KV cache dtype must match qkv dtype.")
+    if num_heads % num_kv_heads:
+        raise ValueError(f"n_q={num_heads} not divisible by n_kv={num_kv_heads}.")
+    n_kv, max_len = k_cache.shape[1], k_cache.shape[2]
+    P = split_len or attn_split_len(max_len, bsz, n_kv)
+    out = torch.empty(bsz, num_heads, 1, head_dim, device=qkv.device, dtype=qkv.dtype)
+    o3 = out[:, :, 0, :]
+    L = lib()
+    nbytes = L.maple_decode_gqa_workspace_bytes(bsz, num_heads, head_dim, max_len, P) if -(-max_len // P) > 16 else 0
+    ws = _ws(qkv.device, nbytes)
+    sl = seqlen.reshape(-1).to(torch.int64)
+    rm = row_map.reshape(-1).to(torch.int32) if row_map is not None else None
+    qw = q_weight.reshape(-1).contiguous()
+    kw = k_weight.reshape(-1).contiguous().to(qw.dtype)
+    rot = max(int(rotary_dim), 0) if use_rope else 0
+    if use_rope and (cos.stride(1) != 1 or sin.stride(1) != 1 or cos.stride(0) != sin.stride(0)):
+        cos, sin = cos.contiguous(), sin.contiguous()
+    check(L.maple_decode_gqa_attn_qk(
+        ptr(qkv), dtype_code(qkv, op), bsz, qkv.stride(0), ptr(qw), ptr(kw), dtype_code(qw, op),
+        ptr(cos) if use_rope else None, ptr(sin) if use_rope else None, dtype_code(cos, op) if use_rope else 0,
+        cos.stride(0) if use_rope else 0, int(cos.shape[0]) if use_rope else 0, rot, int(bool(use_rope)), float(eps),
+        num_heads, ptr(k_cache), ptr(v_cache), k_cache.shape[0], n_kv, k_cache.stride(0), k_cache.stride(1), max_len,
+        head_dim, ptr(sl), ptr(rm), float(scale), int(window or 0), P, ptr(o3), o3.stride(0), o3.stride(1), ptr(ws),
+        ws.numel() if ws is not None else 0, ptr(_err(qkv.device)), stream_ptr(qkv.device)), op)
+    return out
+
+
 def _rtn4_common(x, packed_weight, scales, biases, op):
     require_cuda(op, x, packed_weight, scales, biases)
     _u32(packed_weight, op)

@@ -27,6 +27,7 @@ from maple_flash_dgx_spark_b200.kernels import (
     apply_qkv_decode,
     attn_split_len,
     decode_gqa_attn,
+    decode_gqa_attn_qk,
     moe_plan,
     rms_norm,
     router_topk,
@@ -40,6 +41,13 @@ from maple_flash_dgx_spark_b200.linear import (
 )
 
 MLP_CLAMP = 7.0
+
+
+def _fused_qk_attention() -> bool:
+    """``MAPLE_FUSED_QK_ATTN=0`` keeps QK-norm/RoPE/K-V store as its own launch."""
+    import os
+
+    return os.environ.get("MAPLE_FUSED_QK_ATTN", "1") != "0"
 HEAD_GROUP_SIZE = 64
 
 
@@ -215,6 +223,15 @@ class MapleAttention:
         k_cache, v_cache = cache.k[self.layer_idx], cache.v[self.layer_idx]
         if row_map is None:
             k_cache, v_cache = k_cache[:rows], v_cache[:rows]
+        if kv_final and _fused_qk_attention():
+            # decode rows: QK-norm + RoPE + K/V store inside the attention launch
+            attn = decode_gqa_attn_qk(qkv, self.q_norm.weight, self.k_norm.weight, rotary.cos_table,
+                                      rotary.sin_table, k_cache, v_cache, seqlen, row_map=row_map,
+                                      num_heads=self.num_heads, num_kv_heads=self.num_kv_heads,
+                                      head_dim=self.head_dim, rotary_dim=rotary.rotary_dim, use_rope=self.use_rope,
+                                      eps=self.q_norm.eps, scale=self.scale, window=self.sliding_window,
+                                      split_len=cache.split_len)
+            return self.o_proj(attn.reshape(rows, -1))
         q = apply_qkv_decode(qkv, self.q_norm.weight, self.k_norm.weight, rotary.cos_table, rotary.sin_table,
                              k_cache, v_cache, seqlen, row_map=row_map, num_heads=self.num_heads,
                              num_kv_heads=self.num_kv_heads, head_dim=self.head_dim,

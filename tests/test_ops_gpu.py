@@ -330,3 +330,40 @@ def test_add_norm_router_fused_equals_sequence(cuda, K, T):
     r2, n2, i2, w2 = K.add_rms_norm_router_topk(x, y, w, 1e-6, g, 8)
     for a, b in ((res, r2), (normed, n2), (idx, i2), (wt, w2)):
         torch.testing.assert_close(a, b, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D,T,lens,split,window,remap", [
+    (1, 32, 4, 128, 4096, [4096], 64, 0, False),
+    (1, 32, 4, 128, 768, [640], 32, 0, False),
+    (7, 32, 4, 128, 1024, [1, 63, 64, 65, 300, 511, 1000], 64, 0, False),
+    (2, 2, 2, 64, 64, [20, 64], 32, 0, False),
+    (3, 16, 2, 128, 600, [600, 17, 333], 128, 0, True),
+    (2, 8, 8, 128, 512, [512, 100], 64, 96, False),
+    (1, 32, 4, 128, 8192, [8192], 64, 0, False),
+    (3, 16, 2, 128, 16384, [16384, 9000, 1], 128, 0, True),
+])
+def test_fused_qk_attention_equals_two_launches(cuda, K, B, Hq, Hkv, D, T, lens, split, window, remap):
+    """decode_gqa_attn_qk == apply_qkv_decode + decode_gqa_attn (oracle), out
+    and caches bit for bit, cluster and workspace merges, through a row map."""
+    rs = rng(B * 57 + T)
+    Bc = B + 2 if remap else B
+    qkv, qw, kw, kc, vc, pos, _, _ = _attn_case(rs, B, Hq, Hkv, D, T, lens, Bc=Bc)
+    inv = 1.0 / (1e6 ** (np.arange(0, D, 2, dtype=np.float32) / D))
+    ang = np.outer(np.arange(T, dtype=np.float32), inv)
+    emb = np.concatenate([ang, ang], -1).astype(np.float32)
+    cos_t, sin_t = bf(np.cos(emb)), bf(np.sin(emb))
+    rmap = (np.arange(B, dtype=np.int32)[::-1] + 2).copy() if remap else None
+    kc_d, vc_d = to_dev(kc, cuda, torch.bfloat16), to_dev(vc, cuda, torch.bfloat16)
+    out = K.decode_gqa_attn_qk(to_dev(qkv, cuda, torch.bfloat16), to_dev(qw, cuda), to_dev(kw, cuda),
+                               to_dev(cos_t, cuda, torch.bfloat16), to_dev(sin_t, cuda, torch.bfloat16), kc_d, vc_d,
+                               to_dev(pos, cuda), row_map=None if rmap is None else to_dev(rmap, cuda),
+                               num_heads=Hq, num_kv_heads=Hkv, head_dim=D, rotary_dim=D, use_rope=True, eps=1e-6,
+                               scale=D ** -0.5, window=window or None, split_len=split)
+    kc_o, vc_o = kc.copy(), vc.copy()
+    q_o = oracle.apply_qkv_decode(qkv, qw, kw, cos_t[pos], sin_t[pos], kc_o, vc_o, pos, rmap, num_heads=Hq,
+                                  num_kv_heads=Hkv, head_dim=D)
+    out_o = oracle.decode_gqa(q_o, kc_o, vc_o, pos, rmap, scale=np.float32(D ** -0.5), window=window,
+                              split_len=split)
+    np.testing.assert_array_equal(to_np(out)[:, :, 0], out_o)
+    np.testing.assert_array_equal(to_np(kc_d), kc_o)
+    np.testing.assert_array_equal(to_np(vc_d), vc_o)
