@@ -136,62 +136,73 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
     if (s_last) atomicExch(&p.tickets[tok], 0u);
   }
   __syncthreads();
-  if (!s_last || warp != 0) return;
+  if (!s_last) return;
   __threadfence();
-  // Softmax + top-k on one warp; lane l holds experts l + 32i.
+  // Softmax on warp 0 (lane l holds experts l + 32i), then the top-k: the
+  // order in which repeated argmax (largest first, ties to the lowest index,
+  // NaN never) would pick the experts is each expert's rank, computed by one
+  // thread per expert.
   constexpr int kMaxE = 256;
-  float v[kMaxE / 32];
+  __shared__ float s_prob[kMaxE];
+  __shared__ float s_sel_p[32];
+  __shared__ int s_sel_i[32];
   const float ninf = __int_as_float(0xff800000);
-  float m = ninf;
-#pragma unroll
-  for (int i = 0; i < kMaxE / 32; ++i) {
-    const int ee = lane + 32 * i;
-    v[i] = ee < p.E ? __ldcg(&p.logits[(int64_t)tok * p.E + ee]) : ninf;
-    m = fmaxf(m, v[i]);
-  }
-  m = warp_max(m);
-  // R128 sum of exp: partial j = expert j, j+128 (sequential).
-  float q0 = 0.f, q1 = 0.f, q2 = 0.f, q3 = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxE / 32; ++i) {
-    const int ee = lane + 32 * i;
-    v[i] = ee < p.E ? mexp(__fsub_rn(v[i], m)) : 0.0f;
-    const int j = (i & 3);
-    if (j == 0) q0 = __fadd_rn(q0, v[i]);
-    if (j == 1) q1 = __fadd_rn(q1, v[i]);
-    if (j == 2) q2 = __fadd_rn(q2, v[i]);
-    if (j == 3) q3 = __fadd_rn(q3, v[i]);
-  }
-  const float sum = r128_lane_finish(q0, q1, q2, q3);
-#pragma unroll
-  for (int i = 0; i < kMaxE / 32; ++i) v[i] = (lane + 32 * i < p.E) ? __fdiv_rn(v[i], sum) : ninf;
-  float total = 0.0f;
-  float sel_p = 0.0f;
-  int sel_i = 0;
-  for (int r = 0; r < p.topk; ++r) {
-    float bv = ninf;
-    int bi = 0x7fffffff;
+  if (warp == 0) {
+    float v[kMaxE / 32];
+    float m = ninf;
 #pragma unroll
     for (int i = 0; i < kMaxE / 32; ++i) {
       const int ee = lane + 32 * i;
-      if (v[i] > bv || (v[i] == bv && ee < bi)) { bv = v[i]; bi = ee; }
+      v[i] = ee < p.E ? __ldcg(&p.logits[(int64_t)tok * p.E + ee]) : ninf;
+      m = fmaxf(m, v[i]);
     }
+    m = warp_max(m);
+    // R128 sum of exp: partial j = expert j, j+128 (sequential).
+    float q0 = 0.f, q1 = 0.f, q2 = 0.f, q3 = 0.f;
 #pragma unroll
-    for (int mm = 16; mm >= 1; mm >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, mm);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, mm);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    for (int i = 0; i < kMaxE / 32; ++i) {
+      const int ee = lane + 32 * i;
+      v[i] = ee < p.E ? mexp(__fsub_rn(v[i], m)) : 0.0f;
+      const int j = (i & 3);
+      if (j == 0) q0 = __fadd_rn(q0, v[i]);
+      if (j == 1) q1 = __fadd_rn(q1, v[i]);
+      if (j == 2) q2 = __fadd_rn(q2, v[i]);
+      if (j == 3) q3 = __fadd_rn(q3, v[i]);
     }
-    total = __fadd_rn(total, bv);
-    if (lane == r) { sel_p = bv; sel_i = bi; }
+    const float sum = r128_lane_finish(q0, q1, q2, q3);
 #pragma unroll
-    for (int i = 0; i < kMaxE / 32; ++i)
-      if (lane + 32 * i == bi) v[i] = ninf;
+    for (int i = 0; i < kMaxE / 32; ++i) {
+      const int ee = lane + 32 * i;
+      if (ee < p.E) s_prob[ee] = __fdiv_rn(v[i], sum);
+    }
+    s_sel_p[lane] = ninf;        // picks past the last finite expert: (-inf, INT_MAX)
+    s_sel_i[lane] = 0x7fffffff;
   }
-  const float inv = __fdiv_rn(1.0f, __fadd_rn(total, 1e-20f));
-  if (lane < p.topk) {
-    p.idx[(int64_t)tok * p.topk + lane] = sel_i;
-    p.wt[(int64_t)tok * p.topk + lane] = __fmul_rn(sel_p, inv);
+  __syncthreads();
+  if (tid < p.E) {
+    const float pi = s_prob[tid];
+    if (pi == pi) {
+      int rank = 0;
+#pragma unroll 8
+      for (int j = 0; j < p.E; ++j) {
+        const float pj = s_prob[j];
+        rank += (pj > pi || (pj == pi && j < tid)) ? 1 : 0;
+      }
+      if (rank < p.topk) {
+        s_sel_p[rank] = pi;
+        s_sel_i[rank] = tid;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float total = 0.0f;
+    for (int r = 0; r < p.topk; ++r) total = __fadd_rn(total, s_sel_p[r]);
+    const float inv = __fdiv_rn(1.0f, __fadd_rn(total, 1e-20f));
+    if (lane < p.topk) {
+      p.idx[(int64_t)tok * p.topk + lane] = s_sel_i[lane];
+      p.wt[(int64_t)tok * p.topk + lane] = __fmul_rn(s_sel_p[lane], inv);
+    }
   }
 }
 
