@@ -149,31 +149,43 @@ __device__ __forceinline__ float ldf_rt(const void* p, int64_t i, int f32) {
   return f32 ? static_cast<const float*>(p)[i] : bf16_to_f32(static_cast<const uint16_t*>(p)[i]);
 }
 
-// One warp: RMSNorm (R128 over D) * w, then RoPE of head `base` of a QKV row
-// (the arithmetic of qk_norm_rope_store_kernel); o[u] is the value of dim
-// lane + 32u before its bf16 store.  xh: D floats of warp-private shared memory.
-template <int XT, int D>
-__device__ __forceinline__ void qk_norm_rope_warp(const AttnParams& p, const char* row, int base, const void* w,
-                                                  int64_t pos, float* xh, float (&o)[D / 32]) {
+// QK mode: the q/k norm weights and the RoPE cos/sin row of position pos are
+// static inputs of the launch, staged into shared memory c = [4][D] (q weight,
+// k weight, cos, sin; zero cos/sin past the rotary dims) by the whole CTA.
+template <int D>
+__device__ __forceinline__ void qk_stage_consts(const AttnParams& p, int64_t pos, float* c) {
+  const int64_t cs_row = pos < 0 ? 0 : (pos >= p.cs_len ? p.cs_len - 1 : pos);
+  const char* cs = static_cast<const char*>(p.cos) + cs_row * p.cs_sb * (p.cs_f32 ? 4 : 2);
+  const char* sn = static_cast<const char*>(p.sin) + cs_row * p.cs_sb * (p.cs_f32 ? 4 : 2);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    c[d] = ldf_rt(p.q_w, d, p.w_f32);
+    c[D + d] = ldf_rt(p.k_w, d, p.w_f32);
+    const bool r = p.use_rope && d < p.R;
+    c[2 * D + d] = r ? ldf_rt(cs, d, p.cs_f32) : 0.0f;
+    c[3 * D + d] = r ? ldf_rt(sn, d, p.cs_f32) : 0.0f;
+  }
+}
+
+// One warp: RMSNorm (R128 over D) * w, then RoPE of one head whose values
+// xv[u] (dim lane + 32u) are already loaded -- the arithmetic of
+// qk_norm_rope_store_kernel; o[u] is the value of dim lane + 32u before its
+// bf16 store.  w, cs, sn: the staged weight and cos/sin rows; xh: D floats of
+// warp-private shared memory.
+template <int D>
+__device__ __forceinline__ void qk_norm_rope_vals(const AttnParams& p, const float (&xv)[D / 32], const float* w,
+                                                  const float* cs, const float* sn, float* xh, float (&o)[D / 32]) {
   constexpr int U = D / 32;
   const int lane = threadIdx.x & 31;
-  float xv[U];
   float part[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int u = 0; u < U; ++u) {
-    xv[u] = load_f<XT>(row, base + lane + 32 * u);
-    part[u & 3] = __fmaf_rn(xv[u], xv[u], part[u & 3]);
-  }
+  for (int u = 0; u < U; ++u) part[u & 3] = __fmaf_rn(xv[u], xv[u], part[u & 3]);
   const float rstd = rstd_of(r128_lane_finish(part[0], part[1], part[2], part[3]), D, p.eps);
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const int d = lane + 32 * u;
-    xh[d] = __fmul_rn(__fmul_rn(xv[u], rstd), ldf_rt(w, d, p.w_f32));
+    xh[d] = __fmul_rn(__fmul_rn(xv[u], rstd), w[d]);
   }
   __syncwarp();
-  const int64_t cs_row = pos < 0 ? 0 : (pos >= p.cs_len ? p.cs_len - 1 : pos);
-  const char* cs = static_cast<const char*>(p.cos) + cs_row * p.cs_sb * (p.cs_f32 ? 4 : 2);
-  const char* sn = static_cast<const char*>(p.sin) + cs_row * p.cs_sb * (p.cs_f32 ? 4 : 2);
   const int half = p.R / 2;
 #pragma unroll
   for (int u = 0; u < U; ++u) {
@@ -181,9 +193,9 @@ __device__ __forceinline__ void qk_norm_rope_warp(const AttnParams& p, const cha
     float v = xh[d];
     if (p.use_rope && d < p.R) {
       if (d < half)
-        v = __fadd_rn(__fmul_rn(xh[d], ldf_rt(cs, d, p.cs_f32)), __fmul_rn(-xh[d + half], ldf_rt(sn, d, p.cs_f32)));
+        v = __fadd_rn(__fmul_rn(xh[d], cs[d]), __fmul_rn(-xh[d + half], sn[d]));
       else
-        v = __fadd_rn(__fmul_rn(xh[d], ldf_rt(cs, d, p.cs_f32)), __fmul_rn(xh[d - half], ldf_rt(sn, d, p.cs_f32)));
+        v = __fadd_rn(__fmul_rn(xh[d], cs[d]), __fmul_rn(xh[d - half], sn[d]));
     }
     o[u] = v;
   }
@@ -193,19 +205,32 @@ __device__ __forceinline__ void qk_norm_rope_warp(const AttnParams& p, const cha
 // QK mode: the split's q heads into qsm ([8][D], bf16-rounded values; zero
 // rows beyond G) and, in the split that holds position pos, the new K/V row
 // into the cache and the tiles.  Warp w takes q heads w, w + nwarps, ...;
-// warps 0 / 1 then take the new K / V row.  Ends synchronised.
+// warps 0 / 1 also take the new K / V row, whose loads are issued with the q
+// loads.  c: the staged constants (qk_stage_consts, visible to all threads).
+// Ends synchronised.
 template <int XT, int D>
 __device__ __forceinline__ void qk_fused_rows(const AttnParams& p, int b, int h, int cb, int64_t pos, int t0,
                                               int n, bool active, bool cb_ok, unsigned char* ktile,
-                                              unsigned char* vtile, float* qsm, float* kscr, int nwarps) {
+                                              unsigned char* vtile, float* qsm, float* kscr, const float* c,
+                                              int nwarps) {
   constexpr int U = D / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int es = XT == kBF16 ? 2 : 4;
   const char* row = static_cast<const char*>(p.qkv) + b * p.qkv_sb * es;
+  const bool has_new = active && pos >= t0 && pos < (int64_t)t0 + n && pos < p.T && cb_ok;
+  const bool do_k = has_new && warp == 0, do_v = has_new && warp == 1;
+  float xn[U];
+  if (do_k || do_v) {
+    const int nb = do_k ? p.Hq * D + h * D : (p.Hq + p.Hkv) * D + h * D;
+#pragma unroll
+    for (int u = 0; u < U; ++u) xn[u] = load_f<XT>(row, nb + lane + 32 * u);
+  }
   for (int g = warp; g < 8; g += nwarps) {
     if (g < p.G && active) {
-      float o[U];
-      qk_norm_rope_warp<XT, D>(p, row, (h * p.G + g) * D, p.q_w, pos, qsm + g * D, o);
+      float xq[U], o[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) xq[u] = load_f<XT>(row, (h * p.G + g) * D + lane + 32 * u);
+      qk_norm_rope_vals<D>(p, xq, c, c + 2 * D, c + 3 * D, qsm + g * D, o);
 #pragma unroll
       for (int u = 0; u < U; ++u) qsm[g * D + lane + 32 * u] = XT == kBF16 ? bf16_to_f32(f32_to_bf16(o[u])) : o[u];
     } else {
@@ -213,10 +238,9 @@ __device__ __forceinline__ void qk_fused_rows(const AttnParams& p, int b, int h,
       for (int u = 0; u < U; ++u) qsm[g * D + lane + 32 * u] = 0.0f;
     }
   }
-  const bool has_new = active && pos >= t0 && pos < (int64_t)t0 + n && pos < p.T && cb_ok;
-  if (has_new && warp == 0) {
+  if (do_k) {
     float o[U];
-    qk_norm_rope_warp<XT, D>(p, row, p.Hq * D + h * D, p.k_w, pos, kscr, o);
+    qk_norm_rope_vals<D>(p, xn, c + D, c + 2 * D, c + 3 * D, kscr, o);
     char* dst = static_cast<char*>(const_cast<void*>(p.kc)) + (cb * p.kc_sb + h * p.kc_sh + pos * D) * es;
     unsigned char* tt = ktile + (size_t)(pos - t0) * D * es;
 #pragma unroll
@@ -224,15 +248,13 @@ __device__ __forceinline__ void qk_fused_rows(const AttnParams& p, int b, int h,
       store_f<XT>(dst, lane + 32 * u, o[u]);
       store_f<XT>(tt, lane + 32 * u, o[u]);
     }
-  } else if (has_new && warp == 1) {
-    const int vb = (p.Hq + p.Hkv) * D + h * D;
+  } else if (do_v) {
     char* dst = static_cast<char*>(const_cast<void*>(p.vc)) + (cb * p.vc_sb + h * p.vc_sh + pos * D) * es;
     unsigned char* tt = vtile + (size_t)(pos - t0) * D * es;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const float v = load_f<XT>(row, vb + lane + 32 * u);
-      store_f<XT>(dst, lane + 32 * u, v);
-      store_f<XT>(tt, lane + 32 * u, v);
+      store_f<XT>(dst, lane + 32 * u, xn[u]);
+      store_f<XT>(tt, lane + 32 * u, xn[u]);
     }
   }
   __syncthreads();
@@ -289,7 +311,9 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
   // q of the group's heads while the copies are in flight.
   float qv[8][U];
   if constexpr (QK) {
-    qk_fused_rows<XT, D>(p, b, h, cb, pos, t0, n, true, cb_ok, ktile, vtile, qsm, qsm + 8 * D, 4);
+    qk_stage_consts<D>(p, pos, qsm + 9 * D);
+    __syncthreads();
+    qk_fused_rows<XT, D>(p, b, h, cb, pos, t0, n, true, cb_ok, ktile, vtile, qsm, qsm + 8 * D, qsm + 9 * D, 4);
 #pragma unroll
     for (int g = 0; g < 8; ++g)
 #pragma unroll
@@ -476,6 +500,7 @@ __global__ void __launch_bounds__(256) gqa_cluster_kernel(AttnParams p) {
   float* part_m = part + 8 * D;
   float* part_l = part_m + 8;
   float* kscr = part_l + 8;                                                   // QK: [D] K scratch
+  float* qkc = kscr + D;                                                      // QK: [4][D] constants
 
   const int64_t pos = p.seqlen[b];
   const int kv_len = (int)min(pos + 1, (int64_t)p.T);
@@ -501,6 +526,10 @@ __global__ void __launch_bounds__(256) gqa_cluster_kernel(AttnParams p) {
       bulk_g2s(vtile, vsrc, (unsigned)(n_pre * D * es), &bar[0]);
     }
   }
+  if constexpr (QK) {
+    qk_stage_consts<D>(p, pos, qkc);
+    __syncthreads();
+  }
   pdl_wait();
   pdl_trigger();
   if (tid == 0) {
@@ -515,7 +544,7 @@ __global__ void __launch_bounds__(256) gqa_cluster_kernel(AttnParams p) {
   float qv[8][U];
   if constexpr (QK) {
     // q heads and the newest K/V row from the QKV rows (the merge area holds q until P.V)
-    qk_fused_rows<XT, D>(p, b, h, cb, pos, t0, n, active, cb_ok, ktile, vtile, part, kscr, 8);
+    qk_fused_rows<XT, D>(p, b, h, cb, pos, t0, n, active, cb_ok, ktile, vtile, part, kscr, qkc, 8);
 #pragma unroll
     for (int g = 0; g < 8; ++g)
 #pragma unroll
@@ -796,7 +825,7 @@ static int gqa_common(const void* q, int x_dtype, int64_t batch, int64_t num_hea
     int cl = 1;
     while (cl < ns) cl *= 2;
     const size_t smem = 2 * (size_t)split_len * head_dim * es + 2 * 8 * (size_t)split_len * sizeof(float) +
-                        (8 * (size_t)head_dim + 16) * sizeof(float) + (qk ? (size_t)head_dim * sizeof(float) : 0);
+                        (8 * (size_t)head_dim + 16) * sizeof(float) + (qk ? 5 * (size_t)head_dim * sizeof(float) : 0);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)cl, (unsigned)num_kv_heads, (unsigned)batch);
     cfg.blockDim = dim3(256);
@@ -829,7 +858,7 @@ static int gqa_common(const void* q, int x_dtype, int64_t batch, int64_t num_hea
     return e == cudaSuccess ? kOk : kErrCuda;
   }
   const size_t smem = 2 * (size_t)split_len * head_dim * es + 2 * 8 * (size_t)split_len * sizeof(float) +
-                      (qk ? 9 * (size_t)head_dim * sizeof(float) : 0);
+                      (qk ? 13 * (size_t)head_dim * sizeof(float) : 0);
   dim3 grid((unsigned)ns, (unsigned)num_kv_heads, (unsigned)batch);
   cudaError_t e = cudaSuccess;
   // Long contexts: the splits' merge gets its own launch spread over

@@ -5,17 +5,36 @@
 //                  by kernels/fused_norm.py:164-202 (moe_reduce_add), fused; and
 //                  ternary_expert_down_sum (ternary_expert.py:471-556)
 // moe_reduce_add   reference kernels/fused_norm.py:164-202
+#include <cooperative_groups.h>
+
 #include "fxa.cuh"
 #include "launch.cuh"
 
 namespace mb {
 
+namespace cg = cooperative_groups;
+
+// Thread-block cluster barrier halves (every thread of every CTA executes them).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
 constexpr int kTicketBytesMoe = 1 << 20;
 
 // ----------------------------------------------------------------- router --
 // Logits: one warp per (token, expert), R128 order over K (products x*g added
-// with fmaf).  The last CTA of a token (ticket) runs softmax, top-k by
-// repeated argmax (ties -> lowest index), and the 1/(sum+1e-20) renorm.
+// with fmaf).  One CTA of a token then runs softmax, top-k by repeated argmax
+// (ties -> lowest index), and the 1/(sum+1e-20) renorm: with CL (at most 8
+// CTAs per token, one thread-block cluster) the CTAs write their logits into
+// cluster rank 0's shared memory and rank 0 continues after a cluster
+// barrier; otherwise the logits go through global scratch and the last CTA
+// to take the token's ticket continues.
 struct RouterParams {
   const void* x;       // [T, K]
   const void* gate;    // [E, K]
@@ -38,15 +57,18 @@ struct RouterParams {
 
 constexpr int kRouterWarps = 8;
 
-template <int XT, int GT, bool FUSE>
+template <int XT, int GT, bool FUSE, bool CL>
 __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
   extern __shared__ __align__(16) unsigned char rsm[];  // x as fp32 [K] | gate rows raw [8][K] | (FUSE) y, w [K]
+  constexpr int kMaxE = 256;
+  __shared__ float s_logit[kMaxE];  // CL: every expert's logit (rank 0's copy is filled)
   __shared__ int s_last;
   __shared__ float s_part[128];
   __shared__ float s_rstd;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tok = blockIdx.y;
   const int e0 = blockIdx.x * kRouterWarps;
+  if constexpr (CL) cluster_arrive_relaxed();  // this CTA has started
   // gate rows are weights: loaded before waiting for the activation
   const int ne = min(kRouterWarps, p.E - e0);
   const int ges = GT == kBF16 ? 2 : 4;
@@ -114,6 +136,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
     }
     __syncthreads();
   }
+  if constexpr (CL) cluster_wait_acquire();  // every CTA of the cluster has started
   if (warp < ne) {
     const unsigned char* gr = gs + (size_t)warp * p.K * ges;
     // Lane l owns R128 partials j = l + 32u (elements j, j+128, ...).
@@ -126,23 +149,31 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
       }
     }
     const float logit = r128_lane_finish(pj[0], pj[1], pj[2], pj[3]);
-    if (lane == 0) p.logits[(int64_t)tok * p.E + e0 + warp] = logit;
+    if (lane == 0) {
+      if constexpr (CL) *cg::this_cluster().map_shared_rank(&s_logit[e0 + warp], 0) = logit;
+      else p.logits[(int64_t)tok * p.E + e0 + warp] = logit;
+    }
   }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const unsigned old = atomicAdd(&p.tickets[tok], 1u);
-    s_last = (old == gridDim.x - 1);
-    if (s_last) atomicExch(&p.tickets[tok], 0u);
+  if constexpr (CL) {
+    cluster_arrive_release();
+    cluster_wait_acquire();
+    if (blockIdx.x != 0) return;
+  } else {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const unsigned old = atomicAdd(&p.tickets[tok], 1u);
+      s_last = (old == gridDim.x - 1);
+      if (s_last) atomicExch(&p.tickets[tok], 0u);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
   }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
   // Softmax on warp 0 (lane l holds experts l + 32i), then the top-k: the
   // order in which repeated argmax (largest first, ties to the lowest index,
   // NaN never) would pick the experts is each expert's rank, computed by one
   // thread per expert.
-  constexpr int kMaxE = 256;
   __shared__ float s_prob[kMaxE];
   __shared__ float s_sel_p[32];
   __shared__ int s_sel_i[32];
@@ -153,7 +184,8 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
 #pragma unroll
     for (int i = 0; i < kMaxE / 32; ++i) {
       const int ee = lane + 32 * i;
-      v[i] = ee < p.E ? __ldcg(&p.logits[(int64_t)tok * p.E + ee]) : ninf;
+      if constexpr (CL) v[i] = ee < p.E ? s_logit[ee] : ninf;
+      else v[i] = ee < p.E ? __ldcg(&p.logits[(int64_t)tok * p.E + ee]) : ninf;
       m = fmaxf(m, v[i]);
     }
     m = warp_max(m);
@@ -231,7 +263,10 @@ template <int XT, int AT, int MODE>
 __global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ float s_y[kDownMaxTopk][16];
+  __shared__ float s_a[kDownMaxTopk][16];  // MODE 1: the slots' row scales
+  __shared__ float s_w[kDownMaxTopk];      // MODE 0: the slots' combine weights
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float res = 0.0f;  // residual of row tid (warp 0, lanes < 16)
   const int g = lane >> 2, t = lane & 3;
   const int tok = blockIdx.y;
   const int row_g = blockIdx.x * 16 + g, row_h = row_g + 8;
@@ -257,7 +292,22 @@ __global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
         if (row_h < p.N) wb[i] = ld_stream_u4(codes + (int64_t)row_h * p.nwords + word);
       }
     }
+    // The slot's row scales and combine weight come with the ids (static
+    // weights / the router's output), so they load before the wait too.
+    const void* al = static_cast<const char*>(p.alpha) + (int64_t)e * p.N * (AT == kBF16 ? 2 : 4);
+    float ag = 0.0f, ah = 0.0f;
+    if (t == 0) {
+      if (row_g < p.N) ag = load_f<AT>(al, row_g);
+      if (row_h < p.N) ah = load_f<AT>(al, row_h);
+    }
+    const float w = __ldcg(&p.wt[(int64_t)tok * p.topk + warp]);
     pdl_wait();
+    // the residual row is read right after the wait, beside the activations
+    if (warp == 0 && lane < 16 && p.residual != nullptr) {
+      const int row = blockIdx.x * 16 + lane;
+      if (row < p.N)
+        res = load_f<XT>(static_cast<const char*>(p.residual) + tok * p.res_stride * (XT == kBF16 ? 2 : 4), row);
+    }
     const void* hr = static_cast<const char*>(p.h) +
                      (tok * p.h_tok_stride + warp * p.h_slot_stride) * (XT == kBF16 ? 2 : 4);
     int tot[4];
@@ -267,13 +317,10 @@ __global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
     long long Sg, Sh;
     combine_digits(acc, tot, t, Sg, Sh);
     if (t == 0) {
-      const void* al = static_cast<const char*>(p.alpha) + (int64_t)e * p.N * (AT == kBF16 ? 2 : 4);
       const bool nan_out = bad || s == kFxaNonFinite;
       const float nanv = __int_as_float(0x7fc00000);
       const float vg = nan_out ? nanv : fxa_value(Sg, s);
       const float vh = nan_out ? nanv : fxa_value(Sh, s);
-      const float ag = row_g < p.N ? load_f<AT>(al, row_g) : 0.f;
-      const float ah = row_h < p.N ? load_f<AT>(al, row_h) : 0.f;
       if constexpr (MODE == 0) {
         // the expert output is stored in the activation dtype before the combine
         float yg = __fmul_rn(vg, ag), yh = __fmul_rn(vh, ah);
@@ -283,11 +330,13 @@ __global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
         }
         s_y[warp][g] = yg;
         s_y[warp][g + 8] = yh;
+        if (lane == 0) s_w[warp] = w;
       } else {
         // alpha is applied in the combine below: acc = fmaf(w*S, alpha, acc)
-        const float w = p.wt[(int64_t)tok * p.topk + warp];
         s_y[warp][g] = __fmul_rn(w, vg);
         s_y[warp][g + 8] = __fmul_rn(w, vh);
+        s_a[warp][g] = ag;
+        s_a[warp][g + 8] = ah;
       }
     }
   }
@@ -299,18 +348,10 @@ __global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
     if (row < p.N) {
       float acc = 0.0f;
       for (int sl = 0; sl < p.topk; ++sl) {
-        if constexpr (MODE == 0) {
-          acc = __fmaf_rn(p.wt[(int64_t)tok * p.topk + sl], s_y[sl][tid], acc);
-        } else {
-          int e = p.ids[(int64_t)tok * p.topk + sl];
-          if (e < 0 || e >= p.E) e = 0;
-          const void* al = static_cast<const char*>(p.alpha) + (int64_t)e * p.N * (AT == kBF16 ? 2 : 4);
-          acc = __fmaf_rn(s_y[sl][tid], load_f<AT>(al, row), acc);
-        }
+        if constexpr (MODE == 0) acc = __fmaf_rn(s_w[sl], s_y[sl][tid], acc);
+        else acc = __fmaf_rn(s_y[sl][tid], s_a[sl][tid], acc);
       }
-      if (p.residual != nullptr)
-        acc = __fadd_rn(acc, load_f<XT>(static_cast<const char*>(p.residual) +
-                                            tok * p.res_stride * (XT == kBF16 ? 2 : 4), row));
+      if (p.residual != nullptr) acc = __fadd_rn(acc, res);
       store_f<XT>(static_cast<char*>(p.out) + tok * p.out_stride * (XT == kBF16 ? 2 : 4), row, acc);
     }
   }
@@ -345,6 +386,32 @@ extern "C" int64_t maple_router_topk_workspace_bytes(int64_t tokens, int64_t n_e
   return kTicketBytesMoe + tokens * n_experts * (int64_t)sizeof(float);
 }
 
+// Cluster variants get a (grid.x, 1, 1) cluster per token; the others launch
+// plainly.  Both with PDL.
+static void launch_router(void (*kern)(RouterParams), bool cl, dim3 grid, size_t smem, cudaStream_t st,
+                          const RouterParams& p) {
+  if (smem > 32 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (!cl) {
+    launch_k(kern, grid, dim3(256), smem, st, p);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = grid.x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cudaLaunchKernelEx(&cfg, kern, p);
+}
+
 static int router_common(const void* x, int x_dtype, int64_t x_row_stride, int64_t tokens, int64_t k,
                          const void* gate, int gate_dtype, int64_t n_experts, int64_t topk, int32_t* idx, float* wt,
                          void* workspace, int64_t workspace_bytes, const void* y, const void* norm_w,
@@ -373,16 +440,16 @@ static int router_common(const void* x, int x_dtype, int64_t x_row_stride, int64
   const size_t smem = (size_t)k * sizeof(float) + (size_t)kRouterWarps * k * (gate_dtype == kBF16 ? 2 : 4) +
                       (fuse ? 2 * (size_t)k * sizeof(float) : 0);
   if (smem > 200 * 1024) return kErrShape;
+  // At most 8 CTAs per token (64 experts): one portable cluster per token.
+  const bool cl = grid.x <= 8;
 #define MB_ROUTER(XT, GT)                                                                                       \
   do {                                                                                                          \
     if (fuse) {                                                                                                 \
-      if (smem > 32 * 1024)                                                                                     \
-        cudaFuncSetAttribute(router_kernel<XT, GT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-      launch_k(router_kernel<XT, GT, true>, dim3(grid), dim3(256), smem, st, p);                               \
+      if (cl) launch_router(router_kernel<XT, GT, true, true>, true, grid, smem, st, p);                             \
+      else launch_router(router_kernel<XT, GT, true, false>, false, grid, smem, st, p);                               \
     } else {                                                                                                    \
-      if (smem > 32 * 1024)                                                                                     \
-        cudaFuncSetAttribute(router_kernel<XT, GT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-      launch_k(router_kernel<XT, GT, false>, dim3(grid), dim3(256), smem, st, p);                              \
+      if (cl) launch_router(router_kernel<XT, GT, false, true>, true, grid, smem, st, p);                            \
+      else launch_router(router_kernel<XT, GT, false, false>, false, grid, smem, st, p);                              \
     }                                                                                                           \
   } while (0)
   if (x_dtype == kBF16) {

@@ -272,12 +272,23 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
       }
     }
   }
+  // Row scales and the norm weight are static: they load with the codes,
+  // not after the contraction (each is a DRAM round trip of its own).
+  const void* alpha = static_cast<const char*>(p.alpha) + (int64_t)e * p.alpha_estride * (AT == kBF16 ? 2 : 4);
+  float al_g = 0.0f, al_h = 0.0f;
+  if (wk == 0 && t == 0) {
+    if (ok_g) al_g = load_f<AT>(alpha, row_g);
+    if (ok_h) al_h = load_f<AT>(alpha, row_h);
+  }
+  if constexpr (RMS) {
+    if (dense) stage_row<RT, NT, (8192 * 4 / 16 + NT - 1) / NT>(p.rms_w, p.K, wsm, tid);
+  }
   if (dense) {
     pdl_wait();
     pdl_trigger();
   }
   const void* xr = static_cast<const char*>(p.x) + (z / p.x_div) * p.x_stride * (XT == kBF16 ? 2 : 4);
-  fxa_prologue<XT, RT, RMS, 2, NT>(xr, p.rms_w, p.K, p.eps, 0, iters_total, xsm, wsm, frag, fb);
+  fxa_prologue<XT, RT, RMS, 2, NT>(xr, p.rms_w, p.K, p.eps, 0, iters_total, xsm, wsm, frag, fb, nullptr, 0, dense);
   const int s = fb.s;
   const bool nan_out = (s == kFxaNonFinite) || bad_id;
 
@@ -288,7 +299,6 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
     for (int j = 0; j < 4; ++j) red[wk - 1][wm][lane][j] = acc[j];
   }
   __syncthreads();
-  const void* alpha = static_cast<const char*>(p.alpha) + (int64_t)e * p.alpha_estride * (AT == kBF16 ? 2 : 4);
   char* yz = static_cast<char*>(p.y) + (int64_t)z * p.y_stride * (XT == kBF16 ? 2 : 4);
   if (wk == 0) {
 #pragma unroll
@@ -298,17 +308,17 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
     long long Sg, Sh;
     combine_digits(acc, fb.tot, t, Sg, Sh);
     if (t == 0) {
-      auto value = [&](int row, long long S) -> float {
+      auto value = [&](float a, long long S) -> float {
         float v = nan_out ? __int_as_float(0x7fc00000) : fxa_value(S, s);
         if constexpr (RMS) v = __fmul_rn(v, fb.rstd);
-        return __fmul_rn(v, load_f<AT>(alpha, row));
+        return __fmul_rn(v, a);
       };
       if constexpr (MODE == kSwiglu) {
-        s_val[16 * wm + g] = ok_g ? value(row_g, Sg) : 0.0f;
-        s_val[16 * wm + g + 8] = ok_h ? value(row_h, Sh) : 0.0f;
+        s_val[16 * wm + g] = ok_g ? value(al_g, Sg) : 0.0f;
+        s_val[16 * wm + g + 8] = ok_h ? value(al_h, Sh) : 0.0f;
       } else {
-        if (ok_g) store_f<XT>(yz, row_g, value(row_g, Sg));
-        if (ok_h) store_f<XT>(yz, row_h, value(row_h, Sh));
+        if (ok_g) store_f<XT>(yz, row_g, value(al_g, Sg));
+        if (ok_h) store_f<XT>(yz, row_h, value(al_h, Sh));
       }
     }
   }
