@@ -35,6 +35,17 @@ def _log_print(msg: str) -> None:
     print(msg, flush=True)
 
 
+def resolve_max_tokens(max_tokens: int, prompt_len: int, max_context: int) -> int:
+    """A request's token cap within the context left after its prompt; -1
+    means no cap of its own (reference generate.py:31-38)."""
+    remaining = max(int(max_context) - int(prompt_len), 0)
+    if max_tokens == -1:
+        return remaining
+    if max_tokens < 0:
+        raise ValueError("max_tokens must be >= 0 or -1")
+    return min(int(max_tokens), remaining)
+
+
 def is_greedy(temperature: float, top_k: int) -> bool:
     """Reference generate.py:66-68."""
     return temperature <= 0.0 or top_k == 1
