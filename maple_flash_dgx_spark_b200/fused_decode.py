@@ -166,3 +166,61 @@ def fused_decode_supported(model, cache) -> bool:
         if not hasattr(ly.mlp, "fused_add_norm") or not getattr(ly.self_attn, "qkv_proj", None):
             return False
     return all(t.dtype == torch.bfloat16 for t in cache.k[:1])
+
+
+def phase_report(layers: int = 48, prompt_len: int = 512, seed: int = 1) -> str:
+    """Per-phase timing of one whole-step launch on configs[2]-shaped layers
+    (hidden 2048, 32/4 heads of 128, 64 experts top-8, intermediate 1024; a
+    4096-token vocabulary, since the head is not part of the launch), read
+    from the grid barriers' timestamps: for each phase the median over layers
+    of its work (first release of the previous barrier to the last CTA's
+    arrival), of the barrier itself (last arrival to last release) and of the
+    previous barrier's release spread."""
+    import statistics
+
+    from maple_flash_dgx_spark_b200.kernels import argmax
+    from maple_flash_dgx_spark_b200.model import MapleForCausalLM
+    from maple_flash_dgx_spark_b200.synth import synthetic_config, synthetic_tokens, synthetic_weights
+
+    os.environ["MAPLE_FUSED_DECODE"] = "1"
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = synthetic_config(num_layers=layers, vocab=4096)
+    model = MapleForCausalLM.from_weight_dict(cfg, synthetic_weights(cfg, seed, dev), device=dev)
+    cache = model.make_cache(max_len=prompt_len + 16)
+    with torch.inference_mode():
+        logits = model.forward(synthetic_tokens(seed, prompt_len, cfg["vocab_size"], dev).reshape(1, -1), cache=cache)
+        tok = argmax(logits[:, -1, :]).reshape(1, 1)
+        for _ in range(4):
+            tok = argmax(model.forward(tok, cache=cache)[:, -1, :]).reshape(1, 1)
+        plan = cache._fused_plan
+        plan.enable_trace(True)
+        model.forward(tok, cache=cache)
+        torch.cuda.synchronize(dev)
+        tr = plan.read_trace(model).double()
+        plan.enable_trace(False)
+    names = ["qkv", "attention", "o", "router", "swiglu", "down"]
+    arr, rel = tr[:, 0, :], tr[:, 1, :]
+    work = {n: [] for n in names}
+    wait = {n: [] for n in names}
+    spread = {n: [] for n in names}
+    for b in range(1, tr.shape[0]):
+        n = names[b % 6]
+        work[n].append((arr[b].max() - rel[b - 1].min()).item() / 1000)
+        wait[n].append((rel[b].max() - arr[b].max()).item() / 1000)
+        spread[n].append((rel[b - 1].max() - rel[b - 1].min()).item() / 1000)
+    lines = ["phase      work us  barrier us  release spread us (medians over layers)"]
+    for n in names:
+        lines.append(f"{n:10s} {statistics.median(work[n]):7.2f}  {statistics.median(wait[n]):10.2f}  "
+                     f"{statistics.median(spread[n]):17.2f}")
+    total = (rel[-1].max() - arr[0].min()).item() / 1000
+    lines.append(f"first arrival -> last release: {total:.1f} us over {tr.shape[0]} barriers "
+                 f"({total / layers:.2f} us per layer)")
+    return "\n".join(lines)
+
+
+if __name__ == "__main__":
+    import argparse
+
+    ap = argparse.ArgumentParser(description="Phase timing of the whole-step decode launch (needs a GPU).")
+    ap.add_argument("--layers", type=int, default=48)
+    print(phase_report(ap.parse_args().layers))
