@@ -320,13 +320,17 @@ class PackedEngine:
             if slot != last:
                 self._cache.swap_slots(slot, last)
                 self._slots[slot], self._slots[last] = self._slots[last], self._slots[slot]
-            self._finish_slot(last)
+            row = self._slots[last]
+            # the slot is free and empty before its request is told it is done
             self._cache.reset_slot(last)
             self._slots[last] = None
             self._live -= 1
+            self._finish_row(row)
 
     def _finish_slot(self, slot: int, error: BaseException | None = None) -> None:
-        row = self._slots[slot]
+        self._finish_row(self._slots[slot], error)
+
+    def _finish_row(self, row: _Slot | None, error: BaseException | None = None) -> None:
         if row is None:
             return
         job = row.job
