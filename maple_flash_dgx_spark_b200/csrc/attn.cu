@@ -149,6 +149,35 @@ __device__ __forceinline__ float ldf_rt(const void* p, int64_t i, int f32) {
   return f32 ? static_cast<const float*>(p)[i] : bf16_to_f32(static_cast<const uint16_t*>(p)[i]);
 }
 
+// acc[u] (dim lane + 32u) += sum over positions t < n of p[t] * V[t], one
+// fmaf per position in position order; the shared-memory loads of four
+// positions are issued together ahead of their fmafs.
+template <int XT, int D>
+__device__ __forceinline__ void pv_accumulate(const float* prow, const unsigned char* vtile, int n, int lane,
+                                              float (&acc)[D / 32]) {
+  constexpr int U = D / 32;
+  constexpr int es = XT == kBF16 ? 2 : 4;
+  int t = 0;
+  for (; t + 4 <= n; t += 4) {
+    float pt[4], vv[4][U];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      pt[i] = prow[t + i];
+#pragma unroll
+      for (int u = 0; u < U; ++u) vv[i][u] = load_f<XT>(vtile + (size_t)(t + i) * D * es, lane + 32 * u);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int u = 0; u < U; ++u) acc[u] = __fmaf_rn(pt[i], vv[i][u], acc[u]);
+  }
+  for (; t < n; ++t) {
+    const float pt = prow[t];
+#pragma unroll
+    for (int u = 0; u < U; ++u) acc[u] = __fmaf_rn(pt, load_f<XT>(vtile + (size_t)t * D * es, lane + 32 * u), acc[u]);
+  }
+}
+
 // QK mode: the q/k norm weights and the RoPE cos/sin row of position pos are
 // static inputs of the launch, staged into shared memory c = [4][D] (q weight,
 // k weight, cos, sin; zero cos/sin past the rotary dims) by the whole CTA.
@@ -398,12 +427,7 @@ __global__ void __launch_bounds__(128) gqa_decode_kernel(AttnParams p) {
     float acc[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) acc[u] = 0.0f;
-    for (int t = 0; t < n; ++t) {
-      const float pt = pb[g * P + t];
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        acc[u] = __fmaf_rn(pt, load_f<XT>(vtile + (size_t)t * D * es, lane + 32 * u), acc[u]);
-    }
+    pv_accumulate<XT, D>(pb + g * P, vtile, n, lane, acc);
     const int hq = h * G + g;
     if (ns == 1) {
       char* o = static_cast<char*>(p.out) + (b * p.o_sb + hq * p.o_sh) * es;
@@ -629,12 +653,7 @@ __global__ void __launch_bounds__(256) gqa_cluster_kernel(AttnParams p) {
     float acc[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) acc[u] = 0.0f;
-    for (int t = 0; t < n; ++t) {
-      const float pt = pb[g * P + t];
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        acc[u] = __fmaf_rn(pt, load_f<XT>(vtile + (size_t)t * D * es, lane + 32 * u), acc[u]);
-    }
+    pv_accumulate<XT, D>(pb + g * P, vtile, n, lane, acc);
 #pragma unroll
     for (int u = 0; u < U; ++u) part[g * D + lane + 32 * u] = acc[u];
     if (lane == 0) {
@@ -643,41 +662,42 @@ __global__ void __launch_bounds__(256) gqa_cluster_kernel(AttnParams p) {
     }
   }
   cluster.sync();
-  if (s == 0 && warp < G && ns > 0) {
-    const int g = warp, hq = h * G + g;
-    float mj_all = ninf;
-    if (lane < ns) mj_all = cluster.map_shared_rank(part_m, lane)[g];
-    const float M = warp_max(mj_all);
-    float num[U];
+  // Merge: the cluster's CTAs share the G*D outputs; a thread reads the ns
+  // splits' (m, l, acc) of its head and dimension from their CTAs' shared
+  // memory with all loads issued together, then M = max_j m_j,
+  // w_j = exp(m_j - M), den and num as fmaf chains in split order,
+  // out = num / den.
+  if (ns > 0) {
+    constexpr int kMaxSplits = 16;
+    const int cl = (int)gridDim.x;
+    for (int o = s * (int)blockDim.x + tid; o < G * D; o += cl * (int)blockDim.x) {
+      const int g = o / D, dd = o - g * D;
+      float mj[kMaxSplits], lj[kMaxSplits], aj[kMaxSplits];
 #pragma unroll
-    for (int u = 0; u < U; ++u) num[u] = 0.0f;
-    float den = 0.0f;
-    for (int j0 = 0; j0 < ns; j0 += 4) {
-      float mj[4], lj[4], aj[4][U];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int j = j0 + i;
+      for (int j = 0; j < kMaxSplits; ++j) {
         if (j < ns) {
           const float* rp = cluster.map_shared_rank(part, j);
-          mj[i] = rp[8 * D + g];
-          lj[i] = rp[8 * D + 8 + g];
-#pragma unroll
-          for (int u = 0; u < U; ++u) aj[i][u] = rp[g * D + lane + 32 * u];
+          mj[j] = rp[8 * D + g];
+          lj[j] = rp[8 * D + 8 + g];
+          aj[j] = rp[g * D + dd];
         }
       }
+      float M = ninf;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (j0 + i < ns) {
-          const float w = mexp(__fsub_rn(mj[i], M));
-          den = __fmaf_rn(w, lj[i], den);
+      for (int j = 0; j < kMaxSplits; ++j)
+        if (j < ns) M = fmaxf(M, mj[j]);
+      float num = 0.0f, den = 0.0f;
 #pragma unroll
-          for (int u = 0; u < U; ++u) num[u] = __fmaf_rn(w, aj[i][u], num[u]);
+      for (int j = 0; j < kMaxSplits; ++j) {
+        if (j < ns) {
+          const float w = mexp(__fsub_rn(mj[j], M));
+          den = __fmaf_rn(w, lj[j], den);
+          num = __fmaf_rn(w, aj[j], num);
         }
       }
+      char* out = static_cast<char*>(p.out) + (b * p.o_sb + (h * G + g) * p.o_sh) * es;
+      store_f<XT>(out, dd, __fdiv_rn(num, den));
     }
-    char* o = static_cast<char*>(p.out) + (b * p.o_sb + hq * p.o_sh) * es;
-#pragma unroll
-    for (int u = 0; u < U; ++u) store_f<XT>(o, lane + 32 * u, __fdiv_rn(num[u], den));
   }
   cluster.sync();  // peers keep their shared memory until the merge has read it
 }

@@ -259,8 +259,12 @@ struct DownParams {
 constexpr int kDownMaxIters = 8;
 constexpr int kDownMaxTopk = 8;
 
-template <int XT, int AT, int MODE>
-__global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
+// NI: K iterations held in registers (K <= 256 * NI).  The smaller
+// instantiation (K <= 1024) needs few enough registers for a CTA to become
+// resident beside two CTAs of the SwiGLU launch it follows, so it starts (and
+// loads its expert rows) before that launch ends.
+template <int XT, int AT, int MODE, int NI>
+__global__ void __launch_bounds__(256, NI == 4 ? 3 : 1) down_sum_kernel(DownParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ float s_y[kDownMaxTopk][16];
   __shared__ float s_a[kDownMaxTopk][16];  // MODE 1: the slots' row scales
@@ -281,9 +285,9 @@ __global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
     const bool bad = (e < 0 || e >= p.E);
     if (bad) e = 0;
     const uint32_t* codes = p.codes + (int64_t)e * p.N * p.nwords;
-    uint4 wa[kDownMaxIters], wb[kDownMaxIters];
+    uint4 wa[NI], wb[NI];
 #pragma unroll
-    for (int i = 0; i < kDownMaxIters; ++i) {
+    for (int i = 0; i < NI; ++i) {
       wa[i] = make_uint4(0, 0, 0, 0);
       wb[i] = make_uint4(0, 0, 0, 0);
       const int word = i * 16 + 4 * t;
@@ -313,7 +317,7 @@ __global__ void __launch_bounds__(256) down_sum_kernel(DownParams p) {
     int tot[4];
     const int s = fxa_warp_prologue2<XT>(hr, p.K, p.iters, xsm, frag, tot);
     int acc[4] = {0, 0, 0, 0};
-    contract_tile2<kDownMaxIters>(wa, wb, p.iters, frag, lane, acc);
+    contract_tile2<NI>(wa, wb, p.iters, frag, lane, acc);
     long long Sg, Sh;
     combine_digits(acc, tot, t, Sg, Sh);
     if (t == 0) {
@@ -484,11 +488,15 @@ template <int XT, int AT, int MODE>
 cudaError_t launch_down(const DownParams& p, int T, cudaStream_t st) {
   const size_t per_warp = (size_t)p.iters * 256 * sizeof(uint2) + (size_t)p.K * sizeof(float);
   const size_t smem = per_warp * kDownMaxTopk;
-  auto kern = down_sum_kernel<XT, AT, MODE>;
+  auto kern = p.iters <= 4 ? down_sum_kernel<XT, AT, MODE, 4> : down_sum_kernel<XT, AT, MODE, kDownMaxIters>;
   if (smem > 32 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
+  // whole carveout: room beside the expert SwiGLU CTAs this launch overlaps
+  cudaError_t ce = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared);
+  if (ce != cudaSuccess) return ce;
   dim3 grid((p.N + 15) / 16, T);
   launch_k(kern, dim3(grid), dim3(256), smem, st, p);
   return cudaGetLastError();

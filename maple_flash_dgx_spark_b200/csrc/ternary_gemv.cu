@@ -396,6 +396,11 @@ cudaError_t launch_v2(const TGemvParams& p, int Z, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
+  // The whole shared-memory carveout, so the next launch's CTAs (which start
+  // early under PDL) find room beside these.
+  static const cudaError_t carve =
+      cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (carve != cudaSuccess) return carve;
   return launch_k(kern, grid, dim3(32 * WM * WK), smem, st, p);
 }
 
