@@ -215,6 +215,31 @@ __device__ __forceinline__ void widen_u4(const uint4& r, float* out) {
 // NT * MAXC vectors).  Threads 0..NT-1 of the block take part (the caller
 // synchronises).  Falls back to element loads when src is not 16-byte
 // aligned or n is not a whole number of vectors.
+// stage_row in two halves: each thread's first 16-byte chunk is loaded into a
+// register early (stage_row_issue), so that the load goes out ahead of later
+// traffic, and written out with the remaining chunks by stage_row_finish.
+template <int XT, int NT>
+__device__ __forceinline__ uint4 stage_row_issue(const void* src, int n, int tid) {
+  constexpr int EPC = XT == kBF16 ? 8 : 4;
+  uint4 r = make_uint4(0u, 0u, 0u, 0u);
+  if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && n % EPC == 0 && tid < n / EPC)
+    r = ld_u4(static_cast<const char*>(src) + (size_t)tid * 16);
+  return r;
+}
+
+template <int XT, int NT>
+__device__ __forceinline__ void stage_row_finish(const void* src, int n, float* dst, int tid, const uint4& r) {
+  constexpr int EPC = XT == kBF16 ? 8 : 4;
+  if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && n % EPC == 0) {
+    const int nch = n / EPC;
+    const char* s8 = static_cast<const char*>(src);
+    if (tid < nch) widen_u4<XT>(r, dst + (size_t)tid * EPC);
+    for (int c = tid + NT; c < nch; c += NT) widen_u4<XT>(ld_u4(s8 + (size_t)c * 16), dst + (size_t)c * EPC);
+  } else {
+    for (int k = tid; k < n; k += NT) dst[k] = load_f<XT>(src, k);
+  }
+}
+
 template <int XT, int NT, int MAXC>
 __device__ __forceinline__ void stage_row(const void* src, int n, float* dst, int tid) {
   constexpr int EPC = XT == kBF16 ? 8 : 4;

@@ -248,10 +248,12 @@ __device__ __forceinline__ void fxa_build(const float* xs, int n, int s, bool ba
 template <int XT, int RT, bool RMS, int BITS, int NT>
 __device__ __forceinline__ void fxa_prologue(const void* xr, const void* rms_w, int K, float eps, int k_lo,
                                              int iters, float* xsm, float* wsm, uint2* frag, FxaBlock& fb,
-                                             long long* xg = nullptr, int group = 0, bool w_staged = false) {
+                                             long long* xg = nullptr, int group = 0, bool w_staged = false,
+                                             bool x_staged = false) {
   constexpr int NW = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  stage_row<XT, NT, (8192 * 2 / 16 + NT - 1) / NT>(xr, K, xsm, tid);
+  // x_staged: the caller already wrote x into xsm
+  if (!x_staged) stage_row<XT, NT, (8192 * 2 / 16 + NT - 1) / NT>(xr, K, xsm, tid);
   // w_staged: the caller already copied the norm weight into wsm (before its
   // dependency wait, since the weight is static)
   if constexpr (RMS) {

@@ -236,9 +236,14 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
   float* wsm = xsm + p.K;
 
   const bool dense = p.ids == nullptr;
+  const void* xr = static_cast<const char*>(p.x) + (z / p.x_div) * p.x_stride * (XT == kBF16 ? 2 : 4);
+  uint4 x0 = make_uint4(0u, 0u, 0u, 0u);
   if (!dense) {
     pdl_wait();
     pdl_trigger();
+    // The activation row comes from the previous launch like the ids: its
+    // loads go out before the expert rows', so they do not queue behind them.
+    x0 = stage_row_issue<XT, NT>(xr, p.K, tid);
   }
   int e = 0;
   bool bad_id = false;
@@ -286,9 +291,11 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
   if (dense) {
     pdl_wait();
     pdl_trigger();
+  } else {
+    stage_row_finish<XT, NT>(xr, p.K, xsm, tid, x0);
   }
-  const void* xr = static_cast<const char*>(p.x) + (z / p.x_div) * p.x_stride * (XT == kBF16 ? 2 : 4);
-  fxa_prologue<XT, RT, RMS, 2, NT>(xr, p.rms_w, p.K, p.eps, 0, iters_total, xsm, wsm, frag, fb, nullptr, 0, dense);
+  fxa_prologue<XT, RT, RMS, 2, NT>(xr, p.rms_w, p.K, p.eps, 0, iters_total, xsm, wsm, frag, fb, nullptr, 0, dense,
+                                   !dense);
   const int s = fb.s;
   const bool nan_out = (s == kFxaNonFinite) || bad_id;
 
