@@ -498,7 +498,7 @@ def run_bs64(args):
                      "frac": kv_per_launch / (att_us * 1e-6) / 1e9 / peak, "traffic": None,
                      "algorithmic_bytes": kv_per_launch, "launch_us": att_us, "peak_kind": f"{peak_kind} hbm_gbs"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * T, "d2h_bytes_per_step": 8 * T},
-        "gpu_launches": Kst * ((12 + _attn_launches()) * cfg["num_hidden_layers"] + 4),
+        "gpu_launches": Kst * ((12 + _attn_launches(cache)) * cfg["num_hidden_layers"] + 4),
         "clocks": clocks.summary(),
     }
     if rank == 0:
@@ -667,7 +667,7 @@ def run_long(args):
                      "frac": kv_per_launch / (att_us * 1e-6) / 1e9 / peak, "traffic": None,
                      "algorithmic_bytes": kv_per_launch, "launch_us": att_us, "peak_kind": f"{peak_kind} hbm_gbs"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 8 * B},
-        "gpu_launches": Kst * ((5 + _attn_launches()) * cfg["num_hidden_layers"] + 8),
+        "gpu_launches": Kst * ((5 + _attn_launches(cache)) * cfg["num_hidden_layers"] + 8),
         "clocks": clocks.summary(),
     }
     if flash:
@@ -725,12 +725,14 @@ def _step_launches(n_layers: int) -> int:
     return _attn_launches() * n_layers + 4 * n_layers + 4
 
 
-def _attn_launches() -> int:
+def _attn_launches(cache=None) -> int:
     """Launches of the attention block of a decode layer besides O: QKV + the
-    fused attention, or QKV + QK-norm + attention."""
-    from maple_flash_dgx_spark_b200.model import _fused_qk_attention
+    fused attention, or QKV + QK-norm + attention (the model fuses only where
+    a row's attention splits fit one cluster)."""
+    from maple_flash_dgx_spark_b200.model import _QK_FUSED_MAX_SPLITS, _fused_qk_attention
 
-    return 2 if _fused_qk_attention() else 3
+    splits = 1 if cache is None else -(-int(cache.max_len) // int(cache.split_len))
+    return 2 if _fused_qk_attention() and splits <= _QK_FUSED_MAX_SPLITS else 3
 
 
 def op_breakdown(model, cache, dev):
