@@ -158,8 +158,8 @@ def run_reference(args):
         "impl": "reference", "metric": "decode tok/s (bs1, configs[2])", "value": v, "unit": "tok/s",
         "n_gpus": world, "steps": n, "warmup": args.warmup, "ms_per_step": 1000 * dt / n, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "configs[2] bs1 greedy decode, 48 layers, ctx 512+", "global_batch": 1,
-                   "seq_len": PROMPT_LEN, "parallelism": f"replicas{world}"},
+        "config": {"workload": "configs[2]: 48-layer ternary MoE, bs1 greedy decode after a 512-token prompt",
+                   "global_batch": 1, "seq_len": PROMPT_LEN, "parallelism": "single" if world == 1 else f"replicas{world}"},
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
                          "sample": f"{n} decode tokens (cap {budget_s:.0f}s) of the CPU oracle on {cores} threads"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
