@@ -288,7 +288,7 @@ def main():
                    "l2": "5.3 GB of weights streamed per step (> 126 MB L2), no flush needed"},
         "hbm_roofline_step": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes * (Kst / (ms / 1000.0)) / 1e9,
                               "peak_gbs": peak, "frac": step_bytes * (Kst / (ms / 1000.0)) / 1e9 / peak},
-        "roofline": {"kernel": "ternary_gemv_kernel<swiglu> (expert up|gate + SwiGLU, bs1)", "bound": "hbm",
+        "roofline": {"kernel": "tgemv2_kernel<swiglu> (expert up|gate + SwiGLU, bs1)", "bound": "hbm",
                      "achieved": swiglu_bytes / (launch_us * 1e-6) / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": swiglu_bytes / (launch_us * 1e-6) / 1e9 / peak, "traffic": traffic,
                      "algorithmic_bytes": swiglu_bytes, "launch_us": launch_us, "peak_kind": f"{peak_kind} hbm_gbs"},
