@@ -88,7 +88,7 @@ def rope_tables(head_dim, partial, theta, n):
 class OracleModel:
     """Synthetic model of ``config`` (the engine's synthetic_config) held on the host."""
 
-    def __init__(self, config: dict, seed: int, max_len: int, split_len: int):
+    def _setup(self, config: dict, max_len: int, split_len: int) -> None:
         c = config
         self.c = c
         self.L, self.H, self.V = c["num_hidden_layers"], c["hidden_size"], c["vocab_size"]
@@ -98,6 +98,26 @@ class OracleModel:
         self.group = c["maple_run"]["rtn_4bit"]["group_size"]
         self.T, self.P = max_len, split_len
         self.scale = np.float32(self.D ** -0.5)
+        self.cos, self.sin = rope_tables(self.D, float(c.get("partial_rotary_factor", 0.5)), float(c["rope_theta"]),
+                                         max(self.T, 64))
+        self.emb_rtn = None
+        self.head_biases = None
+        self.pos = 0
+
+    def _layer_attention(self, i: int) -> dict:
+        """Per-layer attention knobs (reference model.py:800-812): RoPE off on
+        global layers when ``nope_on_global_attention``; sliding layers attend
+        to the last ``sliding_window`` positions."""
+        c = self.c
+        kind = list(c["layer_types"])[i]
+        nope = bool(c.get("nope_on_global_attention", True)) and kind == "full_attention"
+        window = int(c.get("sliding_window", 512)) if kind == "sliding_attention" else 0
+        return {"use_rope": not nope, "window": window,
+                "kc": np.zeros((1, self.Hkv, self.T, self.D), np.float32),
+                "vc": np.zeros((1, self.Hkv, self.T, self.D), np.float32)}
+
+    def __init__(self, config: dict, seed: int, max_len: int, split_len: int):
+        self._setup(config, max_len, split_len)
         H, D, E, I = self.H, self.D, self.E, self.I
         self.emb = synth_normal(seed, S_EMB, (self.V, H), 0.02)
         self.head_codes, self.head_scales = synth_rtn4_sym(seed, S_HEAD, self.V, H, self.group, 0.02)
@@ -130,12 +150,53 @@ class OracleModel:
                  synth_normal(seed, s(L_GATEA), (E, I), 0.02, 1e-3, True)], 1))
             lay["down"] = synth_ternary(seed, s(L_DOWN), (E, H, I // 16))
             lay["down_a"] = synth_normal(seed, s(L_DOWNA), (E, H), 0.02, 1e-3, True)
-            lay["kc"] = np.zeros((1, self.Hkv, self.T, D), np.float32)
-            lay["vc"] = np.zeros((1, self.Hkv, self.T, D), np.float32)
+            lay.update(self._layer_attention(i))
             self.layers.append(lay)
-        self.cos, self.sin = rope_tables(D, float(c.get("partial_rotary_factor", 0.5)), float(c["rope_theta"]),
-                                         max(self.T, 64))
-        self.pos = 0
+
+    @classmethod
+    def from_weights(cls, config: dict, weights: dict, max_len: int, split_len: int) -> "OracleModel":
+        """A converted packed-ternary-v1 checkpoint (tensor names of the
+        reference's convert.py:180-303), as the reference loader holds it
+        (model.py:719-832): router and RTN scales/biases in bf16, row_alpha
+        and norm weights in fp32, QKV rows and [up; gate] rows concatenated."""
+        m = cls.__new__(cls)
+        m._setup(config, max_len, split_len)
+        w = {k: np.asarray(v) for k, v in weights.items()}
+        f32 = lambda k: np.ascontiguousarray(w[k], np.float32)  # noqa: E731
+        b16 = lambda k: O.round_bf16(f32(k))  # noqa: E731
+        u32 = lambda k: np.ascontiguousarray(w[k]).view(np.uint32)  # noqa: E731
+        if "model.word_embeddings.scales" in w:
+            m.emb = None
+            m.emb_rtn = (u32("model.word_embeddings.weight"), b16("model.word_embeddings.scales"),
+                         b16("model.word_embeddings.biases") if "model.word_embeddings.biases" in w else None)
+        else:
+            m.emb = b16("model.word_embeddings.weight")
+        m.head_codes, m.head_scales = u32("lm_head.weight"), b16("lm_head.scales")
+        m.head_biases = b16("lm_head.biases") if "lm_head.biases" in w else None
+        m.final_norm = f32("model.norm.weight")
+        m.layers = []
+        for i in range(m.L):
+            p = f"model.layers.{i}"
+            lay = {
+                "in_ln": f32(f"{p}.input_layernorm.weight"),
+                "post_ln": f32(f"{p}.post_attention_layernorm.weight"),
+                "q_norm": f32(f"{p}.self_attn.q_norm.weight"),
+                "k_norm": f32(f"{p}.self_attn.k_norm.weight"),
+                "router": b16(f"{p}.mlp.gate.weight"),
+                "qkv": np.ascontiguousarray(np.concatenate([u32(f"{p}.self_attn.{n}_proj.weight") for n in "qkv"])),
+                "qkv_a": np.concatenate([f32(f"{p}.self_attn.{n}_proj.row_alpha") for n in "qkv"]),
+                "o": u32(f"{p}.self_attn.o_proj.weight"),
+                "o_a": f32(f"{p}.self_attn.o_proj.row_alpha"),
+                "ug": np.ascontiguousarray(np.concatenate([u32(f"{p}.mlp.switch_mlp.up_proj.weight"),
+                                                           u32(f"{p}.mlp.switch_mlp.gate_proj.weight")], 1)),
+                "ug_a": np.ascontiguousarray(np.concatenate([f32(f"{p}.mlp.switch_mlp.up_proj.row_alpha"),
+                                                             f32(f"{p}.mlp.switch_mlp.gate_proj.row_alpha")], 1)),
+                "down": u32(f"{p}.mlp.switch_mlp.down_proj.weight"),
+                "down_a": f32(f"{p}.mlp.switch_mlp.down_proj.row_alpha"),
+            }
+            lay.update(m._layer_attention(i))
+            m.layers.append(lay)
+        return m
 
     def fill_cache(self, seed: int, length: int) -> None:
         """Random cached context: positions [0, length) of K/V bf16 N(0, 1)."""
@@ -150,12 +211,18 @@ class OracleModel:
         pos = np.array([self.pos], np.int64)
         cs_row = min(self.pos, self.cos.shape[0] - 1)
         cos, sin = self.cos[cs_row:cs_row + 1], self.sin[cs_row:cs_row + 1]
-        h = self.emb[token:token + 1]
+        if self.emb_rtn is not None:
+            codes, sc, bi = self.emb_rtn
+            h = O.rtn4_embedding(np.array([token]), codes, sc, bi, self.group)
+        else:
+            h = self.emb[token:token + 1]
         for lay in self.layers:
             qkv = O.ternary_gemv(h, lay["qkv"], lay["qkv_a"], lay["in_ln"], self.eps)
             q = O.apply_qkv_decode(qkv, lay["q_norm"], lay["k_norm"], cos, sin, lay["kc"], lay["vc"], pos,
-                                   num_heads=self.Hq, num_kv_heads=self.Hkv, head_dim=self.D, eps=self.eps)
-            attn = O.decode_gqa(q, lay["kc"], lay["vc"], pos, scale=self.scale, split_len=self.P)
+                                   num_heads=self.Hq, num_kv_heads=self.Hkv, head_dim=self.D,
+                                   use_rope=lay["use_rope"], eps=self.eps)
+            attn = O.decode_gqa(q, lay["kc"], lay["vc"], pos, scale=self.scale, window=lay["window"],
+                                split_len=self.P)
             o = O.ternary_gemv(attn.reshape(1, -1), lay["o"], lay["o_a"])
             res, normed = O.add_rms_norm(h, o, lay["post_ln"], self.eps)
             idx, wt = O.router_topk(normed, lay["router"], self.topk)
@@ -163,7 +230,7 @@ class OracleModel:
             h = O.expert_down_reduce(hs, lay["down"], lay["down_a"], idx, wt, res, mode=0)
         self.pos += 1
         normed = O.rms_norm(h, self.final_norm, self.eps)
-        logits = O.rtn4_gemv(normed, self.head_codes, self.head_scales, None, self.group)
+        logits = O.rtn4_gemv(normed, self.head_codes, self.head_scales, self.head_biases, self.group)
         nxt = int(O.argmax(logits)[0])
         return (nxt, logits[0]) if want_logits else nxt
 

@@ -438,7 +438,9 @@ void orc_decode_gqa(const float* q, int64_t B, int64_t Hq, const float* kc, cons
           for (int64_t t = 0; t < n; ++t) sc[t] = orc_exp(sc[t] - m);
           ls[s] = orc_r128_sum(sc, n);
           ms[s] = m;
-          for (int64_t t = 0; t < n; ++t) pb[t] = bf(sc[t]);
+          /* P rounds to the cache dtype before P.V (decode_attn.py:284-289); an
+           * fp32 cache (out_bf16 == 0) keeps it in fp32 (the IEEE path). */
+          for (int64_t t = 0; t < n; ++t) pb[t] = out_bf16 ? bf(sc[t]) : sc[t];
           for (int64_t d = 0; d < D; ++d) {
             float a = 0.0f;
             for (int64_t t = 0; t < n; ++t) a = fmaf(pb[t], vc[((cb * Hkv + h) * T + t0 + t) * D + d], a);

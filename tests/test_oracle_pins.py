@@ -93,3 +93,113 @@ def test_oracle_ternary_gemv_matches_reference(golden, name):
     y = oracle.ternary_gemv(d["x"], d["packed"], d["alpha"], d["rms_weight"], 1e-6, out_bf16=False)
     # Both accumulate in >= fp32; the reference's tl.rsqrt is approximate.
     np.testing.assert_allclose(y, y_ref, rtol=2e-5, atol=2e-6 * np.abs(y_ref).max())
+
+
+def _close(got, want, rtol, what=""):
+    """max |got - want| <= rtol * max |want| (a scale-relative bound: values
+    near zero carry the row's absolute rounding, not their own)."""
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    assert got.shape == want.shape, (what, got.shape, want.shape)
+    err = np.abs(got - want).max()
+    scale = np.abs(want).max()
+    assert err <= rtol * scale, f"{what}: max err {err:.3g} > {rtol:g} * {scale:.3g}"
+
+
+def _cases(kind):
+    return [n for n, c in CASES.items() if c.kind == kind]
+
+
+# Router: indices bit-exact (ties to the lower index), weights to fp32 rounding.
+@pytest.mark.parametrize("name", _cases("router"))
+def test_oracle_router_matches_reference(golden, name):
+    case = CASES[name]
+    d = case.inputs()
+    idx, wt = oracle.router_topk(d["x"], d["gate"], case.top_k)
+    np.testing.assert_array_equal(idx, golden[f"{name}/idx"])
+    np.testing.assert_allclose(wt, golden[f"{name}/wt"], rtol=2e-6, atol=1e-7)
+    # The margin that makes the selection robust to summation order: the gap
+    # between the 8th and 9th logit (exact in float64), reported per token.
+    logits = d["x"].astype(np.float64) @ d["gate"].astype(np.float64).T
+    srt = -np.sort(-logits, axis=-1)
+    gap = srt[:, case.top_k - 1] - srt[:, case.top_k]
+    print(f"{name}: min top-{case.top_k}/{case.top_k + 1} logit gap {gap.min():.3e}")
+    if case.ties:
+        # duplicated gate rows score alike; the lower index must come first
+        for t in range(idx.shape[0]):
+            pos = {int(e): r for r, e in enumerate(idx[t])}
+            for lo, hi in ((5, 9), (3, 40), (17, 30), (30, 61)):
+                if lo in pos and hi in pos:
+                    assert pos[lo] < pos[hi]
+
+
+@pytest.mark.parametrize("name", _cases("norms"))
+def test_oracle_norms_match_reference(golden, name):
+    d = CASES[name].inputs()
+    _close(oracle.rms_norm(d["x"], d["w"], 1e-6, out_bf16=False), golden[f"{name}/rms"], 1e-6, "rms_norm")
+    res, nrm = oracle.add_rms_norm(d["x"], d["y"], d["w"], 1e-6, out_bf16=False)
+    np.testing.assert_array_equal(res, golden[f"{name}/residual"])
+    _close(nrm, golden[f"{name}/normed"], 1e-6, "add_rms_norm")
+    _close(oracle.moe_reduce_add(d["slots"], d["wt"], d["x"], out_bf16=False), golden[f"{name}/reduce"], 1e-6,
+           "moe_reduce_add")
+    _close(oracle.moe_reduce_add(d["slots"], d["wt"], None, out_bf16=False), golden[f"{name}/reduce_nores"], 1e-6,
+           "moe_reduce_add (no residual)")
+
+
+@pytest.mark.parametrize("name", _cases("experts"))
+def test_oracle_experts_match_reference(golden, name):
+    case = CASES[name]
+    d = case.inputs()
+    h = oracle.expert_swiglu(d["x"], d["ug"], d["ug_a"], d["ids"], out_bf16=False)
+    _close(h, golden[f"{name}/h"], 2e-6, "expert swiglu")
+    T, k = d["ids"].shape
+    y = oracle.expert_gemv(d["h_in"].reshape(T * k, -1), d["down"], d["down_a"], d["ids"].reshape(-1),
+                           out_bf16=False)
+    _close(y.reshape(T, k, -1), golden[f"{name}/down"], 2e-6, "expert down")
+    out = oracle.expert_down_reduce(d["h_in"], d["down"], d["down_a"], d["ids"], d["wt"], d["residual"], mode=1,
+                                    out_bf16=False)
+    _close(out, golden[f"{name}/down_sum"], 2e-6, "expert down_sum")
+    if case.alpha_scale > 0.1:  # the clamp case must actually clamp
+        up_gate = golden[f"{name}/h"]
+        assert np.abs(up_gate).max() > 7.0
+
+
+@pytest.mark.parametrize("name", _cases("attention"))
+def test_oracle_attention_matches_reference(golden, name):
+    case = CASES[name]
+    d = case.inputs()
+    kc, vc = d["kc"].copy(), d["vc"].copy()
+    q = oracle.apply_qkv_decode(d["qkv"], d["qw"], d["kw"], d["cos"], d["sin"], kc, vc, d["seqlen"], d["row_map"],
+                                num_heads=case.hq, num_kv_heads=case.hkv, head_dim=case.d, use_rope=case.use_rope,
+                                eps=1e-6, out_bf16=False)
+    _close(q, golden[f"{name}/q"], 2e-6, "q (QK-norm + RoPE)")
+    rows = np.arange(len(case.lengths)) if d["row_map"] is None else d["row_map"]
+    _close(kc[rows, :, d["seqlen"], :], golden[f"{name}/k_new"], 2e-6, "stored K row")
+    np.testing.assert_array_equal(vc[rows, :, d["seqlen"], :], golden[f"{name}/v_new"])
+    out = oracle.decode_gqa(q, kc, vc, d["seqlen"], d["row_map"], scale=np.float32(case.d ** -0.5),
+                            window=case.window, split_len=64, out_bf16=False)
+    _close(out, golden[f"{name}/out"], 1e-5, "attention out")
+
+
+@pytest.mark.parametrize("name", _cases("rtn4"))
+def test_oracle_rtn4_matches_reference(golden, name):
+    case = CASES[name]
+    d = case.inputs()
+    biases = None if case.symmetric else d["b"]  # symmetric: the oracle's own b = -8 s
+    if case.n_clusters:
+        S = case.cluster_size
+        rows = (d["cids"][:, None] * S + np.arange(S)).reshape(-1)
+        y = oracle.rtn4_gemv(d["x"], d["packed"], d["s"], biases, case.group, row_index=rows, out_bf16=False)
+    else:
+        y = oracle.rtn4_gemv(d["x"], d["packed"], d["s"], biases, case.group, out_bf16=False)
+    _close(y, golden[f"{name}/y"], 2e-6, "rtn4")
+
+
+@pytest.mark.parametrize("name", _cases("sampler"))
+def test_oracle_sampler_matches_reference(golden, name):
+    case = CASES[name]
+    d = case.inputs()
+    got = np.stack([oracle.fused_sample(d["logits"], np.full(case.batch, u, np.float32),
+                                        temperature=case.temperature, top_p=case.top_p, top_k=case.top_k)
+                    for u in d["u"]], axis=1)
+    np.testing.assert_array_equal(got, golden[f"{name}/single"])
+    np.testing.assert_array_equal(got, golden[f"{name}/batched"])
