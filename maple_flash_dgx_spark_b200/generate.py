@@ -2,19 +2,23 @@
 
 Reference: generate.py:91-120 (sample_next), :168-373 (decode graph capture and
 the replay == eager gate), :703-816 (bucketed batch graphs), :842-1028
-(batched_generate), :1107-1281 (run_generate).  Text-side pieces (chat
+(batched_generate), :1107-1281 (run_generate): same entry points, arguments
+and results; the batched driver and graph ladder are this engine's own
+(per-row records, two-cursor slot compaction, a logits-level replay gate).  Text-side pieces (chat
 templates, think/tool parsing, detokenisation) are outside this engine: the
 loop takes and returns token ids.
 """
 
 from __future__ import annotations
 
+import bisect
 import time
 from collections.abc import Callable
 from dataclasses import dataclass, field
 
 import torch
 
+from maple_flash_dgx_spark_b200._lib import raise_device_errors
 from maple_flash_dgx_spark_b200.kernels import (
     MAX_TOP_K,
     argmax,
@@ -99,41 +103,46 @@ def _length_restore(cache, snap):
 
 class DecodeGraph:
     """``forward(tokens)`` plus next-token selection for a fixed batch width,
-    captured in one CUDA graph (reference generate.py:168-227, 703-816).
+    captured in one CUDA graph (reference generate.py:168-227).
 
-    Only lengths are snapshotted around warm-up and capture: the steps write
-    K/V at positions >= each row's length, which attention never reads before
-    the real tokens overwrite them, so the (possibly huge) cache is not
-    copied."""
+    ``tokens`` / ``uniform`` may be buffers shared with graphs of other widths
+    (the first ``width`` entries are this graph's inputs).  Only lengths are
+    snapshotted around warm-up and capture: the steps write K/V at positions
+    >= each row's length, which attention never reads before the real tokens
+    overwrite them, so the (possibly huge) cache is not copied."""
 
-    def __init__(self, model, cache, *, width: int = 1, sample: tuple | None = None):
+    def __init__(self, model, cache, *, width: int = 1, sample: tuple | None = None,
+                 tokens: torch.Tensor | None = None, uniform: torch.Tensor | None = None):
         dev = model.device
         self.width = width
         self.sample = sample
-        self.token_ids = torch.zeros(width, 1, dtype=torch.long, device=dev)
-        self.uniform = torch.zeros(width, dtype=torch.float32, device=dev)
+        self.token_ids = tokens if tokens is not None else torch.zeros(width, 1, dtype=torch.long, device=dev)
+        self.uniform = uniform if uniform is not None else torch.zeros(width, dtype=torch.float32, device=dev)
         snap = _length_snapshot(cache)
         stream = torch.cuda.Stream(dev)
         stream.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(stream):
-            for _ in range(_GRAPH_WARMUP):
-                self._step(model, cache)
-                _length_restore(cache, snap)
-            self.graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(self.graph, stream=stream):
-                self.logits, self.next_id = self._step(model, cache)
-        torch.cuda.current_stream(dev).wait_stream(stream)
-        torch.cuda.synchronize(dev)
-        _length_restore(cache, snap)
+        try:
+            with torch.cuda.stream(stream):
+                for _ in range(_GRAPH_WARMUP):
+                    self._step(model, cache)
+                    _length_restore(cache, snap)
+                self.graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self.graph, stream=stream):
+                    self.logits, self.next_id = self._step(model, cache)
+            torch.cuda.current_stream(dev).wait_stream(stream)
+            torch.cuda.synchronize(dev)
+        finally:
+            _length_restore(cache, snap)
 
     def _step(self, model, cache):
-        logits = model.forward(self.token_ids, cache=cache, logits_to_keep=1)
+        w = self.width
+        logits = model.forward(self.token_ids[:w], cache=cache, logits_to_keep=1)
         last = logits[:, -1, :]
         if self.sample is None:
             nxt = argmax(last)
         else:
             ws, temperature, top_p, top_k = self.sample
-            nxt = fused_sample_batched(last, self.uniform, temperature=temperature, top_p=top_p, top_k=top_k,
+            nxt = fused_sample_batched(last, self.uniform[:w], temperature=temperature, top_p=top_p, top_k=top_k,
                                        workspace=ws)
         return logits, nxt
 
@@ -209,6 +218,7 @@ def run_generate(model, input_ids: torch.Tensor, *, max_tokens: int = 128, tempe
             break
     torch.cuda.synchronize(dev)
     t3 = time.perf_counter()
+    raise_device_errors(dev, "run_generate")
     res = GenerateResult(out, prompt_len, len(out), t1 - t0, t3 - t2, reason, graph is not None)
     if log is not None:
         log(f"Prefill: {prompt_len} tok in {res.prefill_s:.3f}s; decode: {res.n_new} tok in {res.decode_s:.3f}s "
@@ -236,88 +246,115 @@ def stop_token_ids(model, tokenizer=None) -> set[int]:
 
 
 class BucketedDecodeGraphs:
-    """One decode graph per batch width, replayed at the narrowest width that
-    fits the live rows (reference generate.py:703-816).  All widths share the
-    token / uniform buffers.  Rows past the live count are padding: they run
-    against the cache rows above the live ones, so the caller keeps live
-    sequences in the low slots (``KVCache.swap_slots``); the graphs read the
-    slot -> cache-row map, so compaction needs no re-capture."""
+    """Decode graphs for a ladder of batch widths over one cache (the
+    reference's bucketed graphs, generate.py:703-816, same observable
+    behaviour): a step replays the narrowest rung that holds the live rows.
+
+    Every rung is a :class:`DecodeGraph` reading the same token / uniform
+    buffers, so loading a step's inputs is one copy whatever the rung.  Rows
+    between the live count and the rung width are padding that runs on the
+    cache rows above the live ones: callers keep live sequences packed into
+    the low slots (:func:`compact_slots`).  The graphs read the slot ->
+    cache-row map at replay time, so slot moves need no re-capture."""
 
     def __init__(self, model, cache, *, widths: tuple[int, ...], sample: tuple | None = None,
                  log: Callable[[str], None] | None = _log_print):
         if not cache.remap:
             raise ValueError("BucketedDecodeGraphs needs cache.remap enabled.")
-        dev = model.device
-        self.widths = tuple(sorted(set(int(w) for w in widths)))
+        self.widths = tuple(sorted({int(w) for w in widths}))
+        if not self.widths or self.widths[0] < 1:
+            raise ValueError(f"graph widths must be >= 1, got {widths}.")
         self.max_width = self.widths[-1]
         if self.max_width > cache.batch:
             raise ValueError(f"widest graph {self.max_width} exceeds the cache batch {cache.batch}.")
+        dev = model.device
         self.sample = sample
         self.token_ids = torch.zeros(self.max_width, 1, dtype=torch.long, device=dev)
         self.uniform = torch.zeros(self.max_width, dtype=torch.float32, device=dev)
-        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
-        self.next_id: dict[int, torch.Tensor] = {}
-        self.logits: dict[int, torch.Tensor] = {}
-        snap = _length_snapshot(cache)
-        stream = torch.cuda.Stream(dev)
-        try:
-            for w in self.widths:
-                stream.wait_stream(torch.cuda.current_stream(dev))
-                with torch.cuda.stream(stream):
-                    for _ in range(_GRAPH_WARMUP):
-                        self._step(model, cache, w)
-                        _length_restore(cache, snap)
-                    graph = torch.cuda.CUDAGraph()
-                    with torch.cuda.graph(graph, stream=stream):
-                        self.logits[w], self.next_id[w] = self._step(model, cache, w)
-                torch.cuda.current_stream(dev).wait_stream(stream)
-                torch.cuda.synchronize(dev)
-                _length_restore(cache, snap)
-                self.graphs[w] = graph
-        finally:
-            _length_restore(cache, snap)
+        self._rungs = {w: DecodeGraph(model, cache, width=w, sample=sample, tokens=self.token_ids,
+                                      uniform=self.uniform) for w in self.widths}
         if log is not None:
-            log(f"Bucketed decode graphs: widths {list(self.widths)}"
-                + (" with fused sampler" if sample is not None else " greedy"))
-
-    def _step(self, model, cache, w: int):
-        logits = model.forward(self.token_ids[:w], cache=cache, logits_to_keep=1)
-        last = logits[:, -1, :]
-        if self.sample is None:
-            nxt = argmax(last)
-        else:
-            ws, temperature, top_p, top_k = self.sample
-            nxt = fused_sample_batched(last, self.uniform[:w], temperature=temperature, top_p=top_p, top_k=top_k,
-                                       workspace=ws)
-        return logits, nxt
+            log(f"decode graphs at widths {list(self.widths)} ({'sampled' if sample is not None else 'greedy'})")
 
     def width_for(self, live: int) -> int:
-        for w in self.widths:
-            if w >= live:
-                return w
-        raise ValueError(f"live batch {live} exceeds widest graph {self.max_width}.")
+        i = bisect.bisect_left(self.widths, int(live))
+        if i == len(self.widths):
+            raise ValueError(f"live batch {live} exceeds widest graph {self.max_width}.")
+        return self.widths[i]
 
-    def _load(self, tokens, uniform):
+    def _run(self, tokens: torch.Tensor, uniform: torch.Tensor | None) -> tuple[int, DecodeGraph]:
         live = int(tokens.shape[0])
-        w = self.width_for(live)
+        rung = self._rungs[self.width_for(live)]
         self.token_ids[:live].copy_(tokens.reshape(live, 1))
-        if live < w:
-            self.token_ids[live:w].zero_()
+        self.token_ids[live:rung.width].zero_()
         if uniform is not None:
             self.uniform[:live].copy_(uniform.reshape(-1)[:live])
-        return live, w
+        rung.graph.replay()
+        return live, rung
 
     def replay(self, tokens: torch.Tensor, uniform: torch.Tensor | None = None) -> torch.Tensor:
         """Step ``tokens`` ``[live, 1]``; returns the next ids ``[live]``."""
-        live, w = self._load(tokens, uniform)
-        self.graphs[w].replay()
-        return self.next_id[w][:live]
+        live, rung = self._run(tokens, uniform)
+        return rung.next_id[:live]
 
     def replay_logits(self, tokens: torch.Tensor) -> torch.Tensor:
         """Step ``tokens``; returns last-token logits ``[live, vocab]``."""
-        live, w = self._load(tokens, None)
-        self.graphs[w].replay()
-        return self.logits[w][:live].reshape(live, -1)
+        live, rung = self._run(tokens, None)
+        return rung.logits[:live].reshape(live, -1)
+
+
+def checked_decode_graphs(model, cache, probe: list[int], *, sample=None, widths=None,
+                          log: Callable[[str], None] | None = _log_print) -> BucketedDecodeGraphs | None:
+    """Capture the decode graphs and keep them only if a replay reproduces
+    the eager step (reference generate.py:1045-1104, the replay == eager
+    gate).  The probe step feeds ``probe`` (one id per live slot) from the
+    cache's current lengths, once eagerly and once through the graph of its
+    width, and compares the last-token logits bit for bit (a stronger check
+    than the sampled ids, and independent of the sampler's uniforms).  The
+    cache lengths are left as they were."""
+    try:
+        graphs = BucketedDecodeGraphs(model, cache, widths=tuple(widths or decode_buckets(cache.batch)),
+                                      sample=sample, log=log)
+    except Exception as exc:  # capture is an optimisation; eager decode stays correct
+        if log is not None:
+            log(f"CUDA graph capture failed ({exc}); decoding eagerly")
+        return None
+    tokens = torch.tensor(probe, device=model.device, dtype=torch.long).view(-1, 1)
+    snap = _length_snapshot(cache)
+    try:
+        eager = model.forward(tokens, cache=cache, logits_to_keep=1)[:, -1, :].clone()
+        _length_restore(cache, snap)
+        replayed = graphs.replay_logits(tokens).clone()
+    finally:
+        _length_restore(cache, snap)
+    if not torch.equal(eager, replayed):
+        if log is not None:
+            log("CUDA graph replay differs from the eager step; decoding eagerly")
+        return None
+    return graphs
+
+
+def compact_slots(cache, entries: list, keep: list[bool]) -> int:
+    """Pack the kept slots among the first ``len(keep)`` (the live ones) into
+    the low slots and return how many there are.  Two cursors walk inwards:
+    the lowest dropped slot takes the highest kept one (a cache row-map swap,
+    no K/V moves) until they meet, so the fewest swaps fill every hole below
+    the new live count.  ``entries`` (one per slot) and ``keep`` are permuted
+    alongside; entries past the live ones are left alone."""
+    lo, hi = 0, len(keep) - 1
+    while True:
+        while lo <= hi and keep[lo]:
+            lo += 1
+        while hi > lo and not keep[hi]:
+            hi -= 1
+        if lo >= hi:
+            break
+        cache.swap_slots(lo, hi)
+        entries[lo], entries[hi] = entries[hi], entries[lo]
+        keep[lo], keep[hi] = keep[hi], keep[lo]
+        lo += 1
+        hi -= 1
+    return sum(keep)
 
 
 @dataclass
@@ -341,44 +378,54 @@ class BatchedResult:
         return self.n_new / self.decode_s if self.decode_s > 0 else 0.0
 
 
-def _first_id(logits, greedy, temperature, top_p, top_k, gen):
-    last = logits[0, -1]
-    if greedy:
-        return argmax(last)
-    return fused_sample(last, torch.rand((), device=last.device, generator=gen), temperature=temperature,
-                        top_p=top_p, top_k=top_k)
+@dataclass
+class _Row:
+    """One sequence of a batched decode: its output row, cap and the id it
+    will emit next."""
+
+    index: int
+    cap: int
+    nxt: int
+    out: list[int] = field(default_factory=list)
+    reason: str = "length"
+
+    def emit(self, stop_ids: set[int]) -> bool:
+        """Append the pending id; True while the row wants another step."""
+        self.out.append(self.nxt)
+        if self.nxt in stop_ids:
+            self.reason = "stop"
+            return False
+        return len(self.out) < self.cap
 
 
-def _try_batched_decode_graphs(model, cache, pending: list[int], *, sample, buckets=None,
-                               log: Callable[[str], None] | None = _log_print):
-    """Capture the bucketed graphs; keep them only if one replay at the full
-    width gives the eager step's ids (reference generate.py:1045-1104)."""
-    widths = tuple(buckets) if buckets else decode_buckets(cache.batch)
-    try:
-        runner = BucketedDecodeGraphs(model, cache, widths=widths, sample=sample, log=log)
-    except Exception as exc:  # capture is an optimisation; eager decode stays correct
-        if log is not None:
-            log(f"CUDA graph capture failed ({exc}); using eager decode")
-        return None
-    live = len(pending)
-    tokens = torch.tensor(pending, device=model.device, dtype=torch.long).view(live, 1)
-    u = torch.rand(live, device=model.device) if sample is not None else None
-    snap = _length_snapshot(cache)
-    last = model.forward(tokens, cache=cache, logits_to_keep=1)[:, -1, :]
-    if sample is None:
-        eager = argmax(last)
-    else:
-        ws, temperature, top_p, top_k = sample
-        eager = fused_sample_batched(last, u, temperature=temperature, top_p=top_p, top_k=top_k, workspace=ws)
-    eager = eager.tolist()
-    _length_restore(cache, snap)
-    graph = runner.replay(tokens, u).tolist()
-    _length_restore(cache, snap)
-    if eager != graph:
-        if log is not None:
-            log(f"CUDA graph replay diverged (eager {eager[:8]} vs graph {graph[:8]}); using eager decode")
-        return None
-    return runner
+class _Picker:
+    """Next-id selection shared by prefill and decode steps: argmax, or the
+    fused sampler with one uniform per row from the caller's generator."""
+
+    def __init__(self, model, rows: int, *, temperature, top_p, top_k, seed):
+        self.dev = model.device
+        self.greedy = is_greedy(temperature, top_k)
+        if not self.greedy and not can_fuse_sampler(temperature, top_p, top_k):
+            raise ValueError(f"sampled decode needs 0 < top_k <= {MAX_TOP_K} and 0 < top_p <= 1.")
+        self.params = (float(temperature), float(top_p), int(top_k))
+        self.gen = None
+        if seed is not None and not self.greedy:
+            self.gen = torch.Generator(device=self.dev)
+            self.gen.manual_seed(int(seed))
+        self.ws = None if self.greedy else batched_sampler_workspace(model.vocab_size, int(top_k), rows, self.dev)
+
+    @property
+    def graph_sample(self):
+        return None if self.greedy else (self.ws, *self.params)
+
+    def uniforms(self, n: int) -> torch.Tensor | None:
+        return None if self.greedy else torch.rand(n, device=self.dev, generator=self.gen)
+
+    def pick(self, last: torch.Tensor, u: torch.Tensor | None) -> torch.Tensor:
+        if self.greedy:
+            return argmax(last)
+        t, p, k = self.params
+        return fused_sample_batched(last, u, temperature=t, top_p=p, top_k=k, workspace=self.ws)
 
 
 @torch.inference_mode()
@@ -387,111 +434,73 @@ def batched_generate(model, prompts, *, max_tokens: int = 128, max_new: list[int
                      stop_ids: set[int] | None = None, cache=None, graphs: bool = False,
                      buckets: tuple[int, ...] | None = None, runner: BucketedDecodeGraphs | None = None,
                      log: Callable[[str], None] | None = _log_print) -> BatchedResult:
-    """Decode several sequences in one batch (reference generate.py:842-1028).
+    """Decode several sequences as one batch (reference generate.py:842-1028,
+    same arguments and result).
 
-    Each prompt is prefilled into its own cache slot; decode goes wide, so the
-    batched GEMMs read every weight once per step for all rows.  Finished
-    rows are swapped out of the low slots; with ``graphs`` each step replays
-    the narrowest captured width that holds the live rows."""
+    Each prompt is prefilled into cache slot i; decode then runs all live
+    rows per step, so the batched GEMMs read every weight once per step.  A
+    row leaves the batch when it emits a stop id or reaches its cap (its own
+    ``max_new`` entry, else ``max_tokens``); the survivors are packed into
+    the low slots, and with ``graphs`` each step replays the narrowest
+    captured width holding them."""
     dev = model.device
-    rows = [torch.as_tensor(p, device=dev, dtype=torch.long).reshape(-1) for p in prompts]
-    if not rows:
+    seqs = [torch.as_tensor(p, device=dev, dtype=torch.long).reshape(-1) for p in prompts]
+    n = len(seqs)
+    if n == 0:
         raise ValueError("batched_generate needs at least one prompt.")
-    bsz = len(rows)
-    prompt_lens = [int(t.numel()) for t in rows]
-    if max_new is None:
-        caps = [int(max_tokens)] * bsz
-    else:
-        if len(max_new) != bsz:
-            raise ValueError(f"max_new length {len(max_new)} != {bsz} prompts.")
-        caps = [int(c) for c in max_new]
-        if any(c < 1 for c in caps):
-            raise ValueError("each max_new row must be >= 1")
-    horizon = max(caps)
-    if stop_ids is None:
-        stop_ids = stop_token_ids(model)
-    need = max(prompt_lens) + max(horizon, 1)
+    caps = [int(max_tokens)] * n if max_new is None else [int(c) for c in max_new]
+    if len(caps) != n:
+        raise ValueError(f"max_new has {len(caps)} entries for {n} prompts.")
+    if min(caps) < 1:
+        raise ValueError("every row needs a cap of at least one token.")
+    prompt_lens = [int(t.numel()) for t in seqs]
+    need = max(prompt_lens) + max(caps)
     if cache is None:
-        cache = model.make_cache(max_len=need, batch=bsz)
-    elif cache.batch < bsz:
-        raise ValueError(f"cache batch {cache.batch} < {bsz} prompts.")
-    elif cache.max_len < need:
-        raise ValueError(f"cache max_len {cache.max_len} < longest prompt {max(prompt_lens)} + {horizon} tokens.")
+        cache = model.make_cache(max_len=need, batch=n)
+    elif cache.batch < n or cache.max_len < need:
+        raise ValueError(f"cache ({cache.batch} rows x {cache.max_len}) cannot hold {n} rows of {need} positions.")
     else:
         cache.reset_identity()
-    greedy = is_greedy(temperature, top_k)
-    if not greedy and not can_fuse_sampler(temperature, top_p, top_k):
-        raise ValueError(f"batched decode needs 0 < top_k <= {MAX_TOP_K} and 0 < top_p <= 1.")
-    gen = None
-    if seed is not None:
-        gen = torch.Generator(device=dev)
-        gen.manual_seed(int(seed))
+    stops = stop_token_ids(model) if stop_ids is None else set(stop_ids)
+    picker = _Picker(model, cache.batch, temperature=temperature, top_p=top_p, top_k=top_k, seed=seed)
 
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
-    pending = [0] * bsz
-    for b, row in enumerate(rows):
-        with cache.prefill_slot(b):
-            logits = model.forward(row.view(1, -1), cache=cache, logits_to_keep=1)
-        pending[b] = int(_first_id(logits, greedy, temperature, top_p, top_k, gen))
+    rows: list[_Row] = []
+    for i, ids in enumerate(seqs):
+        with cache.prefill_slot(i):
+            last = model.forward(ids.view(1, -1), cache=cache, logits_to_keep=1)[:, -1, :]
+        rows.append(_Row(index=i, cap=caps[i], nxt=int(picker.pick(last, picker.uniforms(1))[0])))
     torch.cuda.synchronize(dev)
     prefill_s = time.perf_counter() - t0
 
     cache.remap = True
-    sample_ws = None
-    if not greedy:
-        sample_ws = batched_sampler_workspace(model.vocab_size, int(top_k), cache.batch, dev)
     if graphs and runner is None:
-        runner = _try_batched_decode_graphs(model, cache, pending,
-                                            sample=None if greedy else (sample_ws, temperature, top_p, top_k),
-                                            buckets=buckets, log=log)
-
-    def step(tokens):
-        live = int(tokens.shape[0])
-        u = None if greedy else torch.rand(live, device=dev, generator=gen)
-        if runner is not None:
-            return runner.replay(tokens, u)
-        last = model.forward(tokens, cache=cache, logits_to_keep=1)[:, -1, :]
-        if greedy:
-            return argmax(last)
-        return fused_sample_batched(last, u, temperature=temperature, top_p=top_p, top_k=top_k, workspace=sample_ws)
-
-    out: list[list[int]] = [[] for _ in range(bsz)]
-    reasons = ["length"] * bsz
-    owner = list(range(bsz))  # slot -> output row
-    live, steps = bsz, 0
+        runner = checked_decode_graphs(model, cache, [r.nxt for r in rows], sample=picker.graph_sample,
+                                       widths=buckets, log=log)
     widths: list[int] = []
+    steps = 0
     t0 = time.perf_counter()
-    for i in range(int(horizon)):
-        finished = []
-        for slot in range(live):
-            b = owner[slot]
-            out[b].append(pending[slot])
-            if pending[slot] in stop_ids:
-                reasons[b] = "stop"
-                finished.append(slot)
-            elif len(out[b]) >= caps[b]:
-                reasons[b] = "length"
-                finished.append(slot)
-        if i + 1 >= int(horizon):
+    live = n
+    while live:
+        keep = [r.emit(stops) for r in rows[:live]]
+        live = compact_slots(cache, rows, keep)
+        if not live:
             break
-        for slot in reversed(finished):  # descending: a slot pulled down was never retired here
-            last_slot = live - 1
-            if slot != last_slot:
-                cache.swap_slots(slot, last_slot)
-                owner[slot], owner[last_slot] = owner[last_slot], owner[slot]
-                pending[slot], pending[last_slot] = pending[last_slot], pending[slot]
-            live -= 1
-        if live == 0:
-            break
-        tokens = torch.tensor(pending[:live], device=dev, dtype=torch.long).view(live, 1)
-        nxt = step(tokens)
-        pending[:live] = [int(x) for x in nxt.tolist()]
-        steps += 1
+        tokens = torch.tensor([r.nxt for r in rows[:live]], device=dev, dtype=torch.long).view(live, 1)
+        u = picker.uniforms(live)
         if runner is not None:
-            width = runner.width_for(live)
-            widths.append(width)
-            cache.advance_host(1, width)
+            nxt = runner.replay(tokens, u)
+            widths.append(runner.width_for(live))
+            cache.advance_host(1, widths[-1])
+        else:
+            nxt = picker.pick(model.forward(tokens, cache=cache, logits_to_keep=1)[:, -1, :], u)
+        for r, tok in zip(rows, nxt.tolist()):
+            r.nxt = int(tok)
+        steps += 1
     torch.cuda.synchronize(dev)
     decode_s = time.perf_counter() - t0
-    return BatchedResult(out, prompt_lens, reasons, prefill_s, decode_s, steps, widths)
+    raise_device_errors(dev, "batched_generate")
+    by_index = sorted(rows, key=lambda r: r.index)
+    return BatchedResult([r.out for r in by_index], prompt_lens, [r.reason for r in by_index], prefill_s, decode_s,
+                         steps, widths)

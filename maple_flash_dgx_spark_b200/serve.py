@@ -1,17 +1,25 @@
 """Continuous-batching decode worker over persistent KV-cache slots.
 
-Reference: server.py:352-795 (``PackedEngine``).  One worker thread owns the
-model and a KV cache of ``max_batch`` rows.  Requests queue up; the worker
-prefills each admitted request into a free cache slot, decodes all live slots
-together (one bucketed decode graph per width, the narrowest that holds the
-live rows), samples every row with its own sampling parameters, and retires
-finished rows by swapping them above the live ones, so the live rows stay
-dense in the low slots.  Requests carry and return token ids: the HTTP /
-OpenAI protocol, chat templates and detokenisation are outside this engine.
+Reference: server.py:352-795 (``PackedEngine``): same client API
+(``run`` / ``wait_ready`` / ``close``, ``ServerDefaults``, ``Sampling``,
+``RequestError``) and the same observable scheduling -- a request joins a
+free cache slot as soon as one is free, every live slot decodes in the same
+step, each row samples with its own parameters and generator, and a request
+ends at a stop id, at its cap, or when its slot's cache is full.
+
+The worker here is this engine's own design.  One thread owns the model and
+a KV cache of ``max_batch`` rows and repeats a round: take queued requests
+into the free slots (prefill + first id), run one decode step for all live
+slots (the narrowest captured graph that holds them), deliver each produced
+id at once, then pack the surviving slots into the low rows with the
+two-cursor :func:`compact_slots` and reset the rows that were freed.  Token
+ids go in and come out: the HTTP / OpenAI protocol, chat templates and
+detokenisation are outside this engine.
 """
 
 from __future__ import annotations
 
+import itertools
 import queue
 import threading
 import time
@@ -21,13 +29,15 @@ from typing import Any
 
 import torch
 
+from maple_flash_dgx_spark_b200._lib import raise_device_errors
 from maple_flash_dgx_spark_b200.generate import (
     DEFAULT_TEMPERATURE,
     DEFAULT_TOP_K,
     DEFAULT_TOP_P,
     GenerateResult,
-    _try_batched_decode_graphs,
     can_fuse_sampler,
+    checked_decode_graphs,
+    compact_slots,
     is_greedy,
     resolve_max_tokens,
     stop_token_ids,
@@ -36,7 +46,6 @@ from maple_flash_dgx_spark_b200.kernels import (
     MAX_TOP_K,
     argmax,
     batched_sampler_workspace,
-    fused_sample,
     fused_sample_batched,
 )
 
@@ -77,7 +86,9 @@ class Sampling:
 
 
 @dataclass
-class _Job:
+class _Request:
+    """A queued request and the handle its caller waits on."""
+
     input_ids: Any
     sampling: Sampling
     stop_ids: set[int] | None = None
@@ -86,19 +97,35 @@ class _Job:
     result: GenerateResult | None = None
     error: BaseException | None = None
 
+    def fail(self, exc: BaseException) -> None:
+        if self.error is None and self.result is None:
+            self.error = exc
+        self.done.set()
+
 
 @dataclass
-class _Slot:
-    job: _Job
-    pending: int                 # sampled, not yet emitted nor fed back
-    max_tokens: int
+class _Active:
+    """A request decoding in a cache slot: what it has emitted and the id it
+    feeds to the next step."""
+
+    request: _Request
+    cap: int
     prompt_len: int
     prefill_s: float
-    decode_t0: float
-    stop_ids: set[int]
+    started: float
+    stops: set[int]
     generator: torch.Generator | None
-    token_ids: list[int] = field(default_factory=list)
-    finish_reason: str = "length"
+    nxt: int = 0
+    out: list[int] = field(default_factory=list)
+    reason: str = "length"
+
+    @property
+    def sample_key(self):
+        s = self.request.sampling
+        return None if is_greedy(s.temperature, s.top_k) else (s.temperature, s.top_p, s.top_k)
+
+
+_CLOSE = object()
 
 
 def _log(msg: str) -> None:
@@ -119,27 +146,35 @@ class PackedEngine:
         if self.max_batch < 1 or self.max_len < 2:
             raise ValueError("PackedEngine needs max_batch >= 1 and max_len >= 2.")
         self._log = log
-        self._queue: queue.Queue[_Job | None] = queue.Queue()
+        self._inbox: queue.Queue = queue.Queue()
         self._ready = threading.Event()
-        self._stop = threading.Event()
+        self._closing = threading.Event()
         self._start_error: BaseException | None = None
-        self._live = 0
-        self._slots: list[_Slot | None] = [None] * self.max_batch
+        self._slots: list[_Active] = []   # slot i holds _slots[i]; live slots are always the low ones
         self._cache = None
-        self._runner = None
+        self._graphs = None
         self._sample_ws = None
-        self._worker = threading.Thread(target=self._run, name="maple-batch", daemon=True)
+        self._worker = threading.Thread(target=self._worker_main, name="maple-batch", daemon=True)
         self._worker.start()
 
     # ---------------------------------------------------------------- client
+    @property
+    def live(self) -> int:
+        """Requests decoding right now (one per occupied cache slot)."""
+        return len(self._slots)
+
+    @property
+    def cache(self):
+        return self._cache
+
     def wait_ready(self) -> None:
         self._ready.wait()
         if self._start_error is not None:
             raise self._start_error
 
     def close(self) -> None:
-        self._stop.set()
-        self._queue.put(None)
+        self._closing.set()
+        self._inbox.put(_CLOSE)
         self._worker.join(timeout=30)
 
     def run(self, input_ids, *, max_tokens: int = 128, temperature: float = 0.0, top_p: float = 1.0,
@@ -158,235 +193,187 @@ class PackedEngine:
         if not is_greedy(sampling.temperature, sampling.top_k) and not can_fuse_sampler(
                 sampling.temperature, sampling.top_p, sampling.top_k):
             raise RequestError(f"sampling needs 0 < top_k <= {MAX_TOP_K} and 0 < top_p <= 1.")
-        job = _Job(input_ids=input_ids, sampling=sampling, stop_ids=stop_ids, on_token=on_token)
-        self._queue.put(job)
-        job.done.wait()
-        if job.error is not None:
-            raise job.error
-        assert job.result is not None
-        return job.result
+        req = _Request(input_ids=input_ids, sampling=sampling, stop_ids=stop_ids, on_token=on_token)
+        self._inbox.put(req)
+        req.done.wait()
+        if req.error is not None:
+            raise req.error
+        assert req.result is not None
+        return req.result
 
     # ---------------------------------------------------------------- worker
-    def _run(self) -> None:
+    def _worker_main(self) -> None:
         try:
-            self._setup()
-        except Exception as exc:  # reported to every waiter through wait_ready
+            self._prepare()
+        except Exception as exc:  # reported to every caller through wait_ready
             self._start_error = exc
             self._ready.set()
             return
         self._ready.set()
-        try:
-            with torch.inference_mode():
-                while True:
-                    if not self._admit():
-                        break
-                    if self._live == 0:
-                        continue
-                    self._emit_and_retire()
-                    if self._live == 0:
-                        continue
-                    if self._stop.is_set():
-                        self._drain_stop()
-                        break
-                    self._decode_step()
-        except Exception as exc:
-            self._fail_all(exc)
+        with torch.inference_mode():
+            try:
+                while self._round():
+                    pass
+            except Exception as exc:
+                for a in self._slots:
+                    a.request.fail(exc)
+                self._slots = []
+            self._shut()
 
-    def _setup(self) -> None:
+    def _prepare(self) -> None:
+        """Cache of ``max_batch`` slots and the checked decode graphs (greedy
+        logits graphs; sampling runs after the replay, per row group)."""
         model = self.model
         dev = model.device
         torch.cuda.set_device(dev)
         if getattr(model, "lm_head_flash", None) is not None:
-            # FlashHead is a batch-1 head; batched rows use the exact head
-            model.lm_head_flash = None
+            model.lm_head_flash = None  # FlashHead is a batch-1 head; batched rows use the exact head
             if self._log is not None:
                 self._log("continuous batch uses the exact lm_head (FlashHead is B=1 only)")
         with torch.inference_mode():
-            self._cache = model.make_cache(max_len=self.max_len, batch=self.max_batch)
-            dummy = torch.zeros(1, 1, dtype=torch.long, device=dev)
-            pending: list[int] = []
-            for b in range(self.max_batch):
-                with self._cache.prefill_slot(b):
-                    logits = model.forward(dummy, cache=self._cache, logits_to_keep=1)
-                pending.append(int(argmax(logits[0, -1])))
-            self._cache.remap = True
-            self._runner = _try_batched_decode_graphs(model, self._cache, pending, sample=None, log=self._log)
-            for b in range(self.max_batch):
-                self._cache.reset_slot(b)
+            cache = model.make_cache(max_len=self.max_len, batch=self.max_batch)
+            # one position in every slot, so the capture and its probe step attend to real rows
+            one = torch.zeros(1, 1, dtype=torch.long, device=dev)
+            for slot in range(self.max_batch):
+                with cache.prefill_slot(slot):
+                    model.forward(one, cache=cache, logits_to_keep=1)
+            cache.remap = True
+            self._graphs = checked_decode_graphs(model, cache, [0] * self.max_batch, log=self._log)
+            for slot in range(self.max_batch):
+                cache.reset_slot(slot)
+            self._cache = cache
         self._sample_ws = batched_sampler_workspace(int(model.config["vocab_size"]), MAX_TOP_K, self.max_batch, dev)
 
-    def _admit(self) -> bool:
-        """Fill free slots from the queue; False when the worker should exit."""
-        while self._live < self.max_batch:
-            if self._stop.is_set():
-                self._drain_stop()
+    def _round(self) -> bool:
+        """Take queued requests into free slots, then one decode step for
+        the live slots.  False once the engine is closing."""
+        while len(self._slots) < self.max_batch:
+            if self._closing.is_set():
                 return False
-            if self._live == 0:
-                job = self._queue.get()
-            else:
-                try:
-                    job = self._queue.get_nowait()
-                except queue.Empty:
-                    return True
-            if job is None:
-                self._drain_stop()
-                return False
-            self._admit_job(job)
-        return True
-
-    def _drain_stop(self) -> None:
-        while True:
             try:
-                left = self._queue.get_nowait()
+                item = self._inbox.get(block=not self._slots)
             except queue.Empty:
                 break
-            if left is not None:
-                left.error = RuntimeError("engine stopped")
-                left.done.set()
-        for slot in range(self._live):
-            self._finish_slot(slot, error=RuntimeError("engine stopped"))
-        self._live = 0
+            if item is _CLOSE:
+                return False
+            self._admit(item)
+        if self._slots:
+            self._step()
+        return True
 
-    def _admit_job(self, job: _Job) -> None:
-        dev = self.model.device
-        ids = torch.as_tensor(job.input_ids, device=dev, dtype=torch.long).reshape(-1)
-        prompt_len = int(ids.numel())
-        if prompt_len == 0 or prompt_len >= self.max_len:
-            job.error = RequestError(f"prompt length {prompt_len} must be in [1, max_len {self.max_len}).")
-            job.done.set()
+    def _shut(self) -> None:
+        """Fail what is queued or decoding once the engine closes."""
+        stopped = RuntimeError("engine stopped")
+        for a in self._slots:
+            a.request.fail(stopped)
+        self._slots = []
+        while True:
+            try:
+                item = self._inbox.get_nowait()
+            except queue.Empty:
+                return
+            if item is not _CLOSE:
+                item.fail(stopped)
+
+    def _admit(self, req: _Request) -> None:
+        model, dev = self.model, self.model.device
+        ids = torch.as_tensor(req.input_ids, device=dev, dtype=torch.long).reshape(-1)
+        plen = int(ids.numel())
+        if not 0 < plen < self.max_len:
+            req.fail(RequestError(f"prompt length {plen} must be in [1, max_len {self.max_len})."))
             return
         try:
-            cap = resolve_max_tokens(job.sampling.max_tokens, prompt_len, self.max_len)
+            cap = resolve_max_tokens(req.sampling.max_tokens, plen, self.max_len)
         except ValueError as exc:
-            job.error = RequestError(str(exc))
-            job.done.set()
+            req.fail(RequestError(str(exc)))
             return
         if cap <= 0:
-            job.result = GenerateResult([], prompt_len, 0, 0.0, 0.0, "length", self._runner is not None)
-            job.done.set()
+            req.result = GenerateResult([], plen, 0, 0.0, 0.0, "length", self._graphs is not None)
+            req.done.set()
             return
-        slot = self._live
-        self._cache.reset_slot(slot)
-        t0 = time.perf_counter()
-        with self._cache.prefill_slot(slot):
-            logits = self.model.forward(ids.view(1, -1), cache=self._cache, logits_to_keep=1)
-        s = job.sampling
+        s = req.sampling
         gen = None
         if s.seed is not None and not is_greedy(s.temperature, s.top_k):
             gen = torch.Generator(device=dev)
             gen.manual_seed(int(s.seed))
-        pending = int(self._first_id(logits, s, gen))
-        prefill_s = time.perf_counter() - t0
-        stop = job.stop_ids if job.stop_ids is not None else stop_token_ids(self.model, self.tokenizer)
-        self._slots[slot] = _Slot(job=job, pending=pending, max_tokens=cap, prompt_len=prompt_len,
-                                  prefill_s=prefill_s, decode_t0=time.perf_counter(), stop_ids=set(stop),
-                                  generator=gen)
-        self._live += 1
+        stops = req.stop_ids if req.stop_ids is not None else stop_token_ids(model, self.tokenizer)
+        slot = len(self._slots)
+        self._cache.reset_slot(slot)
+        t0 = time.perf_counter()
+        with self._cache.prefill_slot(slot):
+            last = model.forward(ids.view(1, -1), cache=self._cache, logits_to_keep=1)[:, -1, :]
+        entry = _Active(request=req, cap=cap, prompt_len=plen, prefill_s=0.0, started=0.0, stops=set(stops),
+                        generator=gen)
+        first = self._choose(last, [entry])[0]
+        entry.prefill_s = time.perf_counter() - t0
+        entry.started = time.perf_counter()
+        self._slots.append(entry)
+        if not self._deliver(slot, first):
+            self._retire([False if i == slot else True for i in range(len(self._slots))])
 
-    @staticmethod
-    def _first_id(logits, s: Sampling, gen):
-        last = logits[0, -1]
-        if is_greedy(s.temperature, s.top_k):
-            return argmax(last)
-        u = torch.rand((), device=last.device, generator=gen)
-        return fused_sample(last, u, temperature=s.temperature, top_p=s.top_p, top_k=s.top_k)
+    def _deliver(self, slot: int, tok: int) -> bool:
+        """Emit ``tok`` for the request in ``slot``; True while it continues."""
+        a = self._slots[slot]
+        a.out.append(tok)
+        a.nxt = tok
+        if a.request.on_token is not None:
+            try:
+                a.request.on_token(tok)
+            except Exception as exc:  # a failing callback ends its own request only
+                a.request.error = exc
+                return False
+        if tok in a.stops:
+            a.reason = "stop"
+            return False
+        # the cap, or the slot's last cache position used: no room for another step
+        return len(a.out) < a.cap and self._cache.seen[slot] < self.max_len
 
-    def _emit_and_retire(self) -> None:
-        """Emit every live slot's pending id; retire the slots that stop."""
-        done: list[int] = []
-        for slot in range(self._live):
-            row = self._slots[slot]
-            tok = row.pending
-            row.token_ids.append(tok)
-            if row.job.on_token is not None:
-                try:
-                    row.job.on_token(tok)
-                except Exception as exc:  # a failing callback ends its own request only
-                    row.job.error = exc
-                    done.append(slot)
-                    continue
-            if tok in row.stop_ids:
-                row.finish_reason = "stop"
-                done.append(slot)
-            elif len(row.token_ids) >= row.max_tokens:
-                row.finish_reason = "length"
-                done.append(slot)
-            elif self._cache.seen[slot] >= self.max_len:
-                # the slot's last cache position is used: no room for the next step
-                row.finish_reason = "length"
-                done.append(slot)
-        for slot in reversed(done):
-            last = self._live - 1
-            if slot != last:
-                self._cache.swap_slots(slot, last)
-                self._slots[slot], self._slots[last] = self._slots[last], self._slots[slot]
-            row = self._slots[last]
-            # the slot is free and empty before its request is told it is done
-            self._cache.reset_slot(last)
-            self._slots[last] = None
-            self._live -= 1
-            self._finish_row(row)
+    def _retire(self, keep: list[bool]) -> None:
+        """Pack the continuing slots low; free and reset the rest before
+        their callers are told they are done."""
+        n = compact_slots(self._cache, self._slots, keep)
+        gone, self._slots = self._slots[n:], self._slots[:n]
+        for slot, a in enumerate(gone, start=n):
+            self._cache.reset_slot(slot)
+            if a.request.result is None and a.request.error is None:
+                a.request.result = GenerateResult(list(a.out), a.prompt_len, len(a.out), a.prefill_s,
+                                                  max(time.perf_counter() - a.started, 0.0), a.reason,
+                                                  self._graphs is not None)
+            a.request.done.set()
 
-    def _finish_slot(self, slot: int, error: BaseException | None = None) -> None:
-        self._finish_row(self._slots[slot], error)
-
-    def _finish_row(self, row: _Slot | None, error: BaseException | None = None) -> None:
-        if row is None:
-            return
-        job = row.job
-        if error is not None and job.error is None:
-            job.error = error
-        if job.result is None and job.error is None:
-            job.result = GenerateResult(list(row.token_ids), row.prompt_len, len(row.token_ids), row.prefill_s,
-                                        max(time.perf_counter() - row.decode_t0, 0.0), row.finish_reason,
-                                        self._runner is not None)
-        job.done.set()
-
-    def _decode_step(self) -> None:
-        live = self._live
+    def _step(self) -> None:
+        """One decode step of every live slot."""
+        n = len(self._slots)
         dev = self.model.device
-        tokens = torch.tensor([self._slots[s].pending for s in range(live)], device=dev,
-                              dtype=torch.long).view(live, 1)
-        if self._runner is not None:
-            logits = self._runner.replay_logits(tokens)
-            width = self._runner.width_for(live)
-            self._cache.advance_host(1, live)
-            # padding rows of a wider graph ran on free slots: put them back to empty
-            for s in range(live, width):
-                self._cache.reset_slot(s)
+        tokens = torch.tensor([a.nxt for a in self._slots], device=dev, dtype=torch.long).view(n, 1)
+        if self._graphs is not None:
+            logits = self._graphs.replay_logits(tokens)
+            width = self._graphs.width_for(n)
+            self._cache.advance_host(1, n)
+            for slot in range(n, width):  # padding rows of a wider graph ran on free slots
+                self._cache.reset_slot(slot)
         else:
             logits = self.model.forward(tokens, cache=self._cache, logits_to_keep=1)[:, -1, :]
-        for s, tok in enumerate(self._sample_rows(logits)):
-            self._slots[s].pending = int(tok)
+        produced = self._choose(logits, self._slots)
+        raise_device_errors(dev, "PackedEngine decode step")
+        keep = [self._deliver(slot, tok) for slot, tok in enumerate(produced)]
+        if not all(keep):
+            self._retire(keep)
 
-    def _sample_rows(self, logits) -> list[int]:
-        """Greedy rows by argmax; the others grouped by (temperature, top_p,
-        top_k) through the batched fused sampler, each row drawing its
-        uniform from its own generator."""
-        live = logits.shape[0]
+    def _choose(self, logits: torch.Tensor, entries: list[_Active]) -> list[int]:
+        """Next id per row: one argmax over all rows, then each group of
+        sampled rows with equal (temperature, top_p, top_k) through one
+        batched fused-sampler launch, every row drawing its uniform from its
+        own generator."""
         dev = logits.device
-        nxt = torch.empty(live, dtype=torch.long, device=dev)
-        greedy: list[int] = []
-        groups: dict[tuple[float, float, int], list[int]] = {}
-        for s in range(live):
-            sp = self._slots[s].job.sampling
-            if is_greedy(sp.temperature, sp.top_k):
-                greedy.append(s)
-            else:
-                groups.setdefault((sp.temperature, sp.top_p, sp.top_k), []).append(s)
-        if greedy:
-            idx = torch.tensor(greedy, device=dev, dtype=torch.long)
-            nxt[idx] = argmax(logits[idx])
-        for (temperature, top_p, top_k), rows in groups.items():
+        nxt = argmax(logits)
+        sampled = sorted((i for i, a in enumerate(entries) if a.sample_key is not None),
+                         key=lambda i: entries[i].sample_key)
+        for key, grp in itertools.groupby(sampled, key=lambda i: entries[i].sample_key):
+            rows = list(grp)
             idx = torch.tensor(rows, device=dev, dtype=torch.long)
-            u = torch.empty(len(rows), device=dev)
-            for n, s in enumerate(rows):
-                u[n] = torch.rand((), device=dev, generator=self._slots[s].generator)
+            u = torch.stack([torch.rand((), device=dev, generator=entries[i].generator) for i in rows])
+            temperature, top_p, top_k = key
             nxt[idx] = fused_sample_batched(logits[idx], u, temperature=temperature, top_p=top_p, top_k=top_k,
                                             workspace=self._sample_ws)
         return [int(x) for x in nxt.tolist()]
-
-    def _fail_all(self, exc: BaseException) -> None:
-        for slot in range(self._live):
-            self._finish_slot(slot, error=exc)
-        self._live = 0

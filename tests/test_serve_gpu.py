@@ -105,10 +105,10 @@ def test_padding_rows_leave_free_slots_empty(cuda):
     try:
         _concurrently([lambda i=i: eng.run(prompts[i], max_tokens=10 + i, temperature=0.0, top_k=1, stop_ids=set())
                        for i in range(3)])
-        assert eng._live == 0
+        assert eng.live == 0
         for s in range(4):
-            assert eng._cache.seen[s] == 0
-            assert int(eng._cache.seqlen[s]) == 0
+            assert eng.cache.seen[s] == 0
+            assert int(eng.cache.seqlen[s]) == 0
         res = eng.run(prompts[0], max_tokens=12, temperature=0.0, top_k=1, stop_ids=set())
         assert len(res.token_ids) == 12
     finally:
