@@ -98,9 +98,6 @@ _SIGS: dict[str, tuple] = {
     "maple_fused_sample": (i32, [vp, i32, i64, i64, i64, vp, f32, f32, i64, vp, vp, i64, vp]),
     "maple_embedding": (i32, [vp, i64, vp, i32, i64, i64, vp, i32, i64, vp, vp]),
     "maple_rtn4_embedding": (i32, [vp, i64, vp, vp, vp, i32, i64, i64, i64, vp, i32, i64, vp, vp]),
-    "maple_decode_layers_workspace_bytes": (i64, [i64, i64, i64, i64, i64, i64, i64, i64, i64]),
-    "maple_decode_layers": (i32, [vp, i64, vp, vp, vp, vp, vp, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64,
-                                  i64, i64, i64, i64, i64, i64, i32, i32, i32, f32, f32, vp, i64, vp, vp]),
     "maple_synth_ternary": (i32, [ctypes.c_uint64, ctypes.c_uint64, i64, vp, vp]),
     "maple_synth_normal": (i32, [ctypes.c_uint64, ctypes.c_uint64, i64, ctypes.c_double, f32, i32, i32, vp, vp]),
     "maple_synth_rtn4_sym": (i32, [ctypes.c_uint64, ctypes.c_uint64, i64, i64, i64, ctypes.c_double, vp, vp, vp]),
@@ -211,3 +208,18 @@ def take_device_errors(device: torch.device) -> int:
     if v:
         e.zero_()
     return v
+
+
+_DEVICE_FLAGS = {1: "a bounded device wait gave up", 2: "an index or position was out of range"}
+
+
+def raise_device_errors(device: torch.device, where: str) -> None:
+    """Read and clear the device error word; raise if a kernel flagged
+    anything since the last read.  The drivers call this at their existing
+    synchronisation points (end of a generate call, every serve step, every
+    expert-parallel step), so a give-up or a clamped index never passes
+    silently as wrong tokens."""
+    v = take_device_errors(device)
+    if v:
+        what = ", ".join(msg for bit, msg in _DEVICE_FLAGS.items() if v & bit) or f"flags {v:#x}"
+        raise RuntimeError(f"{where}: device error word {v:#x} ({what}); results of this call are not valid.")

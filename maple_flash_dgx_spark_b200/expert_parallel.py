@@ -33,6 +33,7 @@ from maple_flash_dgx_spark_b200 import _lib
 from maple_flash_dgx_spark_b200._lib import check, dtype_code, lib, ptr, stream_ptr
 
 from maple_flash_dgx_spark_b200.kernels import (
+    add_rms_norm,
     argmax,
     ep_combine,
     moe_plan,
@@ -41,6 +42,35 @@ from maple_flash_dgx_spark_b200.kernels import (
     ternary_expert_gemv,
     ternary_expert_swiglu,
 )
+
+PHASES = ("attention", "router", "dispatch", "experts", "combine", "head")
+
+
+class PhaseMarks:
+    """Timing events at the phase boundaries of one decode step, recorded as
+    event nodes when the step is captured in a CUDA graph (``external``
+    events), so a replay can be split into its phases: attention (QKV,
+    attention, O, residual add + norm), router, dispatch, experts (SwiGLU +
+    down), combine, and the sharded head (final norm, row gather, head GEMV,
+    candidate gather).  Phase times are summed over the layers."""
+
+    def __init__(self):
+        self.events: list[tuple[str, torch.cuda.Event]] = []
+
+    def mark(self, name: str) -> None:
+        # only the captured step counts: warm-up steps run eagerly before it
+        if not torch.cuda.is_current_stream_capturing():
+            return
+        ev = torch.cuda.Event(enable_timing=True, external=True)
+        ev.record()
+        self.events.append((name, ev))
+
+    def phase_ms(self) -> dict[str, float]:
+        """Milliseconds per phase of the last replay (events must be complete)."""
+        out = {p: 0.0 for p in PHASES}
+        for (_, a), (name, b) in zip(self.events, self.events[1:]):
+            out[name] += a.elapsed_time(b)
+        return out
 
 _EXPERT_KEYS = ("up_proj", "gate_proj", "down_proj")
 
@@ -250,18 +280,29 @@ class EPMoeBlock:
     def __init__(self, block, exchange: EPExchange):
         self.block = block
         self.ex = exchange
+        self.marks: PhaseMarks | None = None
+
+    def _mark(self, name: str) -> None:
+        if self.marks is not None:
+            self.marks.mark(name)
 
     def __call__(self, hidden_states, residual=None):
         b = self.block
         idx, wt = router_topk(hidden_states, b.gate_weight, b.top_k)
+        self._mark("router")
         x_all, ids_all = self.ex.dispatch(hidden_states, idx)
+        self._mark("dispatch")
         plan = moe_plan(ids_all, self.ex.n_experts, e_first=self.ex.e_first, n_local=self.ex.n_local)
         h = ternary_expert_swiglu(x_all, b.up_gate.packed_weight, b.up_gate.row_alpha, ids_all, plan=plan)
         y = ternary_expert_gemv(h, b.down.packed_weight, b.down.row_alpha, ids_all, plan=plan)
+        self._mark("experts")
         if isinstance(self.ex, EPExchangeP2P):
-            return self.ex.combine(y, idx, wt, residual)
-        recv = self.ex.combine_exchange(y.reshape(-1, y.shape[-1]))
-        return ep_combine(recv, idx, wt, self.ex.n_experts, residual)
+            out = self.ex.combine(y, idx, wt, residual)
+        else:
+            recv = self.ex.combine_exchange(y.reshape(-1, y.shape[-1]))
+            out = ep_combine(recv, idx, wt, self.ex.n_experts, residual)
+        self._mark("combine")
+        return out
 
 
 class EPHead:
@@ -308,18 +349,42 @@ class EPDecoder:
             if not isinstance(layer.mlp, EPMoeBlock):
                 layer.mlp = EPMoeBlock(layer.mlp, exchange)
         self.head = EPHead(model.lm_head, exchange)
+        self.marks: PhaseMarks | None = None
+
+    def set_marks(self, marks: PhaseMarks | None) -> None:
+        """Record phase boundaries into ``marks`` during the next steps
+        (``None`` stops recording)."""
+        self.marks = marks
+        for layer in self.model.layers:
+            layer.mlp.marks = marks
+
+    def _mark(self, name: str) -> None:
+        if self.marks is not None:
+            self.marks.mark(name)
 
     def step(self, tokens: torch.Tensor, cache) -> torch.Tensor:
+        """One decode step; the layer body is MapleDecoderLayer's (attention
+        with the input norm fused into QKV, residual add + post-attention
+        norm, MoE with the residual) written out so phases can be marked."""
         m = self.model
         rows = tokens.shape[0]
         seqlen = cache.seqlen[:rows]
         row_map = cache.row_map[:rows] if cache.remap else None
         m.rotary.ensure_length(cache.max_len)
         hidden = m.embed(tokens.reshape(rows))
+        self._mark("head")  # the step's start; embedding time counts with the head
         for layer in m.layers:
-            hidden = layer(hidden, seqlen, row_map, m.rotary, cache, kv_final=True)
+            attn = layer.self_attn(hidden, seqlen, row_map, m.rotary, cache,
+                                   rms_weight=layer.input_layernorm.weight, rms_eps=layer.input_layernorm.eps,
+                                   kv_final=True)
+            post = layer.post_attention_layernorm
+            hidden, mlp_in = add_rms_norm(hidden, attn, post.weight, post.eps)
+            self._mark("attention")
+            hidden = layer.mlp(mlp_in, residual=hidden)
         cache.advance(1, rows)
-        return self.head.next_ids(m.norm(hidden))
+        ids = self.head.next_ids(m.norm(hidden))
+        self._mark("head")
+        return ids
 
 
 class EPDecodeGraph:
@@ -349,3 +414,10 @@ class EPDecodeGraph:
             self.token_ids.copy_(tokens.reshape(-1, 1))
         self.graph.replay()
         return self.next_id
+
+
+def check_step_errors(device: torch.device) -> None:
+    """Raise if a kernel of the expert-parallel steps run since the last
+    check flagged an error (a peer flag wait that gave up leaves the ranks'
+    exchange counters out of step: the exchange must be rebuilt)."""
+    _lib.raise_device_errors(device, "expert-parallel decode step")

@@ -110,6 +110,18 @@ def test_cfg2_first_64_greedy_ids_equal_oracle(cuda):
     prompt = synth_tokens(gold["seed"], gold["prompt_len"], cfg["vocab_size"])
     res = run_generate(model, torch.from_numpy(prompt), max_tokens=gold["n_new"], temperature=0.0, log=None)
     assert res.token_ids == gold["ids"]
+    # every step's bf16 logits, bit for bit (SHA-1 of the bit patterns): the
+    # whole step, routing of all 48 layers included, equals the oracle's
+    import hashlib
+
+    cache = model.make_cache(max_len=gold["max_len"])
+    logits = model.forward(torch.from_numpy(prompt).to(cuda).reshape(1, -1), cache=cache)[0, -1]
+    for i in range(gold["n_new"]):
+        bits = logits.contiguous().view(torch.int16).cpu().numpy().astype("<i2")
+        assert hashlib.sha1(bits.tobytes()).hexdigest() == gold["logits_sha1"][i], i
+        tok = int(logits.argmax())
+        assert tok == gold["ids"][i]
+        logits = model.forward(torch.tensor([[tok]], device=cuda), cache=cache)[0, -1]
 
 
 def test_batched_decode_equals_single_sequences(cuda):

@@ -48,7 +48,11 @@ def _no_alloc(L, x, codes, alpha, w, batch, n, k, stream):
     return rc, y
 
 
-@pytest.mark.parametrize("batch,n,k,rms", [(1, 2048, 4096, False), (3, 1000, 4096, True), (2, 512, 2048, True)])
+# k=2048: one K split (no scratch); 4096: two; 6144: three; 8192: four splits,
+# whose last-arriving CTA sums the partials of the others through the scratch
+@pytest.mark.parametrize("batch,n,k,rms", [(1, 2048, 4096, False), (3, 1000, 4096, True), (2, 512, 2048, True),
+                                           (1, 1024, 6144, False), (1, 1024, 6144, True), (2, 512, 8192, True),
+                                           (2, 512, 8192, False)])
 def test_no_alloc_equals_workspace_entry_point(cuda, batch, n, k, rms):
     from maple_flash_dgx_spark_b200._lib import lib
 
