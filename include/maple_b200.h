@@ -368,61 +368,6 @@ int maple_quantize_rtn(const void* w, int w_dtype, int64_t rows, int64_t k, int6
 int maple_dequantize_rtn(const uint32_t* packed, const float* scales, const float* biases, int64_t rows, int64_t k,
                          int64_t group_size, float* out, void* stream);
 
-/* ---- whole-stack batch-1 decode (one persistent launch) ----------------
- * Replaces the layer loop of model.py:848-886 (MapleForCausalLM.forward at
- * batch 1, q_len 1) through MapleDecoderLayer :490-506, i.e. per layer the
- * reference's ternary_gemv (RMSNorm->QKV), apply_qkv_decode,
- * decode_gqa_attn, ternary_gemv (O), add_rms_norm + router_topk,
- * ternary_expert_swiglu and ternary_expert_gemv (down) + moe_reduce_add.
- * The result is bit-identical to calling the entry points above one by one.
- *
- * layers: DEVICE array of n_layers descriptors (below); every pointer in it
- * is a device pointer with the layouts of the entry points above: QKV rows
- * concatenated q|k|v ([(Hq+2Hkv)*D, hidden/16] codes), experts' up|gate rows
- * concatenated ([E, 2*inter, hidden/16]), caches [cache_batch, Hkv, max_len,
- * D] bf16 with strides cache_sb / cache_sh elements (identical for K and V).
- * x: [hidden] bf16, the embedded token in, the last layer's output out.
- * seqlen: [1] int64 position written this step; row_map: [1] cache row or
- * NULL (row 0).  cos/sin: [cs_table_len, rotary_dim] tables read at
- * clamp(seqlen).  Activations bf16; alpha, norm and gate weights f32/bf16.
- * head_dim 64 or 128, Hq/Hkv <= 8, topk <= 8, n_experts <= 256.
- * workspace: maple_decode_layers_workspace_bytes() bytes, 256-byte aligned,
- * zero-filled once before first use and not shared with other entry points
- * (its first words are a grid barrier that persists across calls).
- * The launch is cooperative: one 512-thread CTA per SM; every wait in it
- * is bounded and a wait that gives up sets bit 1 of *err. */
-typedef struct maple_decode_layer {
-  const uint32_t* qkv_codes;
-  const void* qkv_alpha;
-  const uint32_t* o_codes;
-  const void* o_alpha;
-  const void* in_norm;    /* input_layernorm.weight [hidden] */
-  const void* post_norm;  /* post_attention_layernorm.weight [hidden] */
-  const void* q_norm;     /* [head_dim] */
-  const void* k_norm;     /* [head_dim] */
-  const void* gate;       /* router [n_experts, hidden] */
-  const uint32_t* ug_codes;
-  const void* ug_alpha;   /* [E, 2*inter] */
-  const uint32_t* dn_codes;
-  const void* dn_alpha;   /* [E, hidden] */
-  void* k_cache;
-  void* v_cache;
-  int64_t window;         /* sliding window, 0 = full attention */
-  int64_t use_rope;       /* 0: NoPE layer */
-} maple_decode_layer;
-
-int64_t maple_decode_layers_workspace_bytes(int64_t hidden, int64_t num_heads, int64_t num_kv_heads,
-                                            int64_t head_dim, int64_t n_experts, int64_t topk, int64_t inter,
-                                            int64_t max_len, int64_t split_len);
-int maple_decode_layers(const maple_decode_layer* layers, int64_t n_layers, void* x, const int64_t* seqlen,
-                        const int32_t* row_map, const void* cos, const void* sin, int cs_dtype,
-                        int64_t cs_row_stride, int64_t cs_table_len, int64_t hidden, int64_t num_heads,
-                        int64_t num_kv_heads, int64_t head_dim, int64_t rotary_dim, int64_t n_experts,
-                        int64_t topk, int64_t inter, int64_t cache_batch, int64_t max_len, int64_t cache_sb,
-                        int64_t cache_sh, int64_t split_len, int alpha_dtype, int norm_dtype, int gate_dtype,
-                        float eps, float scale, void* workspace, int64_t workspace_bytes, int* err,
-                        void* stream);
-
 #ifdef __cplusplus
 }
 #endif

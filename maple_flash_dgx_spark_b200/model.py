@@ -516,12 +516,8 @@ class MapleForCausalLM:
             row_map = torch.full((seq_len,), row, device=self.device, dtype=torch.int32)
         self.rotary.ensure_length(cache.max_len)
         hidden = self.embed(input_ids.reshape(rows))
-        if seq_len == 1 and bsz == 1 and self._fused_decode(cache):
-            # every layer in one persistent launch, bit-identical to the loop below
-            self._fused_plan(cache).run(self, cache, hidden, seqlen, row_map)
-        else:
-            for layer in self.layers:
-                hidden = layer(hidden, seqlen, row_map, self.rotary, cache, kv_final=seq_len == 1)
+        for layer in self.layers:
+            hidden = layer(hidden, seqlen, row_map, self.rotary, cache, kv_final=seq_len == 1)
         cache.advance(seq_len, bsz)
         keep = hidden if seq_len == 1 else hidden[-logits_to_keep:] if logits_to_keep else hidden
         normed = self.norm(keep)
@@ -530,19 +526,6 @@ class MapleForCausalLM:
         return self.lm_head(normed).reshape(bsz, -1, self.vocab_size)
 
     __call__ = forward
-
-    def _fused_decode(self, cache: KVCache) -> bool:
-        from maple_flash_dgx_spark_b200.fused_decode import fused_decode_enabled, fused_decode_supported
-
-        return fused_decode_enabled() and fused_decode_supported(self, cache)
-
-    def _fused_plan(self, cache: KVCache):
-        from maple_flash_dgx_spark_b200.fused_decode import FusedDecodePlan
-
-        plan = getattr(cache, "_fused_plan", None)
-        if plan is None or not plan.matches(self, cache):
-            plan = cache._fused_plan = FusedDecodePlan(self, cache)
-        return plan
 
     @torch.inference_mode()
     def generate(self, input_ids, max_tokens: int = 128):
