@@ -552,7 +552,7 @@ def run_bs64(args):
         q = torch.randn(T, model.num_heads, 1, model.head_dim, device=dev).to(torch.bfloat16)
         pos = torch.full((T,), ctx0, dtype=torch.int64, device=dev)
         fns = [lambda i=i: K.decode_gqa_attn(q, cache.k[i], cache.v[i], pos, scale=att.scale, window=None,
-                                             split_len=cache.split_len, kv_final=True)
+                                             split_len=cache.split_len, kv_final=True, tensor_cores=cache.attn_tc)
                for i in range(len(model.layers))]
         att_us = _time_graph(fns, dev) * 1000.0 / len(fns)
         kv_per_launch = T * model.num_kv_heads * model.head_dim * 2 * 2 * (ctx0 + 1)
@@ -580,7 +580,7 @@ def run_bs64(args):
                    "l2": f"{step_bytes / 1e9:.1f} GB streamed per GPU per step (> 126 MB L2), no flush needed"},
         "hbm_roofline_step": {"bytes_per_gpu_step": step_bytes, "achieved_gbs": step_bytes / sec / 1e9,
                               "peak_gbs": peak, "frac": step_bytes / sec / 1e9 / peak},
-        "roofline": {"kernel": f"gqa decode attention ({T} rows, split-K, workspace merge)", "bound": "hbm",
+        "roofline": {"kernel": _attn_kernel_name(cache, T, ctx), "bound": "hbm",
                      "achieved": kv_per_launch / (att_us * 1e-6) / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": kv_per_launch / (att_us * 1e-6) / 1e9 / peak, "traffic": None,
                      "algorithmic_bytes": kv_per_launch, "launch_us": att_us, "peak_kind": f"{peak_kind} hbm_gbs"},
@@ -730,7 +730,7 @@ def run_long(args):
         q = torch.randn(phys, model.num_heads, 1, model.head_dim, device=dev).to(torch.bfloat16)
         pos = torch.full((phys,), ctx, dtype=torch.int64, device=dev)
         fns = [lambda i=i: K.decode_gqa_attn(q, cache.k[i], cache.v[i], pos, scale=att.scale, window=None,
-                                             split_len=cache.split_len, kv_final=True)
+                                             split_len=cache.split_len, kv_final=True, tensor_cores=cache.attn_tc)
                for i in range(len(model.layers))]
         att_us = _time_graph(fns, dev) * 1000.0 / len(fns)
         kv_per_launch = phys * model.num_kv_heads * model.head_dim * 2 * 2 * (ctx + 1)
@@ -754,7 +754,7 @@ def run_long(args):
                    "parallelism": "single", "l2": f"{step_bytes / 1e9:.1f} GB streamed per step (> 126 MB L2)"},
         "hbm_roofline_step": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / sec / 1e9, "peak_gbs": peak,
                               "frac": step_bytes / sec / 1e9 / peak},
-        "roofline": {"kernel": f"gqa decode attention ({phys} rows x {ctx} positions)", "bound": "hbm",
+        "roofline": {"kernel": _attn_kernel_name(cache, phys, ctx), "bound": "hbm",
                      "achieved": kv_per_launch / (att_us * 1e-6) / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": kv_per_launch / (att_us * 1e-6) / 1e9 / peak, "traffic": None,
                      "algorithmic_bytes": kv_per_launch, "launch_us": att_us, "peak_kind": f"{peak_kind} hbm_gbs"},
@@ -810,6 +810,14 @@ def _step_launches(n_layers: int) -> int:
     down (seven with the QK-norm as its own launch); plus embedding, final
     norm, head and argmax."""
     return _attn_launches() * n_layers + 4 * n_layers + 4
+
+
+def _attn_kernel_name(cache, rows: int, ctx: int) -> str:
+    """The decode-attention kernel the model runs for this cache, as the ncu
+    launch list names it, plus its merge launch."""
+    if cache.attn_tc:
+        return f"gqa_tc_kernel + gqa_merge_kernel (tensor-core decode attention, {rows} rows x {ctx} positions)"
+    return f"gqa_decode_kernel (CUDA-core decode attention, {rows} rows x {ctx} positions, split-K)"
 
 
 def _attn_launches(cache=None) -> int:

@@ -258,6 +258,28 @@ int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, int64_t num
                           int64_t window, int64_t split_len, int kv_final, void* out, int64_t o_sb, int64_t o_sh,
                           void* workspace, int64_t workspace_bytes, int* err, void* stream);
 
+/* GQA decode attention on the tensor pipe, for long contexts and large
+ * batches over bf16 caches: the arithmetic of kernels/decode_attn.py:166-313
+ * (_decode_gqa_kernel: bf16 q.K^T and P.V dots with fp32 accumulation, online
+ * softmax, P rounded to bf16) as mma.sync bf16 MMAs, replacing
+ * kernels/decode_attn.py:470 decode_gqa_attn where the CUDA-core kernel above
+ * is instruction-bound.  Same arguments as maple_decode_gqa_attn without
+ * split_len / kv_final; x_dtype must be bf16, head_dim 64 or 128, H/Hkv <= 8.
+ * Positions are split in ranges of 256 (max_len < 8192) or 512 that depend on
+ * max_len only, merged by a second launch through the workspace
+ * (maple_decode_gqa_attn_tc_workspace_bytes(); none needed when max_len fits
+ * one range).  Sums run in the tensor pipe's order: results agree with
+ * maple_decode_gqa_attn to the attention tolerance, not bit for bit.  A bounded
+ * wait that gives up sets bit 1 of *err. */
+int64_t maple_decode_gqa_attn_tc_workspace_bytes(int64_t batch, int64_t num_heads, int64_t head_dim,
+                                                 int64_t max_len);
+int maple_decode_gqa_attn_tc(const void* q, int x_dtype, int64_t batch, int64_t num_heads, int64_t q_sb,
+                             int64_t q_sh, const void* k_cache, const void* v_cache, int64_t cache_batch,
+                             int64_t num_kv_heads, int64_t cache_sb, int64_t cache_sh, int64_t max_len,
+                             int64_t head_dim, const int64_t* seqlen, const int32_t* row_map, float scale,
+                             int64_t window, void* out, int64_t o_sb, int64_t o_sh, void* workspace,
+                             int64_t workspace_bytes, int* err, void* stream);
+
 /* maple_apply_qkv_decode followed by maple_decode_gqa_attn in one launch, for
  * decode rows (K/V at positions < seqlen[b] final before the call): replaces
  * kernels/decode_attn.py:362-439 apply_qkv_decode + :470-592 decode_gqa_attn

@@ -86,6 +86,9 @@ _SIGS: dict[str, tuple] = {
     "maple_decode_gqa_attn_qk": (i32, [vp, i32, i64, i64, vp, vp, i32, vp, vp, i32, i64, i64, i64, i32, f32, i64,
                                        vp, vp, i64, i64, i64, i64, i64, i64, vp, vp, f32, i64, i64, vp, i64, i64, vp,
                                        i64, vp, vp]),
+    "maple_decode_gqa_attn_tc_workspace_bytes": (i64, [i64, i64, i64, i64]),
+    "maple_decode_gqa_attn_tc": (i32, [vp, i32, i64, i64, i64, i64, vp, vp, i64, i64, i64, i64, i64, i64, vp, vp,
+                                       f32, i64, vp, i64, i64, vp, i64, vp, vp]),
     "maple_rtn4_gemv": (i32, [vp, i32, i64, i64, i64, vp, i64, vp, vp, i32, i64, vp, i64, vp]),
     "maple_rtn4_frag_bytes": (i64, [i64, i64]),
     "maple_row_uniform": (i32, [vp, i64, vp, vp, vp]),

@@ -23,6 +23,7 @@
 #include "bulk.cuh"
 #include "common.cuh"
 #include "launch.cuh"
+#include "tmap.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -756,6 +757,254 @@ __global__ void __launch_bounds__(D) gqa_merge_kernel(AttnParams p) {
   store_f<XT>(static_cast<char*>(p.out) + (b * p.o_sb + hq * p.o_sh) * es, d, __fdiv_rn(num, den));
 }
 
+
+// ---------------------------------------------------------------------------
+// Tensor-core decode attention (bf16 caches, long contexts / large batches).
+//
+// The reference kernel's arithmetic (kernels/decode_attn.py:166-313): q.K^T as
+// a bf16 dot with fp32 accumulation, an online softmax per query head, P
+// rounded to bf16 for the P.V dot, fp32 accumulation -- on the bf16 tensor
+// pipe (mma.sync m16n8k16) instead of CUDA-core fp32 fmas.  The GQA group's
+// query heads are the MMA's M rows (8 used of 16), 8 positions or 8 output
+// dims are its N, so the scores of one n-tile pair become the A operand of
+// the P.V product in registers (no trip through shared memory).
+//
+// CTA = 4 warps = one (row, kv head, split of positions); the split streams
+// through shared memory in chunks of 64 positions (16 per warp) with a
+// 3-stage pipeline of tiled TMA loads (cp.async.bulk.tensor over a 4-D tensor
+// map of the cache, boxes of 64 positions x 64 dims with the 128-byte swizzle,
+// so the ldmatrix reads below are bank-conflict free).  Each warp
+// keeps its own running max / sum / accumulator; the CTA merges its 4 warps
+// and stores the split's (acc, m, l) for gqa_merge_kernel (or the output when
+// the row has a single split).  Waits are bounded: a wait that gives up sets
+// the error word, drains the copies in flight and returns.
+constexpr int kTcChunk = 64;
+constexpr int kTcStages = 3;
+
+__device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(unsigned addr, unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// c += A * B with A rows 8-15 zero (a1 = a3 = 0): only c[0], c[1] carry data.
+__device__ __forceinline__ void mma_bf16_h8(float (&c)[4], unsigned a0, unsigned a2, unsigned b0, unsigned b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ unsigned pack_bf16x2(float lo, float hi) {
+  return static_cast<unsigned>(f32_to_bf16(lo)) | (static_cast<unsigned>(f32_to_bf16(hi)) << 16);
+}
+
+// Byte offset of 16-byte unit U (dims 8U..8U+7) of row r in a K or V tile of
+// 128-byte-swizzled 64 x 64 boxes (one box per 64 dims).
+__device__ __forceinline__ unsigned tc_swz(int r, int U) {
+  return (unsigned)((U >> 3) * 8192 + r * 128 + (((U & 7) ^ (r & 7)) << 4));
+}
+
+template <int D>
+__global__ void __launch_bounds__(128) gqa_tc_kernel(AttnParams p, const __grid_constant__ CUtensorMap tmk,
+                                                     const __grid_constant__ CUtensorMap tmv) {
+  constexpr int HALVES = D / 64;                 // 64-dim boxes per row
+  constexpr int TILE = HALVES * 8192;            // one K or V tile of 64 positions
+  constexpr int STAGE = 2 * TILE;                // K tile, then V tile
+  constexpr int NT = D / 8;                      // output n-tiles (8 dims each)
+  extern __shared__ unsigned char smem_raw[];
+  // the 128-byte swizzle repeats every 1024 bytes: tiles start 1024-aligned
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar[kTcStages];
+  __shared__ float s_m[4][8], s_l[4][8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const float ninf = __int_as_float(0xff800000);
+  pdl_wait();
+  pdl_trigger();
+
+  const int64_t pos = p.seqlen[b];
+  const int kv_len = (int)min(pos + 1, (int64_t)p.T);
+  const int start = p.window > 0 ? max(0, kv_len - p.window) : 0;
+  const int ns = kv_len > start ? (kv_len - start + p.P - 1) / p.P : 0;
+  if (s >= ns) return;
+  const int t0 = start + s * p.P;
+  const int hi = min(t0 + p.P, kv_len);
+  const int nchunks = (hi - t0 + kTcChunk - 1) / kTcChunk;
+  int cb = b;
+  if (p.row_map != nullptr) cb = p.row_map[b];
+  if (cb < 0 || cb >= p.Bc) {
+    if (tid == 0) atomicOr(p.err, kErrFlagBounds);
+    cb = 0;
+  }
+
+  if (tid == 0)
+    for (int i = 0; i < kTcStages; ++i) mbar_init(&bar[i], 1);
+  __syncthreads();
+
+  // thread 0 issues chunk c: the full 64-position boxes of K and V (rows past
+  // the cache's end arrive as zeros and count toward the transaction bytes)
+  auto issue = [&](int c) {
+    const int stage = c % kTcStages;
+    const int c0 = t0 + c * kTcChunk;
+    unsigned char* kt = smem + stage * STAGE;
+    mbar_expect_tx(&bar[stage], (unsigned)STAGE);
+#pragma unroll
+    for (int hf = 0; hf < HALVES; ++hf) {
+      tma_load_4d(kt + hf * 8192, &tmk, 64 * hf, c0, h, cb, &bar[stage]);
+      tma_load_4d(kt + TILE + hf * 8192, &tmv, 64 * hf, c0, h, cb, &bar[stage]);
+    }
+  };
+  if (tid == 0)
+    for (int c = 0; c < min(kTcStages, nchunks); ++c) issue(c);
+
+  // this thread's A fragments of q (rows g = query head of the group; rows
+  // 8-15 of the MMA are zero): dims 16kk + 2t, +1 and 16kk + 8 + 2t, +1
+  unsigned qa[D / 16][2];
+  {
+    const bool real = g < p.G;
+    const unsigned* qrow = reinterpret_cast<const unsigned*>(
+        static_cast<const char*>(p.q) + (b * p.q_sb + (h * p.G + (real ? g : 0)) * p.q_sh) * 2);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      qa[kk][0] = real ? qrow[8 * kk + t] : 0u;
+      qa[kk][1] = real ? qrow[8 * kk + 4 + t] : 0u;
+    }
+  }
+
+  float m_run = ninf, l_run = 0.0f;
+  float acc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+  const int r0 = warp * 16;
+
+  for (int c = 0; c < nchunks; ++c) {
+    const int stage = c % kTcStages;
+    const bool ok = mbar_wait_bounded(&bar[stage], (unsigned)((c / kTcStages) & 1));
+    if (__syncthreads_or(!ok)) {
+      // give up: report, let this CTA's copies land (bounded), return
+      if (tid == 0) {
+        atomicOr(p.err, kErrFlagTimeout);
+        for (int c2 = c; c2 < min(c + kTcStages, nchunks); ++c2)
+          mbar_wait_bounded(&bar[c2 % kTcStages], (unsigned)((c2 / kTcStages) & 1));
+      }
+      __syncthreads();
+      return;
+    }
+    const int c0 = t0 + c * kTcChunk;
+    const int n = min(kTcChunk, hi - c0);
+    unsigned char* kt = smem + stage * STAGE;
+    unsigned char* vt = kt + TILE;
+    if (r0 < n) {
+      if (n < r0 + 16) {
+        // rows past the split's end hold other positions' bytes: zero V there
+        // (P is 0 at masked positions, and 0 * anything non-finite is NaN)
+        for (int r = n; r < r0 + 16; ++r)
+          for (int i = lane; i < D / 8; i += 32)
+            *reinterpret_cast<uint4*>(vt + tc_swz(r, i)) = make_uint4(0, 0, 0, 0);
+        __syncwarp();
+      }
+      // S = q K^T for this warp's 16 positions (two n-tiles of 8)
+      float sfr[2][4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        sfr[j][0] = sfr[j][1] = sfr[j][2] = sfr[j][3] = 0.0f;
+#pragma unroll
+        for (int kp = 0; kp < D / 32; ++kp) {
+          unsigned b0, b1, b2, b3;
+          ldsm_x4(smem_u32(kt + tc_swz(r0 + 8 * j + (lane & 7), 4 * kp + (lane >> 3))), b0, b1, b2, b3);
+          mma_bf16_h8(sfr[j], qa[2 * kp][0], qa[2 * kp][1], b0, b1);
+          mma_bf16_h8(sfr[j], qa[2 * kp + 1][0], qa[2 * kp + 1][1], b2, b3);
+        }
+      }
+      // online softmax of row g over positions r0 + {2t, 2t+1, 8+2t, 9+2t}
+      float sv[4] = {sfr[0][0], sfr[0][1], sfr[1][0], sfr[1][1]};
+      const int pr[4] = {r0 + 2 * t, r0 + 2 * t + 1, r0 + 8 + 2 * t, r0 + 9 + 2 * t};
+      float mx = ninf;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sv[i] = pr[i] < n ? __fmul_rn(sv[i], p.scale) : ninf;
+        mx = fmaxf(mx, sv[i]);
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = m_new == ninf ? 0.0f : m_new;
+      const float alpha = __expf(__fsub_rn(m_run, m_use));
+      float pv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pv[i] = __expf(__fsub_rn(sv[i], m_use));
+      l_run = __fadd_rn(__fmul_rn(l_run, alpha), __fadd_rn(__fadd_rn(pv[0], pv[1]), __fadd_rn(pv[2], pv[3])));
+      m_run = m_new;
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        acc[j][0] = __fmul_rn(acc[j][0], alpha);
+        acc[j][1] = __fmul_rn(acc[j][1], alpha);
+      }
+      const unsigned pa0 = pack_bf16x2(pv[0], pv[1]), pa2 = pack_bf16x2(pv[2], pv[3]);
+      // O += P V: V fragments by transposed ldmatrix, two dim n-tiles per load
+#pragma unroll
+      for (int jp = 0; jp < D / 16; ++jp) {
+        unsigned b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(vt + tc_swz(r0 + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * jp + (lane >> 4))), b0, b1, b2,
+                  b3);
+        mma_bf16_h8(acc[2 * jp], pa0, pa2, b0, b1);
+        mma_bf16_h8(acc[2 * jp + 1], pa0, pa2, b2, b3);
+      }
+    }
+    __syncthreads();  // every warp is done with this stage
+    if (tid == 0 && c + kTcStages < nchunks) {
+      fence_proxy_async_smem();
+      issue(c + kTcStages);
+    }
+  }
+
+  // merge the four warps' states: row sums over the 4 threads of a row,
+  // accumulators through the (now idle) stage memory
+  l_run = __fadd_rn(l_run, __shfl_xor_sync(0xffffffffu, l_run, 1));
+  l_run = __fadd_rn(l_run, __shfl_xor_sync(0xffffffffu, l_run, 2));
+  float* wacc = reinterpret_cast<float*>(smem);  // [4 warps][8 heads][D]
+  if (t == 0) {
+    s_m[warp][g] = m_run;
+    s_l[warp][g] = l_run;
+  }
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    wacc[(warp * 8 + g) * D + 8 * j + 2 * t] = acc[j][0];
+    wacc[(warp * 8 + g) * D + 8 * j + 2 * t + 1] = acc[j][1];
+  }
+  __syncthreads();
+  for (int i = tid; i < p.G * D; i += blockDim.x) {
+    const int gg = i / D, d = i - gg * D;
+    float M = s_m[0][gg];
+#pragma unroll
+    for (int w = 1; w < 4; ++w) M = fmaxf(M, s_m[w][gg]);
+    float num = 0.0f, den = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float wt = s_m[w][gg] == ninf ? 0.0f : __expf(__fsub_rn(s_m[w][gg], M));
+      num = __fmaf_rn(wt, wacc[(w * 8 + gg) * D + d], num);
+      den = __fmaf_rn(wt, s_l[w][gg], den);
+    }
+    const int hq = h * p.G + gg;
+    if (ns == 1) {
+      store_f<kBF16>(static_cast<char*>(p.out) + (b * p.o_sb + hq * p.o_sh) * 2, d, __fdiv_rn(num, den));
+    } else {
+      p.ws_acc[(((int64_t)b * p.Hq + hq) * p.NS + s) * D + d] = num;
+      if (d == 0) {
+        float* ml = p.ws_ml + (((int64_t)b * p.Hq + hq) * p.NS + s) * 2;
+        ml[0] = M;
+        ml[1] = den;
+      }
+    }
+  }
+}
+
 }  // namespace mb
 
 using namespace mb;
@@ -936,4 +1185,71 @@ extern "C" int maple_decode_gqa_attn_qk(const void* qkv, int x_dtype, int64_t ba
   return gqa_common(nullptr, x_dtype, batch, num_heads, 0, 0, k_cache, v_cache, cache_batch, num_kv_heads, cache_sb,
                     cache_sh, max_len, head_dim, seqlen, row_map, scale, window, split_len, 1, out, o_sb, o_sh,
                     workspace, workspace_bytes, err, stream, &qk);
+}
+
+// Positions per CTA of the tensor-core attention.  A function of the cache
+// length only, so a row's split boundaries (and so its rounding) do not depend
+// on the batch: batched decode equals per-sequence decode, and expert-parallel
+// ranks (the same cache length, fewer rows) equal one GPU, bit for bit.
+static int64_t gqa_tc_split(int64_t max_len) { return max_len >= 8192 ? 512 : 256; }
+
+extern "C" int64_t maple_decode_gqa_attn_tc_workspace_bytes(int64_t batch, int64_t num_heads, int64_t head_dim,
+                                                            int64_t max_len) {
+  if (batch <= 0 || max_len <= 0) return -1;
+  return maple_decode_gqa_workspace_bytes(batch, num_heads, head_dim, max_len, gqa_tc_split(max_len));
+}
+
+extern "C" int maple_decode_gqa_attn_tc(const void* q, int x_dtype, int64_t batch, int64_t num_heads, int64_t q_sb,
+                                        int64_t q_sh, const void* k_cache, const void* v_cache, int64_t cache_batch,
+                                        int64_t num_kv_heads, int64_t cache_sb, int64_t cache_sh, int64_t max_len,
+                                        int64_t head_dim, const int64_t* seqlen, const int32_t* row_map,
+                                        float scale, int64_t window, void* out, int64_t o_sb, int64_t o_sh,
+                                        void* workspace, int64_t workspace_bytes, int* err, void* stream) {
+  if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_len <= 0) return kErrShape;
+  if (batch == 0) return kOk;
+  if (x_dtype != kBF16) return kErrDtype;
+  if (num_heads % num_kv_heads != 0 || num_heads / num_kv_heads > 8) return kErrShape;
+  if (head_dim != 64 && head_dim != 128) return kErrShape;
+  if (!q || !k_cache || !v_cache || !seqlen || !out || !err || batch > 65535) return kErrShape;
+  if ((reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15) ||
+      ((cache_sb * 2) & 15) || ((cache_sh * 2) & 15) || (reinterpret_cast<uintptr_t>(q) & 3) || (q_sb & 1) ||
+      (q_sh & 1))
+    return kErrAlign;
+  const int64_t sp = gqa_tc_split(max_len);
+  const int64_t ns = (max_len + sp - 1) / sp;
+  if (ns > 65535) return kErrShape;
+  if (ns > 1 && (!workspace || workspace_bytes < maple_decode_gqa_workspace_bytes(batch, num_heads, head_dim,
+                                                                                  max_len, sp)))
+    return kErrWorkspace;
+  AttnParams p{};
+  p.q = q; p.kc = k_cache; p.vc = v_cache; p.seqlen = seqlen; p.row_map = row_map; p.out = out; p.err = err;
+  p.ws_acc = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kAttnTicketBytes) : nullptr;
+  p.ws_ml = p.ws_acc ? p.ws_acc + batch * num_heads * ns * head_dim : nullptr;
+  p.q_sb = q_sb; p.q_sh = q_sh; p.kc_sb = cache_sb; p.kc_sh = cache_sh; p.vc_sb = cache_sb; p.vc_sh = cache_sh;
+  p.o_sb = o_sb; p.o_sh = o_sh;
+  p.Hq = (int)num_heads; p.Hkv = (int)num_kv_heads; p.G = (int)(num_heads / num_kv_heads);
+  p.Bc = (int)cache_batch; p.T = (int)max_len; p.P = (int)sp; p.NS = (int)ns;
+  p.window = (int)window; p.scale = scale;
+  // 4-D maps of the caches: (dim, position, kv head, cache row), boxes of 64 x 64
+  CUtensorMap tmk, tmv;
+  if (!tmap_bf16_4d(k_cache, head_dim, max_len, num_kv_heads, cache_batch, head_dim, cache_sh, cache_sb, 64,
+                    kTcChunk, &tmk) ||
+      !tmap_bf16_4d(v_cache, head_dim, max_len, num_kv_heads, cache_batch, head_dim, cache_sh, cache_sb, 64,
+                    kTcChunk, &tmv))
+    return kErrCuda;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid((unsigned)ns, (unsigned)num_kv_heads, (unsigned)batch);
+  cudaError_t e = cudaSuccess;
+#define MB_TC(DD)                                                                                              \
+  do {                                                                                                         \
+    const size_t smem = (size_t)kTcStages * 2 * (DD / 64) * 8192 + 1024;                                       \
+    e = cudaFuncSetAttribute(gqa_tc_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
+    if (e == cudaSuccess) e = launch_k(gqa_tc_kernel<DD>, grid, dim3(128), smem, st, p, tmk, tmv);             \
+    if (e == cudaSuccess && ns > 1)                                                                            \
+      e = launch_k(gqa_merge_kernel<kBF16, DD>, dim3((unsigned)num_heads, (unsigned)batch), dim3(DD), 0, st, p); \
+  } while (0)
+  if (head_dim == 64) MB_TC(64); else MB_TC(128);
+#undef MB_TC
+  if (e != cudaSuccess) return kErrCuda;
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }

@@ -531,13 +531,21 @@ def attn_split_len(max_len: int, batch: int = 1, num_kv_heads: int = 4) -> int:
 
 
 def decode_gqa_attn(q, k_cache, v_cache, seqlen, *, row_map=None, scale: float, window: int | None,
-                    workspace=None, split_len: int | None = None, kv_final: bool = False):
+                    workspace=None, split_len: int | None = None, kv_final: bool = False,
+                    tensor_cores: bool = False):
     """GQA attention for ``q_len=1``.  Reference kernels/decode_attn.py:470-592.
     ``q`` is ``[B, H, 1, D]``, caches ``[B, n_kv, T, D]``; ``seqlen[b]`` is the
     index just written.  ``workspace`` may be a byte tensor from
     :func:`attn_workspace` (a reference-style tuple is accepted and ignored).
     ``kv_final`` promises K/V before ``seqlen[b]`` was written before the
-    previous launch (decode rows), so those rows can load early."""
+    previous launch (decode rows), so those rows can load early.
+
+    ``tensor_cores`` (bf16 caches, head_dim 64/128): the reference kernel's
+    own arithmetic -- bf16 q.K^T and P.V dots with fp32 accumulation, P
+    rounded to bf16 -- on the tensor pipe (``maple_decode_gqa_attn_tc``), for
+    long contexts and large batches where the CUDA-core path is
+    instruction-bound.  Its sums are in the tensor pipe's order, so it agrees
+    with the canonical fp32 path to the attention tolerance, not bit for bit."""
     op = "decode_gqa_attn"
     if q.ndim != 4 or q.shape[2] != 1:
         raise ValueError(f"decode_gqa_attn expects q [B, H, 1, D], got {tuple(q.shape)}.")
@@ -552,10 +560,23 @@ def decode_gqa_attn(q, k_cache, v_cache, seqlen, *, row_map=None, scale: float, 
         raise ValueError(f"n_q={n_q} not divisible by n_kv={n_kv}.")
     if k_cache.stride(3) != 1 or k_cache.stride(2) != head_dim or k_cache.stride() != v_cache.stride():
         raise ValueError("KV caches must be [B, n_kv, T, D] with contiguous (T, D).")
-    P = split_len or attn_split_len(max_len, bsz, n_kv)
     out = torch.empty_like(q)
     q3, o3 = q[:, :, 0, :], out[:, :, 0, :]
     L = lib()
+    if tensor_cores:
+        if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
+            raise TypeError("tensor-core decode attention needs bf16 q and caches.")
+        nbytes = L.maple_decode_gqa_attn_tc_workspace_bytes(bsz, n_q, head_dim, max_len)
+        ws = workspace if isinstance(workspace, torch.Tensor) and workspace.numel() >= nbytes else _ws(q.device, nbytes)
+        sl = seqlen.reshape(-1).to(torch.int64)
+        rm = row_map.reshape(-1).to(torch.int32) if row_map is not None else None
+        check(L.maple_decode_gqa_attn_tc(
+            ptr(q3), dtype_code(q, op), bsz, n_q, q3.stride(0), q3.stride(1), ptr(k_cache), ptr(v_cache),
+            k_cache.shape[0], n_kv, k_cache.stride(0), k_cache.stride(1), max_len, head_dim, ptr(sl), ptr(rm),
+            float(scale), int(window or 0), ptr(o3), o3.stride(0), o3.stride(1), ptr(ws),
+            ws.numel() if ws is not None else 0, ptr(_err(q.device)), stream_ptr(q.device)), op)
+        return out
+    P = split_len or attn_split_len(max_len, bsz, n_kv)
     nbytes = L.maple_decode_gqa_workspace_bytes(bsz, n_q, head_dim, max_len, P) if -(-max_len // P) > 16 else 0
     ws = workspace if isinstance(workspace, torch.Tensor) and workspace.numel() >= nbytes else _ws(q.device, nbytes)
     sl = seqlen.reshape(-1).to(torch.int64)

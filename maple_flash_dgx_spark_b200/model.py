@@ -56,6 +56,14 @@ def _fused_qk_attention() -> bool:
     import os
 
     return os.environ.get("MAPLE_FUSED_QK_ATTN", "1") != "0"
+
+
+def _tc_attention() -> bool:
+    """``MAPLE_TC_ATTN=0`` keeps long-context decode attention on the
+    canonical CUDA-core kernel (bit-exact with the CPU oracle)."""
+    import os
+
+    return os.environ.get("MAPLE_TC_ATTN", "1") != "0"
 HEAD_GROUP_SIZE = 64
 
 
@@ -121,6 +129,11 @@ class KVCache:
         self.row_map = torch.arange(batch, dtype=torch.int32, device=device)
         self.remap = False
         self.split_len = attn_split_len(max_len, batch, n_kv)
+        # Decode attention on the tensor pipe (the reference's bf16 dots) where
+        # the canonical CUDA-core kernel is instruction-bound: caches with more
+        # positions than one thread-block cluster of splits covers.
+        self.attn_tc = (dtype == torch.bfloat16 and head_dim in (64, 128) and
+                        -(-max_len // self.split_len) > _QK_FUSED_MAX_SPLITS and _tc_attention())
 
     @contextmanager
     def prefill_slot(self, row: int):
@@ -247,7 +260,8 @@ class MapleAttention:
                              rotary_dim=rotary.rotary_dim, use_rope=self.use_rope, use_qk_norm=True,
                              eps=self.q_norm.eps, rope_table=True)
         attn = decode_gqa_attn(q, k_cache, v_cache, seqlen, row_map=row_map, scale=self.scale,
-                               window=self.sliding_window, split_len=cache.split_len, kv_final=kv_final)
+                               window=self.sliding_window, split_len=cache.split_len, kv_final=kv_final,
+                               tensor_cores=getattr(cache, "attn_tc", False))
         return self.o_proj(attn.reshape(rows, -1))
 
 

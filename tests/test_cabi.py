@@ -36,3 +36,21 @@ def test_pure_shape_queries():
     assert L.maple_router_topk_workspace_bytes(1, 64) > 0
     assert L.maple_decode_gqa_workspace_bytes(1, 32, 128, 4096, 64) > 0
     assert L.maple_ternary_gemv_workspace_bytes(1, 5120, 2048) >= 0
+
+
+def test_tc_attention_host_checks():
+    """The tensor-core attention entry refuses what it cannot run before any launch."""
+    from maple_flash_dgx_spark_b200 import _lib
+
+    L = _lib.lib()
+    assert L.maple_decode_gqa_attn_tc_workspace_bytes(64, 32, 128, 8192) > 0
+    d = ctypes.c_void_p(256)
+
+    def call(x_dtype=1, heads=32, kv=4, hd=128):
+        return L.maple_decode_gqa_attn_tc(d, x_dtype, 2, heads, heads * hd, hd, d, d, 2, kv, kv * 4096 * hd,
+                                          4096 * hd, 4096, hd, d, None, 0.088, 0, d, heads * hd, hd, d, 1 << 30, d,
+                                          None)
+
+    assert call(x_dtype=0) == 2        # fp32 caches: the canonical kernel's job
+    assert call(hd=256) == 1           # head_dim 64 or 128
+    assert call(heads=48, kv=4) == 1   # more than 8 query heads per KV head
