@@ -64,7 +64,8 @@ int maple_ternary_gemv(const void* x, int x_dtype, int64_t batch, int64_t k, int
  * maple_ternary_gemv, without the workspace: split-K scratch comes from a
  * fixed 2 MiB __device__ array inside the library (held on every GPU that
  * loads it), so it needs batch * splits * n * 16 bytes <= 2 MiB - 16 KiB
- * (splits = 2 for k = 4096; k <= 2048 uses none) or it returns
+ * (splits = ceil(k / 2048): 2 for k = 4096 up to 4 for k = 8192; k <= 2048 uses
+ * none) or it returns
  * MAPLE_ERR_SCRATCH_LIMIT.  The first call on each device looks up the
  * array's address; make it before any stream capture.  Calls share the
  * array: calls that can overlap on the GPU race and must be serialised. */
@@ -265,8 +266,8 @@ int maple_decode_gqa_attn(const void* q, int x_dtype, int64_t batch, int64_t num
  * kernels/decode_attn.py:470 decode_gqa_attn where the CUDA-core kernel above
  * is instruction-bound.  Same arguments as maple_decode_gqa_attn without
  * split_len / kv_final; x_dtype must be bf16, head_dim 64 or 128, H/Hkv <= 8.
- * Positions are split in ranges of 256 (max_len < 8192) or 512 that depend on
- * max_len only, merged by a second launch through the workspace
+ * Positions are split in ranges of 512 (8192 <= max_len < 32768) or 256 that
+ * depend on max_len only, merged by a second launch through the workspace
  * (maple_decode_gqa_attn_tc_workspace_bytes(); none needed when max_len fits
  * one range).  Sums run in the tensor pipe's order: results agree with
  * maple_decode_gqa_attn to the attention tolerance, not bit for bit.  A bounded

@@ -1005,6 +1005,71 @@ __global__ void __launch_bounds__(128) gqa_tc_kernel(AttnParams p, const __grid_
   }
 }
 
+// Split merge of the tensor-core path: one CTA per (row, query head), its 8
+// warps take splits j = warp, warp + 8, ... with a running max / rescaled sum
+// over D/32 dims per lane (16-byte loads), then the warps combine through
+// shared memory.  Many splits are read at once instead of one after another
+// (a batch-1 row of a 64K cache has 257 splits).
+template <int D>
+__global__ void __launch_bounds__(256) gqa_tc_merge_kernel(AttnParams p) {
+  constexpr int V = D / 32;  // dims per lane
+  __shared__ float s_m[8], s_l[8];
+  __shared__ float s_acc[8][D];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hq = blockIdx.x, b = blockIdx.y;
+  const float ninf = __int_as_float(0xff800000);
+  pdl_wait();
+  pdl_trigger();
+  const int64_t pos = p.seqlen[b];
+  const int kv_len = (int)min(pos + 1, (int64_t)p.T);
+  const int start = p.window > 0 ? max(0, kv_len - p.window) : 0;
+  const int ns = kv_len > start ? (kv_len - start + p.P - 1) / p.P : 0;
+  if (ns <= 1) return;  // a single split was stored directly
+  const float* ml = p.ws_ml + ((int64_t)b * p.Hq + hq) * p.NS * 2;
+  const float* ac = p.ws_acc + ((int64_t)b * p.Hq + hq) * p.NS * D;
+  float m = ninf, l = 0.0f, acc[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) acc[v] = 0.0f;
+  for (int j = warp; j < ns; j += 8) {
+    const float mj = __ldcg(ml + 2 * j), lj = __ldcg(ml + 2 * j + 1);
+    float aj[V];
+    if constexpr (V == 4) {
+      const float4 a4 = __ldcg(reinterpret_cast<const float4*>(ac + (int64_t)j * D) + lane);
+      aj[0] = a4.x; aj[1] = a4.y; aj[2] = a4.z; aj[3] = a4.w;
+    } else {
+      const float2 a2 = __ldcg(reinterpret_cast<const float2*>(ac + (int64_t)j * D) + lane);
+      aj[0] = a2.x; aj[1] = a2.y;
+    }
+    const float mn = fmaxf(m, mj);
+    const float c_old = m == ninf ? 0.0f : __expf(__fsub_rn(m, mn));
+    const float c_new = __expf(__fsub_rn(mj, mn));
+    l = __fmaf_rn(lj, c_new, __fmul_rn(l, c_old));
+#pragma unroll
+    for (int v = 0; v < V; ++v) acc[v] = __fmaf_rn(aj[v], c_new, __fmul_rn(acc[v], c_old));
+    m = mn;
+  }
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_l[warp] = l;
+  }
+#pragma unroll
+  for (int v = 0; v < V; ++v) s_acc[warp][V * lane + v] = acc[v];
+  __syncthreads();
+  if (tid < D) {
+    float M = s_m[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) M = fmaxf(M, s_m[w]);
+    float num = 0.0f, den = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float c = s_m[w] == ninf ? 0.0f : __expf(__fsub_rn(s_m[w], M));
+      num = __fmaf_rn(c, s_acc[w][tid], num);
+      den = __fmaf_rn(c, s_l[w], den);
+    }
+    store_f<kBF16>(static_cast<char*>(p.out) + (b * p.o_sb + hq * p.o_sh) * 2, tid, __fdiv_rn(num, den));
+  }
+}
+
 }  // namespace mb
 
 using namespace mb;
@@ -1191,7 +1256,10 @@ extern "C" int maple_decode_gqa_attn_qk(const void* qkv, int x_dtype, int64_t ba
 // length only, so a row's split boundaries (and so its rounding) do not depend
 // on the batch: batched decode equals per-sequence decode, and expert-parallel
 // ranks (the same cache length, fewer rows) equal one GPU, bit for bit.
-static int64_t gqa_tc_split(int64_t max_len) { return max_len >= 8192 ? 512 : 256; }
+// 512 positions where rows x kv heads fill the GPU (batched decode at 8-16K),
+// 256 for short caches and for very long ones, whose few rows still need
+// about four waves of CTAs.
+static int64_t gqa_tc_split(int64_t max_len) { return (max_len >= 8192 && max_len < 32768) ? 512 : 256; }
 
 extern "C" int64_t maple_decode_gqa_attn_tc_workspace_bytes(int64_t batch, int64_t num_heads, int64_t head_dim,
                                                             int64_t max_len) {
@@ -1246,7 +1314,7 @@ extern "C" int maple_decode_gqa_attn_tc(const void* q, int x_dtype, int64_t batc
     e = cudaFuncSetAttribute(gqa_tc_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
     if (e == cudaSuccess) e = launch_k(gqa_tc_kernel<DD>, grid, dim3(128), smem, st, p, tmk, tmv);             \
     if (e == cudaSuccess && ns > 1)                                                                            \
-      e = launch_k(gqa_merge_kernel<kBF16, DD>, dim3((unsigned)num_heads, (unsigned)batch), dim3(DD), 0, st, p); \
+      e = launch_k(gqa_tc_merge_kernel<DD>, dim3((unsigned)num_heads, (unsigned)batch), dim3(256), 0, st, p);   \
   } while (0)
   if (head_dim == 64) MB_TC(64); else MB_TC(128);
 #undef MB_TC
