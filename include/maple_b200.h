@@ -138,6 +138,25 @@ int maple_p2p_combine(void* const* peer_bases, int world, int rank, int64_t off_
                       int64_t n_experts, const int32_t* ids_mine, const float* w_mine, const void* residual, void* out,
                       unsigned* seq, unsigned* ticket, int* err, void* stream);
 
+/* Grouped expert GEMM on the tcgen05 tensor cores (accumulators in tensor
+ * memory), for experts with many routed slots (prompt prefill, large batches):
+ * the batched branch of kernels/ternary_gemv.py:156-258 and the expert kernels
+ * kernels/ternary_expert.py:58-122 / :240-319 run per expert group.  Takes the
+ * raw activation rows x [in_rows, k] (row stride x_row_stride, bf16 or f32):
+ * each listed slot's row (slot / in_div) is FXA-encoded into the workspace in
+ * plan order, then contracted exactly with the codes [n_experts, code_rows,
+ * k/16].  Same plan (offsets, list), swiglu and output conventions as
+ * maple_ternary_grouped_gemm and bit-identical results.  k % 128 == 0,
+ * k <= 8192; workspace (256-byte aligned) of
+ * maple_ternary_grouped_gemm_tc_workspace_bytes(n_slots, k) bytes.  A bounded
+ * wait that gives up sets bit 1 of *err. */
+int64_t maple_ternary_grouped_gemm_tc_workspace_bytes(int64_t n_slots, int64_t k);
+int maple_ternary_grouped_gemm_tc(const void* x, int x_dtype, int64_t in_rows, int64_t k, int64_t x_row_stride,
+                                  const uint32_t* codes, int64_t n_experts, int64_t code_rows, const void* alpha,
+                                  int alpha_dtype, const int32_t* offsets, const uint32_t* list, int64_t n_slots,
+                                  int64_t in_div, int swiglu, void* y, int y_dtype, int64_t y_row_stride,
+                                  void* workspace, int64_t workspace_bytes, int* err, void* stream);
+
 /* Grouped expert GEMM over a plan: slot s reads encoded row s / in_div
  * (in_div = top_k when rows are tokens, 1 when they are slots) and writes
  * row s of y.  codes [n_experts, code_rows, k/16]; swiglu != 0 runs the

@@ -61,6 +61,9 @@ _SIGS: dict[str, tuple] = {
                                 vp, vp]),
     "maple_ternary_grouped_gemm": (i32, [vp, vp, i64, i64, vp, i64, i64, vp, i32, vp, vp, i64, i64, i32, i32, vp,
                                          i32, i64, vp, vp]),
+    "maple_ternary_grouped_gemm_tc_workspace_bytes": (i64, [i64, i64]),
+    "maple_ternary_grouped_gemm_tc": (i32, [vp, i32, i64, i64, i64, vp, i64, i64, vp, i32, vp, vp, i64, i64, i32,
+                                            vp, i32, i64, vp, i64, vp, vp]),
     "maple_ternary_expert_gemv_workspace_bytes": (i64, [i64, i64, i64]),
     "maple_ternary_expert_gemv": (i32, [vp, i32, i64, i64, vp, i64, i64, vp, i64, i64, vp, i32, vp, i64, vp,
                                         i64, vp]),

@@ -349,8 +349,10 @@ __global__ void __launch_bounds__(32 * WM * WK, NBUF == 1 ? 2 : 1) tgemm_kernel(
           up = fminf(fmaxf(up, -7.0f), 7.0f);
           gate = fminf(gate, 7.0f);
           const int64_t orow = grouped ? (int64_t)(slot & ~kBadSlot) : (int64_t)slot;
+          // an out-of-range expert id gives a NaN row (the clamps would turn NaN into -49)
+          const bool bad = grouped && (slot & kBadSlot);
           store_f<OT>(y + orow * p.y_stride * (OT == kBF16 ? 2 : 4), n,
-                      __fmul_rn(__fmul_rn(up, gate), msigmoid(gate)));
+                      bad ? __int_as_float(0x7fc00000) : __fmul_rn(__fmul_rn(up, gate), msigmoid(gate)));
         }
       }
     }

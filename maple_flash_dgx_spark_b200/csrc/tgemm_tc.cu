@@ -1,0 +1,428 @@
+// Grouped packed-ternary expert GEMM on the 5th-generation tensor cores
+// (tcgen05, accumulators in tensor memory) for experts with many routed
+// tokens: prompt prefill and large batches.
+//
+// Reference: kernels/ternary_expert.py:240-319 (_ternary_expert_swiglu_kernel)
+// and :58-122 (_ternary_expert_gemv_kernel), which the reference runs per
+// (token, slot); kernels/ternary_gemv.py:156-258 is its tl.dot GEMM.
+//
+// Arithmetic: the exact integer contraction of the batch-1 and mma.sync paths
+// (the FXA digits of each activation row contracted with the codes, recombined
+// exactly, rounded once), so every output equals theirs bit for bit.
+//
+//   1. fxa_plain_kernel writes, for every routed slot in expert-sorted order
+//      (the MoE plan), the slot's activation row as four plain s8 digit rows
+//      of K bytes (digit j of X_k = rint(x_k 2^s)) plus the row metadata
+//      (shift, rstd, digit totals) -- the same values fxa_prologue produces.
+//   2. tgemm_tc_kernel, one CTA per (128 weight rows, expert): for each
+//      128-byte K block the threads expand the 2-bit codes of the tile to u8
+//      bytes in shared memory (128-byte swizzled, K-major), a tiled TMA load
+//      brings the 256 digit rows of the next 64 slots, and one thread issues
+//      four tcgen05.mma.kind::i8 (M = 128 codes rows, N = 256 = 64 slots x 4
+//      digits, K = 32 bytes each) accumulating u8 x s8 -> s32 in tensor
+//      memory; tcgen05.commit releases the stage (3 stages).  The epilogue
+//      reads the accumulators with tcgen05.ld (one TMEM lane = one weight
+//      row per thread, the four digit sums of a slot in four columns),
+//      recombines S = sum_j (C_j - tot_j) 128^j exactly, and applies alpha
+//      (and the SwiGLU of the up/gate row pairs) as the mma.sync path does.
+//
+// Every wait is bounded: a wait that gives up sets bit 1 of the error word,
+// waits (bounded) for the CTA's copies and MMAs in flight, frees its tensor
+// memory and returns.  TMA loads are plain (no cluster multicast).
+#include "bulk.cuh"
+#include "fxa.cuh"
+#include "launch.cuh"
+#include "tmap.cuh"
+
+namespace mb {
+
+constexpr unsigned kTcBadSlot = 0x80000000u;  // plan list flag: out-of-range expert id
+constexpr int kTcMeta = 8;                    // s, rstd bits, tot[0..3], 0, 0
+constexpr int kTcStages = 3;
+constexpr int kTcARows = 128;                 // MMA M: weight rows per CTA
+constexpr int kTcBRows = 256;                 // MMA N: 64 slots x 4 digits
+constexpr int kTcSlots = kTcBRows / 4;
+constexpr int kTcABytes = kTcARows * 128;     // one 128-byte K block of A
+constexpr int kTcBBytes = kTcBRows * 128;
+constexpr int kTcStage = kTcABytes + kTcBBytes;
+
+// ---------------------------------------------------------------- encode --
+// Position p (expert-sorted) encodes input row (list[p] & ~bad) / in_div;
+// positions past offsets[n_experts] (slots of other ranks' experts under
+// expert parallelism, not listed) are skipped.
+template <int XT>
+__global__ void __launch_bounds__(256) fxa_plain_kernel(const void* x, int64_t x_stride, int K,
+                                                        const int* offsets, int n_experts, const unsigned* list,
+                                                        int in_div, int8_t* digits, int* meta) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ FxaBlock fb;
+  const int iters = (K + 255) / 256;
+  uint2* frag = reinterpret_cast<uint2*>(smem);
+  float* xsm = reinterpret_cast<float*>(smem + (size_t)iters * 256 * sizeof(uint2));
+  const int p = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  if (p >= offsets[n_experts]) return;
+  const int64_t row = (int64_t)(list[p] & ~kTcBadSlot) / in_div;
+  const void* xr = static_cast<const char*>(x) + row * x_stride * (XT == kBF16 ? 2 : 4);
+  // shift and digit totals exactly as the fragment encoders compute them
+  fxa_prologue<XT, kF32, false, 2, 256>(xr, nullptr, K, 0.0f, 0, iters, xsm, nullptr, frag, fb);
+  const int s = fb.s;
+  const bool bad = (s == kFxaNonFinite);
+  int8_t* d0 = digits + (int64_t)p * 4 * K;
+  for (int k = 4 * threadIdx.x; k < K; k += 4 * 256) {
+    uint32_t u[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) u[i] = static_cast<uint32_t>((bad ? 0 : fxa_enc(xsm[k + i], s)) + kFxaOffset);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint32_t*>(d0 + (int64_t)j * K + k) = signed_digits(raw_digits(u[0], u[1], u[2], u[3], j));
+  }
+  if (threadIdx.x < kTcMeta) {
+    const int j = threadIdx.x;
+    int v = 0;
+    if (j == 0) v = s;
+    else if (j == 1) v = __float_as_int(fb.rstd);
+    else if (j < 6) v = fb.tot[j - 2];
+    meta[(int64_t)p * kTcMeta + j] = v;
+  }
+}
+
+// ------------------------------------------------------------ tcgen05 ----
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(unsigned* dst_smem, unsigned ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(unsigned taddr, unsigned ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), descriptor version 1.
+__device__ __forceinline__ uint64_t umma_desc_sw128(unsigned saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// D[tmem] (+)= A x B^T, u8 x s8 -> s32.
+__device__ __forceinline__ void umma_i8(unsigned tmem_d, uint64_t da, uint64_t db, unsigned idesc, unsigned accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accum), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(unsigned taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+
+// The 16 two-bit codes of a word (LSB first) as 16 bytes, code i in byte i.
+__device__ __forceinline__ uint4 expand_codes16(uint32_t w) {
+  const uint32_t t0 = w & 0x33333333u, t1 = (w >> 2) & 0x33333333u;
+  const uint32_t e = t0 & 0x0F0F0F0Fu, f = (t0 >> 4) & 0x0F0F0F0Fu;  // codes 4b, 4b+2 in byte b
+  const uint32_t g = t1 & 0x0F0F0F0Fu, h = (t1 >> 4) & 0x0F0F0F0Fu;  // codes 4b+1, 4b+3
+  const uint32_t lo = __byte_perm(e, g, 0x5140), hi = __byte_perm(f, h, 0x5140);
+  const uint32_t lo2 = __byte_perm(e, g, 0x7362), hi2 = __byte_perm(f, h, 0x7362);
+  return make_uint4(__byte_perm(lo, hi, 0x5410), __byte_perm(lo, hi, 0x7632), __byte_perm(lo2, hi2, 0x5410),
+                    __byte_perm(lo2, hi2, 0x7632));
+}
+
+struct TcGemmParams {
+  const uint32_t* codes;  // [E, rows, K/16]
+  const void* alpha;      // [E, rows]
+  const int* offsets;     // [E + 1] positions of each expert in the sorted list
+  const unsigned* list;   // [n_pos] slot ids (output rows), kTcBadSlot flagged
+  const int* meta;        // [n_pos, 8]
+  void* y;
+  int* err;
+  int64_t y_stride, expert_words, alpha_estride;
+  int rows, n_out, K, nwords;
+};
+
+template <int AT, int OT, bool SWIGLU>
+__global__ void __launch_bounds__(256, 1) tgemm_tc_kernel(TcGemmParams p, const __grid_constant__ CUtensorMap tmb) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t b_full[kTcStages], mma_done[kTcStages];
+  __shared__ unsigned s_tmem;
+  __shared__ int s_meta[kTcSlots][kTcMeta];
+  __shared__ unsigned s_slot[kTcSlots];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int mt = blockIdx.x, e = blockIdx.y;
+  pdl_wait();
+  pdl_trigger();
+  const int first = p.offsets[e], count = p.offsets[e + 1] - first;
+  if (count <= 0) return;
+
+  if (warp == 0) tmem_alloc(&s_tmem, kTcBRows);
+  if (tid == 0) {
+    for (int i = 0; i < kTcStages; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&mma_done[i], 1);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const unsigned tmem = s_tmem;
+
+  // A-tile role of this thread: tile row am, words 4aq..4aq+3 of each K block
+  const int am = tid >> 1, aq = tid & 1;
+  int arow;
+  bool aok;
+  if constexpr (SWIGLU) {  // rows 0-63: up rows n0+r; rows 64-127: gate rows n_out+n0+r
+    const int n0 = 64 * mt, r = am & 63;
+    aok = n0 + r < p.n_out;
+    arow = (am < 64 ? 0 : p.n_out) + n0 + r;
+  } else {
+    arow = kTcARows * mt + am;
+    aok = arow < p.rows;
+  }
+  const uint32_t* arow_ptr = p.codes + (int64_t)e * p.expert_words + (int64_t)(aok ? arow : 0) * p.nwords;
+  // instruction descriptor: s32 accumulate, A u8, B s8, both K-major, N = 256, M = 128
+  const unsigned idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((unsigned)(kTcBRows >> 3) << 17) |
+                         ((unsigned)(kTcARows >> 4) << 24);
+  const int KB = p.K / 128;
+  const int nchunks = (count + kTcSlots - 1) / kTcSlots;
+  // this thread's epilogue row (= TMEM lane) and column half
+  const int lg = warp & 3, hf = warp >> 2;
+  const int m = 32 * lg + lane;
+  int wrow;
+  bool mok;
+  if constexpr (SWIGLU) {
+    const int r = m & 63;
+    mok = 64 * mt + r < p.n_out;
+    wrow = (m < 64 ? 0 : p.n_out) + 64 * mt + r;
+  } else {
+    wrow = kTcARows * mt + m;
+    mok = wrow < p.rows;
+  }
+  const void* alpha_e = static_cast<const char*>(p.alpha) + (int64_t)e * p.alpha_estride * (AT == kBF16 ? 2 : 4);
+  const float a_m = mok ? load_f<AT>(alpha_e, wrow) : 0.0f;
+
+  bool fail = false;
+  int gi = 0;  // K blocks issued so far (all chunks): stage gi % 3, use gi / 3
+  for (int c = 0; c < nchunks && !fail; ++c) {
+    const int p0 = first + kTcSlots * c, npos = min(kTcSlots, count - kTcSlots * c);
+    if (tid < kTcSlots) {
+      if (tid < npos) {
+        s_slot[tid] = p.list[p0 + tid];
+#pragma unroll
+        for (int j = 0; j < kTcMeta; ++j) s_meta[tid][j] = p.meta[(int64_t)(p0 + tid) * kTcMeta + j];
+      } else {
+        s_slot[tid] = 0xffffffffu;
+      }
+    }
+    uint4 wnext = aok ? ld_stream_u4(arow_ptr + 4 * aq) : make_uint4(0, 0, 0, 0);
+    for (int kb = 0; kb < KB; ++kb, ++gi) {
+      const int st = gi % kTcStages, use = gi / kTcStages;
+      // the stage's previous MMAs must be done before it is refilled
+      const bool ok = gi < kTcStages || mbar_wait_bounded(&mma_done[st], (unsigned)((use - 1) & 1));
+      if (__syncthreads_or(!ok || fail)) {
+        fail = true;
+        break;
+      }
+      unsigned char* A = smem + st * kTcStage;
+      unsigned char* B = A + kTcABytes;
+      if (tid == 0) {
+        mbar_expect_tx(&b_full[st], (unsigned)kTcBBytes);
+        tma_load_2d(B, &tmb, 128 * kb, 4 * p0, &b_full[st]);
+      }
+      const uint4 w = wnext;
+      if (kb + 1 < KB) wnext = aok ? ld_stream_u4(arow_ptr + 8 * (kb + 1) + 4 * aq) : make_uint4(0, 0, 0, 0);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      unsigned char* arow_s = A + (am >> 3) * 1024 + (am & 7) * 128;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int u = 4 * aq + i;
+        *reinterpret_cast<uint4*>(arow_s + ((u ^ (am & 7)) << 4)) = expand_codes16(ws[i]);
+      }
+      fence_proxy_async_smem();  // the expanded codes are read by the tensor core (async proxy)
+      __syncthreads();
+      if (tid == 0) {
+        if (!mbar_wait_bounded(&b_full[st], (unsigned)(use & 1))) {
+          fail = true;
+        } else {
+          tc_fence_after();
+          const unsigned sa = smem_u32(A), sb = smem_u32(B);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_i8(tmem, umma_desc_sw128(sa + 32 * kk), umma_desc_sw128(sb + 32 * kk), idesc,
+                    (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&mma_done[st]);
+        }
+      }
+    }
+    if (__syncthreads_or(fail)) {
+      fail = true;
+      break;
+    }
+    // every MMA of the chunk has completed once the last commit arrives
+    {
+      const int last = gi - 1;
+      const bool ok = mbar_wait_bounded(&mma_done[last % kTcStages], (unsigned)((last / kTcStages) & 1));
+      if (__syncthreads_or(!ok)) {
+        fail = true;
+        break;
+      }
+    }
+    tc_fence_after();
+    // epilogue: 4 slots (16 accumulator columns) per TMEM load
+    float* s_up = reinterpret_cast<float*>(smem);            // [64 slots][64] (stage memory is idle now)
+    float* s_gate = s_up + kTcSlots * 64;
+    char* y = static_cast<char*>(p.y);
+    for (int pb = 0; pb < kTcSlots / 8; ++pb) {
+      const int pos0 = 32 * hf + 4 * pb;
+      if (pos0 >= npos) break;  // warp-uniform
+      uint32_t r[16];
+      tmem_ld16(tmem + ((unsigned)(32 * lg) << 16) + (unsigned)(4 * pos0), r);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int idx = pos0 + i;
+        if (idx < npos) {
+          const int* ms = s_meta[idx];
+          const int c0 = (int)r[4 * i] - ms[2], c1 = (int)r[4 * i + 1] - ms[3];
+          const int c2 = (int)r[4 * i + 2] - ms[4], c3 = (int)r[4 * i + 3] - ms[5];
+          const long long S = ((long long)c0 + 128LL * c1) + 16384LL * ((long long)c2 + 128LL * c3);
+          const unsigned slot = s_slot[idx];
+          const int sh = ms[0];
+          const bool nan_out = (sh == kFxaNonFinite) || (slot & kTcBadSlot);
+          const float v = __fmul_rn(nan_out ? __int_as_float(0x7fc00000) : fxa_value(S, sh), a_m);
+          if constexpr (SWIGLU) {
+            if (m < 64) s_up[idx * 64 + m] = v;
+            else s_gate[idx * 64 + (m - 64)] = v;
+          } else if (mok) {
+            store_f<OT>(y + (int64_t)(slot & ~kTcBadSlot) * p.y_stride * (OT == kBF16 ? 2 : 4), wrow, v);
+          }
+        }
+      }
+    }
+    if constexpr (SWIGLU) {
+      __syncthreads();
+      for (int q = tid; q < npos * 64; q += 256) {
+        const int idx = q >> 6, nn = q & 63;
+        const int n = 64 * mt + nn;
+        if (n < p.n_out) {
+          float up = s_up[idx * 64 + nn], gate = s_gate[idx * 64 + nn];
+          up = fminf(fmaxf(up, -7.0f), 7.0f);
+          gate = fminf(gate, 7.0f);
+          const unsigned slot = s_slot[idx];
+          // an out-of-range expert id gives a NaN row (the clamps would turn NaN into -49)
+          store_f<OT>(y + (int64_t)(slot & ~kTcBadSlot) * p.y_stride * (OT == kBF16 ? 2 : 4), n,
+                      (slot & kTcBadSlot) ? __int_as_float(0x7fc00000)
+                                          : __fmul_rn(__fmul_rn(up, gate), msigmoid(gate)));
+        }
+      }
+    }
+    fence_proxy_async_smem();  // the staging writes precede the next chunk's TMA into the same bytes
+    tc_fence_before();
+    __syncthreads();  // TMEM and stage memory free for the next chunk
+  }
+  if (fail) {
+    if (tid == 0) {
+      atomicOr(p.err, kErrFlagTimeout);
+      // let this CTA's copies and MMAs in flight land (bounded) before exit
+      for (int g = max(0, gi - kTcStages); g < gi; ++g) {
+        mbar_wait_bounded(&b_full[g % kTcStages], (unsigned)((g / kTcStages) & 1));
+        mbar_wait_bounded(&mma_done[g % kTcStages], (unsigned)((g / kTcStages) & 1));
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTcBRows);
+  }
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" int64_t maple_ternary_grouped_gemm_tc_workspace_bytes(int64_t n_slots, int64_t k) {
+  if (n_slots < 0 || k <= 0) return -1;
+  const int64_t dig = (n_slots * 4 * k + 255) / 256 * 256;
+  return dig + (n_slots * kTcMeta * 4 + 255) / 256 * 256;
+}
+
+extern "C" int maple_ternary_grouped_gemm_tc(const void* x, int x_dtype, int64_t in_rows, int64_t k,
+                                             int64_t x_row_stride, const uint32_t* codes, int64_t n_experts,
+                                             int64_t code_rows, const void* alpha, int alpha_dtype,
+                                             const int32_t* offsets, const uint32_t* list, int64_t n_slots,
+                                             int64_t in_div, int swiglu, void* y, int y_dtype,
+                                             int64_t y_row_stride, void* workspace, int64_t workspace_bytes,
+                                             int* err, void* stream) {
+  if (in_rows < 0 || n_slots < 0 || n_experts <= 0 || code_rows <= 0 || in_div <= 0) return kErrShape;
+  if (k <= 0 || k % 128 != 0 || k > 8192) return kErrShape;
+  if (n_slots == 0) return kOk;
+  if (swiglu && code_rows % 2 != 0) return kErrShape;
+  if (!x || !codes || !alpha || !offsets || !list || !y || !err || !workspace) return kErrShape;
+  if ((n_slots - 1) / in_div >= in_rows) return kErrBounds;
+  if (x_dtype != kBF16 && x_dtype != kF32) return kErrDtype;
+  if ((alpha_dtype != kBF16 && alpha_dtype != kF32) || (y_dtype != kBF16 && y_dtype != kF32)) return kErrDtype;
+  if (workspace_bytes < maple_ternary_grouped_gemm_tc_workspace_bytes(n_slots, k)) return kErrWorkspace;
+  if ((reinterpret_cast<uintptr_t>(codes) | reinterpret_cast<uintptr_t>(workspace)) & 255) return kErrAlign;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || ((x_row_stride * (x_dtype == kBF16 ? 2 : 4)) & 15)) return kErrAlign;
+  if (n_experts > 65535 || code_rows > (1LL << 30) || n_slots * 4 > (1LL << 31) - 1) return kErrShape;
+  int8_t* digits = static_cast<int8_t*>(workspace);
+  int* meta = reinterpret_cast<int*>(static_cast<char*>(workspace) + (n_slots * 4 * k + 255) / 256 * 256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int K = (int)k, iters = (K + 255) / 256;
+  const size_t esmem = (size_t)iters * 256 * sizeof(uint2) + (size_t)K * sizeof(float);
+  cudaError_t e = cudaSuccess;
+  {
+    auto kern = x_dtype == kBF16 ? fxa_plain_kernel<kBF16> : fxa_plain_kernel<kF32>;
+    if (esmem > 32 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)esmem);
+    if (e == cudaSuccess)
+      e = launch_k(kern, dim3((unsigned)n_slots), dim3(256), esmem, st, x, x_row_stride, K, offsets, (int)n_experts,
+                   list, (int)in_div, digits, meta);
+    if (e != cudaSuccess) return kErrCuda;
+  }
+  CUtensorMap tmb;
+  if (!tmap_u8_2d(digits, k, 4 * n_slots, 128, kTcBRows, &tmb)) return kErrCuda;
+  TcGemmParams p{};
+  p.codes = codes; p.alpha = alpha; p.offsets = offsets; p.list = list; p.meta = meta; p.y = y; p.err = err;
+  p.y_stride = y_row_stride; p.expert_words = code_rows * (k / 16); p.alpha_estride = code_rows;
+  p.rows = (int)code_rows; p.n_out = swiglu ? (int)(code_rows / 2) : (int)code_rows;
+  p.K = K; p.nwords = (int)(k / 16);
+  const int tiles = swiglu ? (p.n_out + 63) / 64 : (p.rows + kTcARows - 1) / kTcARows;
+  const dim3 grid((unsigned)tiles, (unsigned)n_experts);
+  const size_t gsmem = (size_t)kTcStages * kTcStage + 1024;
+#define MB_TCG(AT_, OT_, SW_)                                                                                  \
+  do {                                                                                                         \
+    auto kern = tgemm_tc_kernel<AT_, OT_, SW_>;                                                                \
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsmem);                   \
+    if (e == cudaSuccess) e = launch_k(kern, grid, dim3(256), gsmem, st, p, tmb);                             \
+  } while (0)
+#define MB_TCG_SW(AT_, OT_) \
+  do {                      \
+    if (swiglu) MB_TCG(AT_, OT_, true); else MB_TCG(AT_, OT_, false); \
+  } while (0)
+  if (alpha_dtype == kBF16) {
+    if (y_dtype == kBF16) MB_TCG_SW(kBF16, kBF16); else MB_TCG_SW(kBF16, kF32);
+  } else {
+    if (y_dtype == kBF16) MB_TCG_SW(kF32, kBF16); else MB_TCG_SW(kF32, kF32);
+  }
+#undef MB_TCG_SW
+#undef MB_TCG
+  return e == cudaSuccess ? kOk : kErrCuda;
+}

@@ -143,11 +143,13 @@ class MoePlan:
     (``offsets [E+1]`` int32, ``slots`` uint32), shared by the grouped up|gate
     and down GEMMs of one MoE layer."""
 
-    def __init__(self, offsets: torch.Tensor, slots: torch.Tensor, n_experts: int, n_slots: int):
+    def __init__(self, offsets: torch.Tensor, slots: torch.Tensor, n_experts: int, n_slots: int,
+                 total_experts: int | None = None):
         self.offsets = offsets
         self.slots = slots
         self.n_experts = n_experts
         self.n_slots = n_slots
+        self.total_experts = n_experts if total_experts is None else total_experts
 
 
 def moe_plan(expert_ids: torch.Tensor, n_experts: int, *, e_first: int = 0, n_local: int | None = None) -> MoePlan:
@@ -163,7 +165,7 @@ def moe_plan(expert_ids: torch.Tensor, n_experts: int, *, e_first: int = 0, n_lo
     slots = torch.empty(max(n, 1), dtype=torch.int32, device=ids.device)
     check(lib().maple_moe_plan_range(ptr(ids), n, n_experts, int(e_first), n_local, ptr(offsets), ptr(slots),
                                      stream_ptr(ids.device)), op)
-    return MoePlan(offsets, slots, n_local, n)
+    return MoePlan(offsets, slots, n_local, n, total_experts=n_experts)
 
 
 def ep_combine(recv: torch.Tensor, expert_ids: torch.Tensor, topk_weight: torch.Tensor, n_experts: int,
@@ -188,10 +190,51 @@ def ep_combine(recv: torch.Tensor, expert_ids: torch.Tensor, topk_weight: torch.
     return y
 
 
-def _grouped(op, x_rows, per, w, alpha, plan, swiglu, out_rows, n_out, dtype, out=None):
-    """Grouped expert GEMM: input row of slot s is ``s // per``."""
+TC_GEMM_MIN_SLOTS = 16
+
+
+def _tc_gemm_enabled() -> bool:
+    """``MAPLE_TC_GEMM=0`` keeps every grouped expert GEMM on mma.sync."""
+    import os
+
+    return os.environ.get("MAPLE_TC_GEMM", "1") != "0"
+
+
+def use_tc_grouped(plan: "MoePlan", k_in: int) -> bool:
+    """The tcgen05 grouped GEMM pays off once the experts average at least
+    TC_GEMM_MIN_SLOTS routed slots (prompt prefill, large batches): its MMA
+    tile is 64 slots wide.  Both paths give identical results."""
+    return (_tc_gemm_enabled() and k_in % 128 == 0 and
+            plan.n_slots >= TC_GEMM_MIN_SLOTS * max(plan.total_experts, 1))
+
+
+def _grouped_tc(op, x_rows, per, w, alpha, plan, swiglu, y):
     E, rows, nwords = w.shape
     k_in = nwords * _CODES_PER_WORD
+    if x_rows.stride(-1) != 1 or (x_rows.stride(0) * x_rows.element_size()) % 16 or x_rows.data_ptr() % 16:
+        x_rows = x_rows.contiguous()
+    L = lib()
+    ws = torch.empty(L.maple_ternary_grouped_gemm_tc_workspace_bytes(plan.n_slots, k_in), dtype=torch.uint8,
+                     device=x_rows.device)
+    check(L.maple_ternary_grouped_gemm_tc(
+        ptr(x_rows), dtype_code(x_rows, op), x_rows.shape[0], k_in, x_rows.stride(0), ptr(w), E, rows, ptr(alpha),
+        dtype_code(alpha, op), ptr(plan.offsets), ptr(plan.slots), plan.n_slots, per, int(swiglu), ptr(y),
+        dtype_code(y, op), y.stride(0), ptr(ws), ws.numel(), ptr(_err(x_rows.device)), stream_ptr(x_rows.device)),
+        op)
+    return y
+
+
+def _grouped(op, x_rows, per, w, alpha, plan, swiglu, out_rows, n_out, dtype, out=None, tc=None):
+    """Grouped expert GEMM: input row of slot s is ``s // per``.  ``tc``
+    forces (True) or forbids (False) the tcgen05 path; by default it runs
+    where the experts average enough routed slots."""
+    E, rows, nwords = w.shape
+    k_in = nwords * _CODES_PER_WORD
+    if tc is None:
+        tc = use_tc_grouped(plan, k_in)
+    if tc:
+        y = out if out is not None else torch.empty(out_rows, n_out, device=x_rows.device, dtype=dtype)
+        return _grouped_tc(op, x_rows, per, w, alpha, plan, swiglu, y)
     frag, meta = fxa_encode(x_rows)
     y = out if out is not None else torch.empty(out_rows, n_out, device=x_rows.device, dtype=dtype)
     check(lib().maple_ternary_grouped_gemm(
