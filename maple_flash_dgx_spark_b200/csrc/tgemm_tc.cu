@@ -45,6 +45,8 @@ constexpr int kTcSlots = kTcBRows / 4;
 constexpr int kTcABytes = kTcARows * 128;     // one 128-byte K block of A
 constexpr int kTcBBytes = kTcBRows * 128;
 constexpr int kTcStage = kTcABytes + kTcBBytes;
+constexpr int kTcCodeSlots = 8;               // code tiles in flight (K blocks ahead)
+constexpr int kTcCodeBytes = kTcARows * 32;   // one K block of packed codes: 128 rows x 8 words
 
 // ---------------------------------------------------------------- encode --
 // Position p (expert-sorted) encodes input row (list[p] & ~bad) / in_div;
@@ -61,8 +63,13 @@ __global__ void __launch_bounds__(256) fxa_plain_kernel(const void* x, int64_t x
   float* xsm = reinterpret_cast<float*>(smem + (size_t)iters * 256 * sizeof(uint2));
   const int p = blockIdx.x;
   pdl_wait();
-  pdl_trigger();
-  if (p >= offsets[n_experts]) return;
+  // the GEMM that follows is released only once these CTAs are done: its
+  // CTAs (216 KB of shared memory each) would otherwise take the SMs this
+  // multi-wave grid still needs
+  if (p >= offsets[n_experts]) {
+    pdl_trigger();
+    return;
+  }
   const int64_t row = (int64_t)(list[p] & ~kTcBadSlot) / in_div;
   const void* xr = static_cast<const char*>(x) + row * x_stride * (XT == kBF16 ? 2 : 4);
   // shift and digit totals exactly as the fragment encoders compute them
@@ -86,6 +93,7 @@ __global__ void __launch_bounds__(256) fxa_plain_kernel(const void* x, int64_t x
     else if (j < 6) v = fb.tot[j - 2];
     meta[(int64_t)p * kTcMeta + j] = v;
   }
+  pdl_trigger();
 }
 
 // ------------------------------------------------------------ tcgen05 ----
@@ -156,198 +164,273 @@ struct TcGemmParams {
   int rows, n_out, K, nwords;
 };
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+constexpr int kTcExp = 256;  // expander / epilogue threads (warps 0-7)
+// Barrier among the expander threads only (the other warps run on).
+__device__ __forceinline__ void sync_expanders() { asm volatile("bar.sync 1, 256;\n" ::: "memory"); }
+// The same barrier returning the AND of every thread's predicate, so a
+// bounded wait's outcome is one decision for all four warps.
+__device__ __forceinline__ bool sync_expanders_and(bool v) {
+  unsigned r;
+  asm volatile(
+      "{\n .reg .pred a, b;\n setp.ne.u32 a, %1, 0;\n bar.red.and.pred b, 1, 256, a;\n selp.u32 %0, 1, 0, b;\n}\n"
+      : "=r"(r)
+      : "r"((unsigned)v)
+      : "memory");
+  return r != 0;
+}
+
+// Roles (352 threads): warps 0-7 expand the codes (thread t: weight row
+// t % 128 of the tile, words 4(t / 128) .. +3 of each K block) and run the
+// epilogue (TMEM lane group = warp % 4, slot quads split between the two
+// warp halves); warp 10 lane 0 streams the packed code tiles from HBM by TMA
+// into a ring of 8 K blocks (32 KB in flight per SM hides the DRAM latency);
+// warp 8 lane 0 loads the digit tiles; warp 9 lane 0 issues the MMAs.  Per
+// code slot: cfull (TMA bytes), cempty (256 expander arrivals); per MMA stage:
+// full (TMA bytes), afull (256 expander arrivals), empty (tcgen05.commit); per
+// chunk of 64 slots: accfull (commit after its last MMA), accempty (256
+// epilogue arrivals).  N = 64 x the digit boxes the chunk needs, so decode-
+// sized groups (a few slots per expert) run narrow MMAs.  The dependent launch
+// is released only after the mainloop: an earlier trigger would let the next
+// kernel's CTAs sit on SMs this multi-wave grid still needs.
 template <int AT, int OT, bool SWIGLU>
-__global__ void __launch_bounds__(256, 1) tgemm_tc_kernel(TcGemmParams p, const __grid_constant__ CUtensorMap tmb) {
+__global__ void __launch_bounds__(352, 1) tgemm_tc_kernel(TcGemmParams p, const __grid_constant__ CUtensorMap tmb,
+                                                          const __grid_constant__ CUtensorMap tmc) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t b_full[kTcStages], mma_done[kTcStages];
+  float* s_gate = reinterpret_cast<float*>(smem + kTcStages * kTcStage);  // [2][64 slots][64 rows]
+  unsigned char* codes_s = smem + kTcStages * kTcStage + 2 * kTcSlots * 64 * sizeof(float);  // [8][128][32 B]
+  __shared__ uint64_t full[kTcStages], afull[kTcStages], empty[kTcStages], accfull, accempty;
+  __shared__ uint64_t cfull[kTcCodeSlots], cempty[kTcCodeSlots];
   __shared__ unsigned s_tmem;
+  __shared__ int s_fail;
   __shared__ int s_meta[kTcSlots][kTcMeta];
   __shared__ unsigned s_slot[kTcSlots];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int mt = blockIdx.x, e = blockIdx.y;
   pdl_wait();
-  pdl_trigger();
   const int first = p.offsets[e], count = p.offsets[e + 1] - first;
-  if (count <= 0) return;
+  if (count <= 0) {
+    pdl_trigger();
+    return;
+  }
 
   if (warp == 0) tmem_alloc(&s_tmem, kTcBRows);
   if (tid == 0) {
     for (int i = 0; i < kTcStages; ++i) {
-      mbar_init(&b_full[i], 1);
-      mbar_init(&mma_done[i], 1);
+      mbar_init(&full[i], 1);
+      mbar_init(&afull[i], kTcExp);
+      mbar_init(&empty[i], 1);
     }
+    mbar_init(&accfull, 1);
+    mbar_init(&accempty, kTcExp);
+    for (int i = 0; i < kTcCodeSlots; ++i) {
+      mbar_init(&cfull[i], 1);
+      mbar_init(&cempty[i], kTcExp);
+    }
+    s_fail = 0;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const unsigned tmem = s_tmem;
-
-  // A-tile role of this thread: tile row am, words 4aq..4aq+3 of each K block
-  const int am = tid >> 1, aq = tid & 1;
-  int arow;
-  bool aok;
-  if constexpr (SWIGLU) {  // rows 0-63: up rows n0+r; rows 64-127: gate rows n_out+n0+r
-    const int n0 = 64 * mt, r = am & 63;
-    aok = n0 + r < p.n_out;
-    arow = (am < 64 ? 0 : p.n_out) + n0 + r;
-  } else {
-    arow = kTcARows * mt + am;
-    aok = arow < p.rows;
-  }
-  const uint32_t* arow_ptr = p.codes + (int64_t)e * p.expert_words + (int64_t)(aok ? arow : 0) * p.nwords;
-  // instruction descriptor: s32 accumulate, A u8, B s8, both K-major, N = 256, M = 128
-  const unsigned idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((unsigned)(kTcBRows >> 3) << 17) |
-                         ((unsigned)(kTcARows >> 4) << 24);
   const int KB = p.K / 128;
   const int nchunks = (count + kTcSlots - 1) / kTcSlots;
-  // this thread's epilogue row (= TMEM lane) and column half
-  const int lg = warp & 3, hf = warp >> 2;
-  const int m = 32 * lg + lane;
-  int wrow;
-  bool mok;
-  if constexpr (SWIGLU) {
-    const int r = m & 63;
-    mok = 64 * mt + r < p.n_out;
-    wrow = (m < 64 ? 0 : p.n_out) + 64 * mt + r;
-  } else {
-    wrow = kTcARows * mt + m;
-    mok = wrow < p.rows;
-  }
-  const void* alpha_e = static_cast<const char*>(p.alpha) + (int64_t)e * p.alpha_estride * (AT == kBF16 ? 2 : 4);
-  const float a_m = mok ? load_f<AT>(alpha_e, wrow) : 0.0f;
+  auto nboxes_of = [&](int c) {  // 64-row digit boxes (16 slots each) chunk c needs
+    const int npos = min(kTcSlots, count - kTcSlots * c);
+    return (npos + 15) / 16;
+  };
 
-  bool fail = false;
-  int gi = 0;  // K blocks issued so far (all chunks): stage gi % 3, use gi / 3
-  for (int c = 0; c < nchunks && !fail; ++c) {
-    const int p0 = first + kTcSlots * c, npos = min(kTcSlots, count - kTcSlots * c);
-    if (tid < kTcSlots) {
-      if (tid < npos) {
-        s_slot[tid] = p.list[p0 + tid];
-#pragma unroll
-        for (int j = 0; j < kTcMeta; ++j) s_meta[tid][j] = p.meta[(int64_t)(p0 + tid) * kTcMeta + j];
-      } else {
-        s_slot[tid] = 0xffffffffu;
+  if (warp == 8) {
+    // ---------------- TMA producer: digit tiles ----------------
+    if (lane == 0) {
+      int gi = 0;
+      for (int c = 0; c < nchunks; ++c) {
+        const int p0 = first + kTcSlots * c, nb = nboxes_of(c);
+        for (int kb = 0; kb < KB; ++kb, ++gi) {
+          const int st = gi % kTcStages, use = gi / kTcStages;
+          if (gi >= kTcStages && !mbar_wait_bounded(&empty[st], (unsigned)((use - 1) & 1))) {
+            s_fail = 1;
+            atomicOr(p.err, kErrFlagTimeout);
+            c = nchunks;
+            break;
+          }
+          unsigned char* B = smem + st * kTcStage + kTcABytes;
+          mbar_expect_tx(&full[st], (unsigned)(nb * 8192));
+          for (int bx = 0; bx < nb; ++bx) tma_load_2d(B + bx * 8192, &tmb, 128 * kb, 4 * p0 + 64 * bx, &full[st]);
+        }
       }
     }
-    uint4 wnext = aok ? ld_stream_u4(arow_ptr + 4 * aq) : make_uint4(0, 0, 0, 0);
-    for (int kb = 0; kb < KB; ++kb, ++gi) {
-      const int st = gi % kTcStages, use = gi / kTcStages;
-      // the stage's previous MMAs must be done before it is refilled
-      const bool ok = gi < kTcStages || mbar_wait_bounded(&mma_done[st], (unsigned)((use - 1) & 1));
-      if (__syncthreads_or(!ok || fail)) {
-        fail = true;
-        break;
+    __syncwarp();
+  } else if (warp == 10) {
+    // ---------------- TMA producer: packed code tiles ----------------
+    if (lane == 0) {
+      // tile rows: two boxes of 64 rows (SwiGLU: the up and the gate rows)
+      const int rows0 = e * p.rows + (SWIGLU ? 64 * mt : kTcARows * mt);
+      const int rows1 = SWIGLU ? e * p.rows + p.n_out + 64 * mt : rows0 + 64;
+      const int total = nchunks * KB;
+      for (int gc = 0; gc < total; ++gc) {
+        const int slot = gc % kTcCodeSlots, use = gc / kTcCodeSlots, kb = gc % KB;
+        if (gc >= kTcCodeSlots && !mbar_wait_bounded(&cempty[slot], (unsigned)((use - 1) & 1))) {
+          s_fail = 1;
+          atomicOr(p.err, kErrFlagTimeout);
+          break;
+        }
+        unsigned char* dst = codes_s + slot * kTcCodeBytes;
+        mbar_expect_tx(&cfull[slot], (unsigned)kTcCodeBytes);
+        tma_load_2d(dst, &tmc, 8 * kb, rows0, &cfull[slot]);
+        tma_load_2d(dst + 64 * 32, &tmc, 8 * kb, rows1, &cfull[slot]);
       }
-      unsigned char* A = smem + st * kTcStage;
-      unsigned char* B = A + kTcABytes;
-      if (tid == 0) {
-        mbar_expect_tx(&b_full[st], (unsigned)kTcBBytes);
-        tma_load_2d(B, &tmb, 128 * kb, 4 * p0, &b_full[st]);
-      }
-      const uint4 w = wnext;
-      if (kb + 1 < KB) wnext = aok ? ld_stream_u4(arow_ptr + 8 * (kb + 1) + 4 * aq) : make_uint4(0, 0, 0, 0);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-      unsigned char* arow_s = A + (am >> 3) * 1024 + (am & 7) * 128;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int u = 4 * aq + i;
-        *reinterpret_cast<uint4*>(arow_s + ((u ^ (am & 7)) << 4)) = expand_codes16(ws[i]);
-      }
-      fence_proxy_async_smem();  // the expanded codes are read by the tensor core (async proxy)
-      __syncthreads();
-      if (tid == 0) {
-        if (!mbar_wait_bounded(&b_full[st], (unsigned)(use & 1))) {
-          fail = true;
-        } else {
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int gi = 0;
+      bool ok = true;
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const unsigned n = (unsigned)(64 * nboxes_of(c));
+        const unsigned idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((n >> 3) << 17) | ((unsigned)(kTcARows >> 4) << 24);
+        if (c > 0) ok = mbar_wait_bounded(&accempty, (unsigned)((c - 1) & 1));
+        for (int kb = 0; kb < KB && ok; ++kb, ++gi) {
+          const int st = gi % kTcStages, use = gi / kTcStages;
+          ok = mbar_wait_bounded(&afull[st], (unsigned)(use & 1)) && mbar_wait_bounded(&full[st], (unsigned)(use & 1));
+          if (!ok) break;
           tc_fence_after();
-          const unsigned sa = smem_u32(A), sb = smem_u32(B);
+          const unsigned sa = smem_u32(smem + st * kTcStage), sb = sa + kTcABytes;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             umma_i8(tmem, umma_desc_sw128(sa + 32 * kk), umma_desc_sw128(sb + 32 * kk), idesc,
                     (kb > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&mma_done[st]);
+          umma_commit(&empty[st]);
+        }
+        if (ok) umma_commit(&accfull);
+      }
+      if (!ok) {
+        s_fail = 1;
+        atomicOr(p.err, kErrFlagTimeout);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- expanders + epilogue (warps 0-7) ----------------
+    const int m = tid & 127, hh = tid >> 7;  // weight row of the tile (= TMEM lane), word half
+    int arow;
+    bool aok;
+    if constexpr (SWIGLU) {  // rows 0-63: up rows n0+r; rows 64-127: gate rows n_out+n0+r
+      const int n0 = 64 * mt, r = m & 63;
+      aok = n0 + r < p.n_out;
+      arow = (m < 64 ? 0 : p.n_out) + n0 + r;
+    } else {
+      arow = kTcARows * mt + m;
+      aok = arow < p.rows;
+    }
+    const void* alpha_e = static_cast<const char*>(p.alpha) + (int64_t)e * p.alpha_estride * (AT == kBF16 ? 2 : 4);
+    const float a_m = aok ? load_f<AT>(alpha_e, arow) : 0.0f;
+    char* y = static_cast<char*>(p.y);
+    int gi = 0;
+    bool ok = true;
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int p0 = first + kTcSlots * c, npos = min(kTcSlots, count - kTcSlots * c);
+      if (tid < kTcSlots) {
+        if (tid < npos) {
+          s_slot[tid] = p.list[p0 + tid];
+#pragma unroll
+          for (int j = 0; j < kTcMeta; ++j) s_meta[tid][j] = p.meta[(int64_t)(p0 + tid) * kTcMeta + j];
+        } else {
+          s_slot[tid] = 0xffffffffu;
         }
       }
-    }
-    if (__syncthreads_or(fail)) {
-      fail = true;
-      break;
-    }
-    // every MMA of the chunk has completed once the last commit arrives
-    {
-      const int last = gi - 1;
-      const bool ok = mbar_wait_bounded(&mma_done[last % kTcStages], (unsigned)((last / kTcStages) & 1));
-      if (__syncthreads_or(!ok)) {
-        fail = true;
+      for (int kb = 0; kb < KB; ++kb, ++gi) {
+        const int st = gi % kTcStages, use = gi / kTcStages;
+        const int cs = gi % kTcCodeSlots, cuse = gi / kTcCodeSlots;
+        const bool ready = (gi < kTcStages || mbar_wait_bounded(&empty[st], (unsigned)((use - 1) & 1))) &&
+                           mbar_wait_bounded(&cfull[cs], (unsigned)(cuse & 1));
+        if (!sync_expanders_and(ready)) {
+          ok = false;
+          break;
+        }
+        const uint4 wa = aok ? *reinterpret_cast<const uint4*>(codes_s + cs * kTcCodeBytes + m * 32 + hh * 16)
+                             : make_uint4(0, 0, 0, 0);
+        mbar_arrive(&cempty[cs]);
+        unsigned char* arow_s = smem + st * kTcStage + (m >> 3) * 1024 + (m & 7) * 128;
+        const uint32_t ws[4] = {wa.x, wa.y, wa.z, wa.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int u = 4 * hh + i;
+          *reinterpret_cast<uint4*>(arow_s + ((u ^ (m & 7)) << 4)) = expand_codes16(ws[i]);
+        }
+        fence_proxy_async_smem();  // the tensor core reads these bytes through the async proxy
+        mbar_arrive(&afull[st]);
+      }
+      if (!ok || !sync_expanders_and(mbar_wait_bounded(&accfull, (unsigned)(c & 1)))) {
+        ok = false;
         break;
       }
-    }
-    tc_fence_after();
-    // epilogue: 4 slots (16 accumulator columns) per TMEM load
-    float* s_up = reinterpret_cast<float*>(smem);            // [64 slots][64] (stage memory is idle now)
-    float* s_gate = s_up + kTcSlots * 64;
-    char* y = static_cast<char*>(p.y);
-    for (int pb = 0; pb < kTcSlots / 8; ++pb) {
-      const int pos0 = 32 * hf + 4 * pb;
-      if (pos0 >= npos) break;  // warp-uniform
-      uint32_t r[16];
-      tmem_ld16(tmem + ((unsigned)(32 * lg) << 16) + (unsigned)(4 * pos0), r);
+      tc_fence_after();  // (the reduction above also made s_slot / s_meta visible)
+      if (c == nchunks - 1) pdl_trigger();
+      for (int pb = hh; 4 * pb < npos; pb += 2) {
+        uint32_t r[16];
+        tmem_ld16(tmem + ((unsigned)(32 * (warp & 3)) << 16) + (unsigned)(16 * pb), r);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int idx = pos0 + i;
-        if (idx < npos) {
-          const int* ms = s_meta[idx];
-          const int c0 = (int)r[4 * i] - ms[2], c1 = (int)r[4 * i + 1] - ms[3];
-          const int c2 = (int)r[4 * i + 2] - ms[4], c3 = (int)r[4 * i + 3] - ms[5];
-          const long long S = ((long long)c0 + 128LL * c1) + 16384LL * ((long long)c2 + 128LL * c3);
-          const unsigned slot = s_slot[idx];
-          const int sh = ms[0];
-          const bool nan_out = (sh == kFxaNonFinite) || (slot & kTcBadSlot);
-          const float v = __fmul_rn(nan_out ? __int_as_float(0x7fc00000) : fxa_value(S, sh), a_m);
-          if constexpr (SWIGLU) {
-            if (m < 64) s_up[idx * 64 + m] = v;
-            else s_gate[idx * 64 + (m - 64)] = v;
-          } else if (mok) {
-            store_f<OT>(y + (int64_t)(slot & ~kTcBadSlot) * p.y_stride * (OT == kBF16 ? 2 : 4), wrow, v);
+        for (int i = 0; i < 4; ++i) {
+          const int idx = 4 * pb + i;
+          if (idx < npos) {
+            const int* ms = s_meta[idx];
+            const int c0 = (int)r[4 * i] - ms[2], c1 = (int)r[4 * i + 1] - ms[3];
+            const int c2 = (int)r[4 * i + 2] - ms[4], c3 = (int)r[4 * i + 3] - ms[5];
+            const long long S = ((long long)c0 + 128LL * c1) + 16384LL * ((long long)c2 + 128LL * c3);
+            const unsigned slot = s_slot[idx];
+            const int sh = ms[0];
+            const bool nan_out = (sh == kFxaNonFinite) || (slot & kTcBadSlot);
+            const float v = __fmul_rn(nan_out ? __int_as_float(0x7fc00000) : fxa_value(S, sh), a_m);
+            if constexpr (SWIGLU) {
+              if (m >= 64) s_gate[idx * 64 + (m - 64)] = v;
+              else s_gate[kTcSlots * 64 + idx * 64 + m] = v;  // up values after the gate block
+            } else if (aok) {
+              store_f<OT>(y + (int64_t)(slot & ~kTcBadSlot) * p.y_stride * (OT == kBF16 ? 2 : 4), arow, v);
+            }
           }
         }
       }
-    }
-    if constexpr (SWIGLU) {
-      __syncthreads();
-      for (int q = tid; q < npos * 64; q += 256) {
-        const int idx = q >> 6, nn = q & 63;
-        const int n = 64 * mt + nn;
-        if (n < p.n_out) {
-          float up = s_up[idx * 64 + nn], gate = s_gate[idx * 64 + nn];
-          up = fminf(fmaxf(up, -7.0f), 7.0f);
-          gate = fminf(gate, 7.0f);
-          const unsigned slot = s_slot[idx];
-          // an out-of-range expert id gives a NaN row (the clamps would turn NaN into -49)
-          store_f<OT>(y + (int64_t)(slot & ~kTcBadSlot) * p.y_stride * (OT == kBF16 ? 2 : 4), n,
-                      (slot & kTcBadSlot) ? __int_as_float(0x7fc00000)
-                                          : __fmul_rn(__fmul_rn(up, gate), msigmoid(gate)));
+      tc_fence_before();
+      mbar_arrive(&accempty);  // this thread's TMEM reads are done
+      if constexpr (SWIGLU) {
+        sync_expanders();
+        for (int q = tid; q < npos * 64; q += kTcExp) {
+          const int idx = q >> 6, nn = q & 63;
+          const int n = 64 * mt + nn;
+          if (n < p.n_out) {
+            float up = s_gate[kTcSlots * 64 + idx * 64 + nn], gate = s_gate[idx * 64 + nn];
+            up = fminf(fmaxf(up, -7.0f), 7.0f);
+            gate = fminf(gate, 7.0f);
+            const unsigned slot = s_slot[idx];
+            // an out-of-range expert id gives a NaN row (the clamps would turn NaN into -49)
+            store_f<OT>(y + (int64_t)(slot & ~kTcBadSlot) * p.y_stride * (OT == kBF16 ? 2 : 4), n,
+                        (slot & kTcBadSlot) ? __int_as_float(0x7fc00000)
+                                            : __fmul_rn(__fmul_rn(up, gate), msigmoid(gate)));
+          }
         }
       }
+      sync_expanders();  // staging and slot tables free for the next chunk
     }
-    fence_proxy_async_smem();  // the staging writes precede the next chunk's TMA into the same bytes
-    tc_fence_before();
-    __syncthreads();  // TMEM and stage memory free for the next chunk
-  }
-  if (fail) {
-    if (tid == 0) {
+    if (!ok) {
+      s_fail = 1;
       atomicOr(p.err, kErrFlagTimeout);
-      // let this CTA's copies and MMAs in flight land (bounded) before exit
-      for (int g = max(0, gi - kTcStages); g < gi; ++g) {
-        mbar_wait_bounded(&b_full[g % kTcStages], (unsigned)((g / kTcStages) & 1));
-        mbar_wait_bounded(&mma_done[g % kTcStages], (unsigned)((g / kTcStages) & 1));
-      }
     }
-    tc_fence_before();
-    __syncthreads();
   }
+  __syncthreads();
+  pdl_trigger();  // (a no-op where the epilogue already released it)
+  if (s_fail) {
+    // give the copies and MMAs this CTA issued time to land (about a
+    // millisecond, bounded) before its shared and tensor memory go
+    for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+  }
+  tc_fence_before();
+  __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTcBRows);
@@ -398,7 +481,10 @@ extern "C" int maple_ternary_grouped_gemm_tc(const void* x, int x_dtype, int64_t
     if (e != cudaSuccess) return kErrCuda;
   }
   CUtensorMap tmb;
-  if (!tmap_u8_2d(digits, k, 4 * n_slots, 128, kTcBRows, &tmb)) return kErrCuda;
+  CUtensorMap tmc;
+  if (!tmap_2d(digits, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, 4 * n_slots, 128, 64, true, &tmb) ||
+      !tmap_2d(codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, k / 16, n_experts * code_rows, 8, 64, false, &tmc))
+    return kErrCuda;
   TcGemmParams p{};
   p.codes = codes; p.alpha = alpha; p.offsets = offsets; p.list = list; p.meta = meta; p.y = y; p.err = err;
   p.y_stride = y_row_stride; p.expert_words = code_rows * (k / 16); p.alpha_estride = code_rows;
@@ -406,12 +492,13 @@ extern "C" int maple_ternary_grouped_gemm_tc(const void* x, int x_dtype, int64_t
   p.K = K; p.nwords = (int)(k / 16);
   const int tiles = swiglu ? (p.n_out + 63) / 64 : (p.rows + kTcARows - 1) / kTcARows;
   const dim3 grid((unsigned)tiles, (unsigned)n_experts);
-  const size_t gsmem = (size_t)kTcStages * kTcStage + 1024;
+  const size_t gsmem = (size_t)kTcStages * kTcStage + 2 * (size_t)kTcSlots * 64 * sizeof(float) +
+                       (size_t)kTcCodeSlots * kTcCodeBytes + 1024;
 #define MB_TCG(AT_, OT_, SW_)                                                                                  \
   do {                                                                                                         \
     auto kern = tgemm_tc_kernel<AT_, OT_, SW_>;                                                                \
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsmem);                   \
-    if (e == cudaSuccess) e = launch_k(kern, grid, dim3(256), gsmem, st, p, tmb);                             \
+    if (e == cudaSuccess) e = launch_k(kern, grid, dim3(352), gsmem, st, p, tmb, tmc);                        \
   } while (0)
 #define MB_TCG_SW(AT_, OT_) \
   do {                      \

@@ -77,15 +77,18 @@ inline bool tmap_bf16_4d(const void* base, int64_t d0, int64_t d1, int64_t d2, i
   return true;
 }
 
-// 2-D uint8 tensor [d1][d0] (row stride d0 bytes, a multiple of 16) with boxes
-// of b0 (= 128) x b1 bytes and the 128-byte swizzle, cached like the 4-D maps.
-inline bool tmap_u8_2d(const void* base, int64_t d0, int64_t d1, int b0, int b1, CUtensorMap* out) {
+// 2-D tensor [d1][d0] of `esize`-byte elements (row stride d0 elements, a
+// multiple of 16 bytes) with boxes of b0 x b1 elements, cached like the 4-D
+// maps; `swz128`: the 128-byte swizzle (b0 * esize must then be 128).
+inline bool tmap_2d(const void* base, CUtensorMapDataType dtype, int esize, int64_t d0, int64_t d1, int b0, int b1,
+                    bool swz128, CUtensorMap* out) {
   static std::mutex mu;
   static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> cache;
   static PFN_cuTensorMapEncodeTiled encode = nullptr;
   TmapKey key{};
   key.addr = reinterpret_cast<uintptr_t>(base);
   key.d0 = d0; key.d1 = d1; key.b0 = b0; key.b1 = b1;
+  key.s1 = esize; key.s2 = (int64_t)dtype; key.s3 = swz128;
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) {
@@ -101,12 +104,13 @@ inline bool tmap_u8_2d(const void* base, int64_t d0, int64_t d1, int b0, int b1,
     encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
   }
   const cuuint64_t dims[2] = {(cuuint64_t)d0, (cuuint64_t)d1};
-  const cuuint64_t strides[1] = {(cuuint64_t)d0};
+  const cuuint64_t strides[1] = {(cuuint64_t)(d0 * esize)};
   const cuuint32_t box[2] = {(cuuint32_t)b0, (cuuint32_t)b1};
   const cuuint32_t estr[2] = {1, 1};
   CUtensorMap m;
-  const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  const CUresult r = encode(&m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            swz128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   if (cache.size() > 4096) cache.clear();
