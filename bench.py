@@ -46,10 +46,12 @@ def _args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--breakdown", action="store_true",
                     help="also time each operator of the decode step in its own CUDA graph (48 layers)")
-    ap.add_argument("--workload", choices=["auto", "bs1", "bs64", "long"], default="auto",
+    ap.add_argument("--workload", choices=["auto", "bs1", "bs64", "long", "attn", "prefill"], default="auto",
                     help="auto: bs64 under torchrun (expert-parallel scaling), else bs1; bs1: configs[2] batch-1 "
                          "decode; bs64: configs[3] batch-64 decode at 8192 cached positions per row; long: "
-                         "configs[4] long-context sampling (FlashHead at batch 1)")
+                         "configs[4] long-context sampling (FlashHead at batch 1); attn: the decode-attention "
+                         "kernels alone (--batch rows x --context positions); prefill: the configs[2] 512-token "
+                         "prompt with and without the tcgen05 expert GEMM, and that GEMM alone")
     ap.add_argument("--context", type=int, default=None,
                     help="cached positions per row (bs64: 8192, long: 65536)")
     ap.add_argument("--batch", type=int, default=1, help="long: rows (1, 16 or 256)")
@@ -217,6 +219,12 @@ def main():
     if args.workload == "long":
         run_long(args)
         return
+    if args.workload == "attn":
+        run_attn(args)
+        return
+    if args.workload == "prefill":
+        run_prefill(args)
+        return
     import torch
 
     from maple_flash_dgx_spark_b200 import _lib
@@ -242,8 +250,16 @@ def main():
     prompt = synthetic_tokens(SEED, PROMPT_LEN, cfg["vocab_size"], dev)
     cache = model.make_cache(max_len=max_len)
     with torch.inference_mode():
+        # time to first token: the 512-token prompt prefilled in one forward
+        model.forward(prompt.reshape(1, -1), cache=model.make_cache(max_len=PROMPT_LEN + 1))  # warm
+        torch.cuda.synchronize(dev)
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record()
         logits = model.forward(prompt.reshape(1, -1), cache=cache)
         first = K.argmax(logits[:, -1, :])
+        p1.record()
+        torch.cuda.synchronize(dev)
+        ttft_ms = p0.elapsed_time(p1)
         graph = DecodeGraph(model, cache, width=1)
         # ---- device-resident timing: next id feeds back on the device ----
         graph.token_ids.copy_(first.reshape(1, 1))
@@ -340,6 +356,9 @@ def main():
         "gpu_launches": Kst * _step_launches(cfg["num_hidden_layers"]),
         "clocks": clocks.summary(),
         "device_errors": device_errors,
+        "prefill": {"prompt_tokens": PROMPT_LEN, "ttft_ms": ttft_ms, "prompt_tok_s": PROMPT_LEN / (ttft_ms / 1000.0),
+                    "note": "one eager forward of the prompt (expert GEMMs on tcgen05 where experts average >= 16 "
+                            "routed slots) plus the first argmax, CUDA events"},
     }
     if device_errors:
         raise SystemExit(f"device error word {device_errors:#x} set during the run: the numbers are not valid")
@@ -765,6 +784,95 @@ def run_long(args):
     if flash:
         line["flash_head"] = flash
     print(json.dumps(line), flush=True)
+
+
+def _event_ms(fn, reps: int) -> float:
+    """Mean CUDA-event time of ``fn`` over ``reps`` calls after one warm call."""
+    import torch
+
+    fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def run_attn(args):
+    """The decode-attention kernels alone: ``--batch`` rows x ``--context``
+    positions of one layer's bf16 cache (seeded random q / K / V, 32 query and
+    4 KV heads of 128 dims), the tensor-core kernel (+ its merge launch) and
+    the canonical CUDA-core kernel, eager launches timed with CUDA events."""
+    import torch
+
+    from maple_flash_dgx_spark_b200 import kernels as K
+
+    dev = torch.device("cuda", 0)
+    rows, ctx, reps = int(args.batch), int(args.context or 8192), max(int(args.steps), 1)
+    Hq, Hkv, D = 32, 4, 128
+    T = ctx + 16
+    g = torch.Generator(device=dev).manual_seed(0)
+    kc = torch.randn(rows, Hkv, T, D, device=dev, generator=g).to(torch.bfloat16)
+    vc = torch.randn(rows, Hkv, T, D, device=dev, generator=g).to(torch.bfloat16)
+    q = torch.randn(rows, Hq, 1, D, device=dev, generator=g).to(torch.bfloat16)
+    sl = torch.full((rows,), ctx - 1, device=dev, dtype=torch.int64)
+    nbytes = rows * Hkv * ctx * D * 2 * 2
+    peak, peak_kind = _peaks()
+    out = {"workload": f"decode attention alone, {rows} rows x {ctx} positions, bf16 cache", "algorithmic_bytes": nbytes}
+    for tc in (True, False):
+        us = _event_ms(lambda: K.decode_gqa_attn(q, kc, vc, sl, scale=D ** -0.5, window=None, split_len=128,
+                                                 tensor_cores=tc), reps) * 1000.0
+        out["tensor_cores" if tc else "cuda_cores"] = {"us_per_launch": us, "gbs": nbytes / us / 1e3,
+                                                       "frac": nbytes / us / 1e3 / peak}
+    out["peak_gbs"] = peak
+    out["peak_kind"] = f"{peak_kind} hbm_gbs"
+    print(json.dumps(out), flush=True)
+
+
+def run_prefill(args):
+    """Prompt prefill of the configs[2] model (``--layers`` layers, 512-token
+    prompt) with the tcgen05 grouped expert GEMM and with the mma.sync one
+    (time to first token, CUDA events), plus the grouped expert SwiGLU GEMM
+    alone at prefill routing (512 tokens x top-8 over 64 experts, seeded
+    random codes)."""
+    import torch
+
+    from maple_flash_dgx_spark_b200 import kernels as K
+    from maple_flash_dgx_spark_b200.model import MapleForCausalLM
+    from maple_flash_dgx_spark_b200.synth import synthetic_config, synthetic_tokens, synthetic_weights
+
+    dev = torch.device("cuda", 0)
+    reps = max(int(args.steps), 1)
+    g = torch.Generator(device=dev).manual_seed(0)
+    T, E, k, H, I = PROMPT_LEN, 64, 8, 2048, 1024
+    x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    ug = (torch.randint(0, 2 ** 31, (E, 2 * I, H // 16), device=dev, generator=g, dtype=torch.int64)
+          .to(torch.int32) & 0x55555555).view(torch.uint32)  # codes 0/1 (every 2-bit field < 3)
+    ua = (torch.rand(E, 2 * I, device=dev, generator=g) * 0.02 + 1e-3).to(torch.bfloat16)
+    ids = torch.stack([torch.randperm(E, device=dev, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    plan = K.moe_plan(ids, E)
+    out = {"workload": f"configs[2] {PROMPT_LEN}-token prefill, {args.layers} layers; grouped SwiGLU at "
+                       f"{T} tokens x top-{k} over {E} experts"}
+    default = K.TC_GEMM_MIN_SLOTS
+    try:
+        for tc in (True, False):
+            K.TC_GEMM_MIN_SLOTS = 0 if tc else 10 ** 9
+            out[f"grouped_swiglu_us_{'tcgen05' if tc else 'mma_sync'}"] = _event_ms(
+                lambda: K.ternary_expert_swiglu(x, ug, ua, ids, plan=plan), reps) * 1000.0
+        if args.layers > 0:
+            cfg = synthetic_config(num_layers=args.layers)
+            model = MapleForCausalLM.from_weight_dict(cfg, synthetic_weights(cfg, SEED, dev), device=dev)
+            prompt = synthetic_tokens(SEED, PROMPT_LEN, cfg["vocab_size"], dev).reshape(1, -1)
+            for tc in (True, False):
+                K.TC_GEMM_MIN_SLOTS = 0 if tc else 10 ** 9
+                ms = _event_ms(lambda: model.forward(prompt, cache=model.make_cache(max_len=PROMPT_LEN + 8)), reps)
+                out[f"ttft_ms_{'tcgen05' if tc else 'mma_sync'}"] = ms
+    finally:
+        K.TC_GEMM_MIN_SLOTS = default
+    print(json.dumps(out), flush=True)
 
 
 def swiglu_roofline(model, prompt, dev):
