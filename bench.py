@@ -44,6 +44,8 @@ def _args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-bs64", action="store_true",
+                    help="bs1 on one GPU: skip the batch-64 point measured after the batch-1 line")
     ap.add_argument("--breakdown", action="store_true",
                     help="also time each operator of the decode step in its own CUDA graph (48 layers)")
     ap.add_argument("--workload", choices=["auto", "bs1", "bs64", "long", "attn", "prefill"], default="auto",
@@ -165,20 +167,37 @@ def cpu_baseline(cfg, n_tokens: int = 3):
 def run_reference(args):
     """--impl reference: the reference's decode restated on the CPU (the
     oracle port: the reference has no CPU kernels, its Triton kernels need a
-    GPU), timed on the host cores; rank 0 only.  The sample is the bs1 decode
-    of the 48-layer model over a random-filled 512-position cache (no prompt
-    prefill: a CPU prefill of 512 tokens would take minutes), attention split
-    32; per-token work is the same as the engine's bs1 step."""
+    GPU), timed on the host cores; rank 0 only, on the workload our arm runs
+    with the same arguments (bs1 by default, bs64 under torchrun).  bs1: a
+    step is one decode token of the 48-layer model over a random-filled
+    512-position cache (no prompt prefill: a CPU prefill of 512 tokens takes
+    minutes).  bs64: a step is one row's decode token at 8192 random cached
+    positions (the 64 rows are independent; the CPU port decodes row by row),
+    so the value is rows decoded per second.  Each run is capped at about
+    90 s of decode."""
     world, rank, _ = _dist()
     if rank != 0:
         return
     from maple_flash_dgx_spark_b200.synth import synthetic_config
 
+    workload = args.workload
+    if workload == "auto":
+        workload = "bs64" if "WORLD_SIZE" in os.environ else "bs1"
     cfg = synthetic_config(num_layers=args.layers)
     import oracle.model as om
 
-    m = om.OracleModel(cfg, SEED, max_len=PROMPT_LEN + args.warmup + args.steps + 8, split_len=32)
-    m.fill_cache(SEED, PROMPT_LEN)
+    if workload == "bs64":
+        ctx = int(args.context or 8192)
+        metric, config = "decode tok/s (bs64, configs[3])", bs64_config(cfg, world, ctx, args.warmup, args.steps)
+        scaling = "strong"
+    else:
+        ctx = PROMPT_LEN
+        metric, config = "decode tok/s (bs1, configs[2])", bs1_config(cfg, world)
+        scaling = "weak"
+    t_build = time.time()
+    m = om.OracleModel(cfg, SEED, max_len=ctx + args.warmup + args.steps + 8, split_len=32 if ctx <= 512 else 256)
+    m.fill_cache(SEED, ctx)
+    build_s = time.time() - t_build
     tok = 1
     for _ in range(max(1, min(args.warmup, 2))):
         tok = m.step(tok)
@@ -192,16 +211,17 @@ def run_reference(args):
     dt = time.time() - t0
     v = n / dt
     cores = os.cpu_count()
+    what = (f"{n} row decode tokens at {ctx} random cached positions (rows of the batch are independent)"
+            if workload == "bs64" else f"{n} decode tokens over a random-filled {ctx}-position cache")
     print(json.dumps({
-        "impl": "reference", "metric": "decode tok/s (bs1, configs[2])", "value": v, "unit": "tok/s",
+        "impl": "reference", "metric": metric, "value": v, "unit": "tok/s",
         "n_gpus": world, "steps": n, "warmup": args.warmup, "ms_per_step": 1000 * dt / n, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "configs[2] architecture: 48-layer ternary MoE, bs1 greedy decode at context 512 "
-                               "(CPU oracle port; cache random-filled, no prefill, attention split 32)",
-                   "global_batch": 1, "seq_len": PROMPT_LEN, "parallelism": "single"},
+        "scaling": scaling, "vs_baseline": None, "dtype": "bf16", "data": SYNTH_DATA,
+        "config": config,
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
-                         "sample": f"{n} decode tokens (cap {budget_s:.0f}s) of the CPU oracle port on {cores} "
-                                   "OpenMP threads, random-filled 512-position cache"},
+                         "sample": f"{what} of the {cfg['num_hidden_layers']}-layer model: the CPU oracle port on "
+                                   f"{cores} OpenMP threads, attention split {m.P}, cap {budget_s:.0f} s "
+                                   f"(model build and cache fill {build_s:.0f} s untimed)"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -225,6 +245,31 @@ def main():
     if args.workload == "prefill":
         run_prefill(args)
         return
+    line = run_bs1(args)
+    world, rank, _ = _dist()
+    if line is None:
+        return
+    if world == 1 and not args.no_bs64:
+        # the batch-64 point of the same single-GPU run (configs[3] on one GPU),
+        # so a 1..N scaling series has its one-GPU batch-64 number
+        import gc
+
+        import torch
+
+        gc.collect()
+        torch.cuda.empty_cache()
+        sub = argparse.Namespace(**vars(args))
+        sub.steps, sub.warmup, sub.context = min(args.steps, 64), max(3, min(args.warmup, 5)), None
+        b64 = run_bs64(sub, emit=False)
+        line["bs64"] = {k: b64.get(k) for k in ("metric", "value", "unit", "ms_per_step", "steps", "warmup",
+                                                 "scaling", "config", "e2e", "roofline", "hbm_roofline_step",
+                                                 "gpu_launches", "clocks", "device_errors", "phases_ms_per_step")}
+    print(json.dumps(line), flush=True)
+
+
+def run_bs1(args):
+    """batch-1 greedy decode after a 512-token prompt.  Returns
+    the JSON line on rank 0 (None elsewhere)."""
     import torch
 
     from maple_flash_dgx_spark_b200 import _lib
@@ -260,7 +305,8 @@ def main():
         p1.record()
         torch.cuda.synchronize(dev)
         ttft_ms = p0.elapsed_time(p1)
-        graph = DecodeGraph(model, cache, width=1)
+        graph = DecodeGraph(model, cache, width=1, keep_graph=True)
+        launches_per_step = graph_kernel_launches(graph.graph)
         # ---- device-resident timing: next id feeds back on the device ----
         graph.token_ids.copy_(first.reshape(1, 1))
         nxt = graph.next_id
@@ -341,11 +387,8 @@ def main():
         "vs_baseline": None,
         "dtype": "bf16",
         "data": SYNTH_DATA + "; 512 random prompt ids",
-        "config": {"workload": "configs[2]: 48-layer ternary MoE, bs1 greedy decode after a 512-token prompt",
-                   "global_batch": world, "seq_len": PROMPT_LEN, "context": [ctx0, ctx0 + Kst],
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "l2": f"{step_bytes / 1e9:.2f} GB of weights and K/V streamed per step (> 126 MB L2), "
-                         "no flush needed"},
+        "config": bs1_config(cfg, world),
+        "context": [ctx0, ctx0 + Kst],
         "hbm_roofline_step": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes * (Kst / (ms / 1000.0)) / 1e9,
                               "peak_gbs": peak, "frac": step_bytes * (Kst / (ms / 1000.0)) / 1e9 / peak},
         "roofline": {"kernel": "tgemv2_kernel<swiglu> (expert up|gate + SwiGLU, bs1)", "bound": "hbm",
@@ -353,7 +396,9 @@ def main():
                      "frac": swiglu_bytes / (launch_us * 1e-6) / 1e9 / peak, "traffic": traffic,
                      "algorithmic_bytes": swiglu_bytes, "launch_us": launch_us, "peak_kind": f"{peak_kind} hbm_gbs"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
-        "gpu_launches": Kst * _step_launches(cfg["num_hidden_layers"]),
+        "gpu_launches": Kst * (launches_per_step or _step_launches(cfg["num_hidden_layers"])),
+        "gpu_launches_source": ("kernel nodes of this library in the captured decode graph x steps"
+                                if launches_per_step else "estimate"),
         "clocks": clocks.summary(),
         "device_errors": device_errors,
         "prefill": {"prompt_tokens": PROMPT_LEN, "ttft_ms": ttft_ms, "prompt_tok_s": PROMPT_LEN / (ttft_ms / 1000.0),
@@ -367,11 +412,84 @@ def main():
     if rank == 0 and not args.no_cpu_baseline:
         v, cores, sample = cpu_baseline(cfg)
         line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     if world > 1:
         del graph, g2
         dist.destroy_process_group()
+    return line if rank == 0 else None
+
+
+def bs1_config(cfg, world: int) -> dict:
+    """The bs1 workload description (both arms): configs[2] at context 512."""
+    from maple_flash_dgx_spark_b200.model import kv_bytes_per_token, packed_decode_bytes
+
+    step = packed_decode_bytes(cfg)["packed_weight_bytes"] + kv_bytes_per_token(cfg, PROMPT_LEN)
+    return {"workload": f"configs[2]: {cfg['num_hidden_layers']}-layer ternary MoE, bs1 greedy decode after a "
+                        f"{PROMPT_LEN}-token prompt",
+            "global_batch": world, "seq_len": PROMPT_LEN,
+            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "l2": f"{step / 1e9:.2f} GB of weights and K/V streamed per step (> 126 MB L2), no flush needed"}
+
+
+BS64_ROWS = 64
+
+
+def bs64_step_bytes(cfg, world: int, ctx: int) -> int:
+    """HBM bytes one GPU streams per configs[3] step at ``ctx`` cached
+    positions: replicated attention / router / norm weights, 1/world of the
+    experts and of the head, the K/V of its 64/world rows."""
+    from maple_flash_dgx_spark_b200.model import packed_decode_bytes
+
+    wb = packed_decode_bytes(cfg)
+    experts_all = cfg["num_hidden_layers"] * cfg["num_experts"] * (
+        (2 * cfg["moe_intermediate_size"] * cfg["hidden_size"] + cfg["hidden_size"] * cfg["moe_intermediate_size"])
+        // 4 + (2 * cfg["moe_intermediate_size"] + cfg["hidden_size"]) * 2)
+    rep = wb["packed_weight_bytes"] - wb["expert_bytes"] - wb["head_bytes"]
+    weights_gpu = rep + (experts_all + wb["head_bytes"]) // world
+    kv_gpu = (BS64_ROWS // world) * cfg["num_hidden_layers"] * cfg["num_key_value_heads"] * cfg["head_dim"] * 4 * ctx
+    return int(weights_gpu + kv_gpu)
+
+
+def bs64_config(cfg, world: int, ctx: int, warmup: int, steps: int) -> dict:
+    """The bs64 workload description (both arms)."""
+    step = bs64_step_bytes(cfg, world, ctx + warmup + steps // 2)
+    return {"workload": f"configs[3]: bs{BS64_ROWS} greedy decode, {ctx} cached positions per row",
+            "global_batch": BS64_ROWS, "seq_len": ctx,
+            "parallelism": f"ep{world}+dp-attention{world}" if world > 1 else "single",
+            "l2": f"{step / 1e9:.1f} GB streamed per GPU per step (> 126 MB L2), no flush needed"}
+
+
+def graph_kernel_launches(graph):
+    """Kernel nodes of a captured CUDA graph (``keep_graph=True``) whose
+    function belongs to this package's library (C++ namespace ``mb``, mangled
+    ``_ZN2mb``): this library's launches per replay, torch's and NCCL's
+    kernels excluded.  None when the graph cannot be inspected."""
+    try:
+        from cuda.bindings import driver as drv
+        from cuda.bindings import runtime as rt
+
+        g = rt.cudaGraph_t(init_value=int(graph.raw_cuda_graph()))
+        err, _, n = rt.cudaGraphGetNodes(g, 0)
+        if err != rt.cudaError_t.cudaSuccess:
+            return None
+        err, nodes, n = rt.cudaGraphGetNodes(g, n)
+        if err != rt.cudaError_t.cudaSuccess:
+            return None
+        count = 0
+        for nd in nodes[:n]:
+            err, kind = rt.cudaGraphNodeGetType(nd)
+            if err != rt.cudaError_t.cudaSuccess or kind != rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+                continue
+            err, prm = drv.cuGraphKernelNodeGetParams(drv.CUgraphNode(init_value=int(nd)))
+            if err != drv.CUresult.CUDA_SUCCESS:
+                return None
+            err, name = drv.cuFuncGetName(prm.func)
+            if err != drv.CUresult.CUDA_SUCCESS:
+                return None
+            if bytes(name).startswith(b"_ZN2mb"):
+                count += 1
+        return count or None
+    except Exception:
+        return None
 
 
 def _time_graph(fns, dev, reps=5):
@@ -400,13 +518,14 @@ def _time_graph(fns, dev, reps=5):
     return a.elapsed_time(b) / reps
 
 
-def run_bs64(args):
+def run_bs64(args, emit: bool = True):
     """64 independent sequences, each with ``--context`` random
     cached positions (bf16 N(0,1) K/V written directly), one new token per row
     per step, greedy.  One GPU: batched decode.  N GPUs (torchrun): expert
     parallelism -- each rank holds 64/N sequences (data-parallel attention),
     64/N experts and 1/N of the vocabulary; NCCL all-gather (dispatch) and
-    all-to-all (combine) per MoE layer, candidate all-gather for the head."""
+    all-to-all (combine) per MoE layer, candidate all-gather for the head.
+    Returns the JSON line (printed on rank 0 when ``emit``)."""
     import datetime
 
     import torch
@@ -428,7 +547,7 @@ def run_bs64(args):
     else:
         dist.init_process_group("nccl", store=dist.HashStore(), rank=0, world_size=1,
                                 timeout=datetime.timedelta(seconds=300), device_id=dev)
-    B, ctx = 64, int(args.context or 8192)
+    B, ctx = BS64_ROWS, int(args.context or 8192)
     cfg = synthetic_config(num_layers=args.layers)
     W, Kst = args.warmup, args.steps
     weights = synthetic_weights(cfg, SEED, dev)
@@ -461,10 +580,12 @@ def run_bs64(args):
 
         holder = {}  # the only references to captured graphs (freed before the group is destroyed)
         ex = None
+        launches_per_step = None
         if world > 1:
             ex, dec = make_decoder()
             try:
-                holder["g"] = EPDecodeGraph(dec, cache, T)
+                holder["g"] = EPDecodeGraph(dec, cache, T, keep_graph=True)
+                launches_per_step = graph_kernel_launches(holder["g"].graph)
                 ids_buf = holder["g"].token_ids
 
                 def step(tok=None):
@@ -482,7 +603,8 @@ def run_bs64(args):
 
                 nxt_of = lambda: state["n"]  # noqa: E731
         else:
-            g = DecodeGraph(model, cache, width=T)
+            g = DecodeGraph(model, cache, width=T, keep_graph=True)
+            launches_per_step = graph_kernel_launches(g.graph)
             ids_buf = g.token_ids
             nxt_of = lambda: g.next_id  # noqa: E731
 
@@ -576,27 +698,16 @@ def run_bs64(args):
         att_us = _time_graph(fns, dev) * 1000.0 / len(fns)
         kv_per_launch = T * model.num_kv_heads * model.head_dim * 2 * 2 * (ctx0 + 1)
     peak, peak_kind = _peaks()
-    wb = packed_decode_bytes(cfg)
-    experts_all = cfg["num_hidden_layers"] * cfg["num_experts"] * (
-        (2 * cfg["moe_intermediate_size"] * cfg["hidden_size"] + cfg["hidden_size"] * cfg["moe_intermediate_size"])
-        // 4 + (2 * cfg["moe_intermediate_size"] + cfg["hidden_size"]) * 2)
-    # per GPU: replicated attention/router/norm weights, 1/N of experts and head, 1/N of the KV rows
-    rep = wb["packed_weight_bytes"] - wb["expert_bytes"] - wb["head_bytes"]
-    weights_gpu = rep + (experts_all + wb["head_bytes"]) // world
-    ctx_mid = ctx0 + Kst // 2
-    kv_gpu = T * cfg["num_hidden_layers"] * cfg["num_key_value_heads"] * cfg["head_dim"] * 2 * 2 * ctx_mid
-    step_bytes = weights_gpu + kv_gpu
+    step_bytes = bs64_step_bytes(cfg, world, ctx0 + Kst // 2)
     sec = ms / Kst / 1000.0
     line = {
         "metric": "decode tok/s (bs64, configs[3])", "value": tok_s, "unit": "tok/s", "n_gpus": world,
         "steps": Kst, "warmup": W, "ms_per_step": ms / Kst, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16",
         "data": SYNTH_DATA + "; cached K/V bf16 from the same generator (N(0,1) stand-in)",
-        "config": {"workload": f"configs[3]: bs64 greedy decode, {ctx} cached positions per row", "global_batch": B,
-                   "seq_len": ctx, "context": [ctx0, ctx0 + Kst],
-                   "parallelism": f"ep{world}+dp-attention{world}" if world > 1 else "single", "step": graph_kind,
-                   "ep_transport": os.environ.get("MAPLE_EP_TRANSPORT", "p2p") if world > 1 else None,
-                   "l2": f"{step_bytes / 1e9:.1f} GB streamed per GPU per step (> 126 MB L2), no flush needed"},
+        "config": bs64_config(cfg, world, ctx, W, Kst),
+        "context": [ctx0, ctx0 + Kst], "step": graph_kind,
+        "ep_transport": os.environ.get("MAPLE_EP_TRANSPORT", "p2p") if world > 1 else None,
         "hbm_roofline_step": {"bytes_per_gpu_step": step_bytes, "achieved_gbs": step_bytes / sec / 1e9,
                               "peak_gbs": peak, "frac": step_bytes / sec / 1e9 / peak},
         "roofline": {"kernel": _attn_kernel_name(cache, T, ctx), "bound": "hbm",
@@ -604,14 +715,16 @@ def run_bs64(args):
                      "frac": kv_per_launch / (att_us * 1e-6) / 1e9 / peak, "traffic": None,
                      "algorithmic_bytes": kv_per_launch, "launch_us": att_us, "peak_kind": f"{peak_kind} hbm_gbs"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * T, "d2h_bytes_per_step": 8 * T},
-        "gpu_launches": Kst * ((12 + _attn_launches(cache)) * cfg["num_hidden_layers"] + 4),
+        "gpu_launches": Kst * (launches_per_step or (12 + _attn_launches(cache)) * cfg["num_hidden_layers"] + 4),
+        "gpu_launches_source": ("kernel nodes of this library in the captured step graph x steps"
+                                if launches_per_step else "estimate"),
         "clocks": clocks.summary(),
         "device_errors": device_errors,
         "phases_ms_per_step": phases,
         "phases_note": "expert-parallel step captured with timing events at phase boundaries (max over ranks, "
                        "summed over 48 layers; at one GPU the same step with a one-rank exchange)",
     }
-    if rank == 0:
+    if rank == 0 and emit:
         print(json.dumps(line), flush=True)
     # a CUDA graph holding NCCL calls must be released before the group goes
     import gc
@@ -626,6 +739,7 @@ def run_bs64(args):
     dist.destroy_process_group()
     if device_errors:
         raise SystemExit(f"device error word {device_errors:#x} set during the run: the numbers are not valid")
+    return line
 
 
 def run_long(args):

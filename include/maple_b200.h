@@ -116,27 +116,34 @@ int maple_ep_combine(const void* recv, int x_dtype, int64_t world, int64_t token
 
 /* Expert-parallel exchange over NVLink peer memory (no reference
  * counterpart; replaces the NCCL all-gather / all-to-all of the EP layer).
- * peer_bases[r] is rank r's symmetric buffer (same size and layout on every
- * rank, mapped here through CUDA IPC; peer_bases[rank] is this rank's own),
- * zero-filled before first use; off_recv / off_flags locate the receive area
- * and the maple_p2p_flag_bytes() flag area in it.  seq / ticket: this rank's
- * device counters for the call type (one pair per call type, zeroed once).
- * Waits for the peers are bounded; a wait that gives up sets bit 1 of *err.
+ * Data travel as tagged words (every 8 data bytes in one 16-byte store with
+ * the call's sequence number twice), polled by the receiver: no fences or
+ * flags.  peer_bases[r] is rank r's symmetric buffer (same size and layout on
+ * every rank, mapped here through CUDA IPC; peer_bases[rank] is this rank's
+ * own), zero-filled before first use; off_ll locates the call type's area
+ * (maple_p2p_dispatch_bytes / maple_p2p_combine_bytes long).  seq / ticket:
+ * this rank's device counters for the call type (one pair per call type,
+ * zeroed once).  Polls are bounded; one that gives up sets bit 1 of *err.
  *
- * maple_p2p_allgather: bytes_per_rank (multiple of 16) from src land at
- * recv + rank * bytes_per_rank on every rank.
- * maple_p2p_combine: the slot rows y[s] (s < world*T*topk, rows of all ranks'
- * tokens) of this rank's experts go to the owning rank's recv area; then
- * out[t] = sum_j w_mine[t,j] * row(owner(e_tj), t*topk+j) (+ residual) for
- * this rank's T tokens, in moe_reduce_add's order. */
-int64_t maple_p2p_flag_bytes(void);
-int maple_p2p_allgather(void* const* peer_bases, int world, int rank, int64_t off_recv, int64_t off_flags,
-                        const void* src, int64_t bytes_per_rank, unsigned* seq, unsigned* ticket, int* err,
-                        void* stream);
-int maple_p2p_combine(void* const* peer_bases, int world, int rank, int64_t off_recv, int64_t off_flags, const void* y,
-                      int x_dtype, const int32_t* ids_all, int64_t tokens_per_rank, int64_t topk, int64_t n,
-                      int64_t n_experts, const int32_t* ids_mine, const float* w_mine, const void* residual, void* out,
-                      unsigned* seq, unsigned* ticket, int* err, void* stream);
+ * maple_p2p_dispatch: this rank's tokens_per_rank rows of x (n elements,
+ * row stride x_row_stride) and their top-k expert ids (int32 [T, topk]) go to
+ * every rank; every rank's rows land in rows_out [world*T][n] (dense, this
+ * GPU's memory, rank order) and their ids in ids_out [world*T][topk].
+ * maple_p2p_combine (topk <= 8): y[s] (rows by slot of the gathered tokens)
+ * for the slots this rank's expert plan lists (moe_plan over the gathered
+ * ids restricted to this rank's n_local_experts) go to the owning rank; then
+ * out[t] = sum_j w[t,j] * row(t*topk + j) (+ residual) for this rank's T
+ * tokens, in moe_reduce_add's order. */
+int64_t maple_p2p_dispatch_bytes(int64_t world, int64_t tokens_per_rank, int64_t n, int x_dtype, int64_t topk);
+int64_t maple_p2p_combine_bytes(int64_t tokens_per_rank, int64_t topk, int64_t n, int x_dtype);
+int maple_p2p_dispatch(void* const* peer_bases, int world, int rank, int64_t off_ll, const void* x, int x_dtype,
+                       int64_t x_row_stride, int64_t tokens_per_rank, int64_t n, const int32_t* expert_ids,
+                       int64_t topk, void* rows_out, int32_t* ids_out, unsigned* seq, unsigned* ticket, int* err,
+                       void* stream);
+int maple_p2p_combine(void* const* peer_bases, int world, int rank, int64_t off_ll, const void* y, int x_dtype,
+                      const int32_t* plan_offsets, const uint32_t* plan_slots, int64_t n_local_experts,
+                      int64_t tokens_per_rank, int64_t topk, int64_t n, const float* topk_weight,
+                      const void* residual, void* out, unsigned* seq, unsigned* ticket, int* err, void* stream);
 
 /* Grouped expert GEMM on the tcgen05 tensor cores (accumulators in tensor
  * memory), for experts with many routed slots (prompt prefill, large batches):

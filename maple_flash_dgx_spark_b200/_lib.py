@@ -55,10 +55,11 @@ _SIGS: dict[str, tuple] = {
     "maple_moe_plan": (i32, [vp, i64, i64, vp, vp, vp]),
     "maple_moe_plan_range": (i32, [vp, i64, i64, i64, i64, vp, vp, vp]),
     "maple_ep_combine": (i32, [vp, i32, i64, i64, i64, i64, vp, vp, i64, vp, vp, vp]),
-    "maple_p2p_flag_bytes": (i64, []),
-    "maple_p2p_allgather": (i32, [vp, i32, i32, i64, i64, vp, i64, vp, vp, vp, vp]),
-    "maple_p2p_combine": (i32, [vp, i32, i32, i64, i64, vp, i32, vp, i64, i64, i64, i64, vp, vp, vp, vp, vp, vp,
-                                vp, vp]),
+    "maple_p2p_dispatch_bytes": (i64, [i64, i64, i64, i32, i64]),
+    "maple_p2p_combine_bytes": (i64, [i64, i64, i64, i32]),
+    "maple_p2p_dispatch": (i32, [vp, i32, i32, i64, vp, i32, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp, vp]),
+    "maple_p2p_combine": (i32, [vp, i32, i32, i64, vp, i32, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp, vp, vp,
+                                vp]),
     "maple_ternary_grouped_gemm": (i32, [vp, vp, i64, i64, vp, i64, i64, vp, i32, vp, vp, i64, i64, i32, i32, vp,
                                          i32, i64, vp, vp]),
     "maple_ternary_grouped_gemm_tc_workspace_bytes": (i64, [i64, i64]),
@@ -199,11 +200,13 @@ _errors: dict[int, torch.Tensor] = {}
 
 def error_word(device: torch.device) -> torch.Tensor:
     """Per-device int32 error word that kernels OR flags into (1: a bounded
-    wait timed out, 2: an index or position was out of range)."""
+    wait timed out, 2: an index or position was out of range).  Allocated
+    outside inference mode, so it can be cleared in place from either mode."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     e = _errors.get(idx)
     if e is None:
-        e = _errors[idx] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        with torch.inference_mode(False):
+            e = _errors[idx] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
     return e
 
 

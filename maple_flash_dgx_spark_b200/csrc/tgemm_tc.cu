@@ -28,7 +28,7 @@
 //
 // Every wait is bounded: a wait that gives up sets bit 1 of the error word,
 // waits (bounded) for the CTA's copies and MMAs in flight, frees its tensor
-// memory and returns.  TMA loads are plain (no cluster multicast).
+// memory and returns.  Each CTA loads its own tiles from this GPU's memory.
 #include "bulk.cuh"
 #include "fxa.cuh"
 #include "launch.cuh"

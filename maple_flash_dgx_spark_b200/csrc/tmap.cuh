@@ -5,7 +5,7 @@
 // tensor's address and geometry so repeated launches over the same buffers
 // (every decode step, every layer) encode each map once.  Device side: the
 // 4-D tiled load into shared memory completing on an mbarrier.  Loads only,
-// from this GPU's own memory, never with cluster multicast.
+// from this GPU's own memory, each CTA fetching its own tiles.
 #pragma once
 
 #include <cuda.h>

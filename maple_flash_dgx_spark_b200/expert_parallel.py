@@ -214,29 +214,28 @@ def _round256(n: int) -> int:
 
 
 class EPExchangeP2P(EPExchange):
-    """EPExchange over NVLink peer memory: ``dispatch`` is a peer-store
-    all-gather kernel and ``combine`` sends each rank's expert rows to the
-    token owners and sums them in the same kernel (``maple_p2p_*``).  Buffers
-    are sized for ``tokens`` rows per rank, fixed for the object's life."""
+    """EPExchange over NVLink peer memory (``maple_p2p_*``): ``dispatch``
+    sends this rank's routed rows and top-k ids to every rank as tagged words
+    and gathers every rank's into dense local buffers; ``combine`` sends each
+    row its experts computed to the token's owner and sums the slots in the
+    same kernel.  Buffers are sized for ``tokens`` rows per rank, fixed for
+    the object's life."""
 
     def __init__(self, group, rank: int, world: int, n_experts: int, *, tokens: int, hidden: int, topk: int,
                  device: torch.device, dtype=torch.bfloat16):
         super().__init__(group, rank, world, n_experts)
         self.tokens, self.hidden, self.topk, self.dtype = tokens, hidden, topk, dtype
-        es = torch.tensor([], dtype=dtype).element_size()
-        self.hb = hidden * es
-        self.rowbytes = (self.hb + 4 * topk + 15) // 16 * 16
-        self.off_disp = 0
-        self.off_comb = _round256(world * tokens * self.rowbytes)
-        self.off_flags = self.off_comb + _round256(world * tokens * topk * hidden * es)
-        total = self.off_flags + _round256(lib().maple_p2p_flag_bytes())
+        code = _lib._DTYPE[dtype]
+        L = lib()
+        self.off_dispatch = 0
+        self.off_combine = _round256(L.maple_p2p_dispatch_bytes(world, tokens, hidden, code, topk))
+        total = self.off_combine + _round256(L.maple_p2p_combine_bytes(tokens, topk, hidden, code))
         self.buf = SymmetricBuffer(total, group, rank, world, device)
-        self.recv = self.buf.view(self.off_disp, world * tokens * self.rowbytes).view(world * tokens, self.rowbytes)
-        self.send = torch.zeros(tokens, self.rowbytes, dtype=torch.uint8, device=device)
+        self.rows_all = torch.empty(world * tokens, hidden, dtype=dtype, device=device)
+        self.ids_all = torch.empty(world * tokens, topk, dtype=torch.int32, device=device)
         self.state = torch.zeros(4, dtype=torch.int32, device=device)  # seq/ticket of dispatch, then of combine
         self.err = _lib.error_word(device)
         self.device = device
-        self.ids_all = None
 
     def _state(self, i):
         return self.state.data_ptr() + 4 * i
@@ -244,28 +243,30 @@ class EPExchangeP2P(EPExchange):
     def dispatch(self, hidden: torch.Tensor, idx: torch.Tensor):
         T, H = hidden.shape
         k = idx.shape[1]
-        if T != self.tokens or H != self.hidden or k != self.topk:
-            raise ValueError(f"EPExchangeP2P sized for {self.tokens}x{self.hidden} top-{self.topk}, got {T}x{H} "
-                             f"top-{k}.")
-        self.send[:, :self.hb].copy_(hidden.contiguous().view(torch.uint8).reshape(T, self.hb))
-        self.send[:, self.hb:self.hb + 4 * k].copy_(idx.to(torch.int32).contiguous().view(torch.uint8)
-                                                    .reshape(T, 4 * k))
-        check(lib().maple_p2p_allgather(self.buf.bases, self.world, self.rank, self.off_disp, self.off_flags,
-                                        ptr(self.send), T * self.rowbytes, self._state(0), self._state(1),
-                                        ptr(self.err), stream_ptr(self.device)), "p2p_dispatch")
-        x_all = self.recv[:, :self.hb].view(hidden.dtype)
-        self.ids_all = self.recv[:, self.hb:self.hb + 4 * k].contiguous().view(torch.int32)
-        return x_all, self.ids_all
-
-    def combine(self, y_all: torch.Tensor, idx: torch.Tensor, wt: torch.Tensor, residual=None) -> torch.Tensor:
-        y = y_all.reshape(-1, self.hidden).contiguous()
-        out = torch.empty(self.tokens, self.hidden, dtype=y.dtype, device=y.device)
+        if T != self.tokens or H != self.hidden or k != self.topk or hidden.dtype != self.dtype:
+            raise ValueError(f"EPExchangeP2P sized for {self.tokens}x{self.hidden} {self.dtype} top-{self.topk}, got "
+                             f"{T}x{H} {hidden.dtype} top-{k}.")
+        x = hidden if hidden.stride(1) == 1 else hidden.contiguous()
         ids = idx.to(torch.int32).contiguous()
+        check(lib().maple_p2p_dispatch(self.buf.bases, self.world, self.rank, self.off_dispatch, ptr(x),
+                                       dtype_code(x, "p2p_dispatch"), x.stride(0), T, H, ptr(ids), k,
+                                       ptr(self.rows_all), ptr(self.ids_all), self._state(0), self._state(1),
+                                       ptr(self.err), stream_ptr(self.device)), "p2p_dispatch")
+        return self.rows_all, self.ids_all
+
+    def combine(self, y_all: torch.Tensor, plan, wt: torch.Tensor, residual=None) -> torch.Tensor:
+        """``y_all``: rows by slot of the gathered tokens (this rank's experts'
+        slots filled, as listed by ``plan``); returns this rank's MoE output
+        rows (+ ``residual``)."""
+        y = y_all.reshape(-1, self.hidden)
+        if not y.is_contiguous():
+            y = y.contiguous()
+        out = torch.empty(self.tokens, self.hidden, dtype=y.dtype, device=y.device)
         w = wt.float().contiguous()
         res = residual.reshape(self.tokens, self.hidden).contiguous() if residual is not None else None
-        check(lib().maple_p2p_combine(self.buf.bases, self.world, self.rank, self.off_comb, self.off_flags, ptr(y),
-                                      dtype_code(y, "p2p_combine"), ptr(self.ids_all), self.tokens, self.topk,
-                                      self.hidden, self.n_experts, ptr(ids), ptr(w), ptr(res), ptr(out),
+        check(lib().maple_p2p_combine(self.buf.bases, self.world, self.rank, self.off_combine, ptr(y),
+                                      dtype_code(y, "p2p_combine"), ptr(plan.offsets), ptr(plan.slots),
+                                      plan.n_experts, self.tokens, self.topk, self.hidden, ptr(w), ptr(res), ptr(out),
                                       self._state(2), self._state(3), ptr(self.err), stream_ptr(self.device)),
               "p2p_combine")
         return out
@@ -297,7 +298,7 @@ class EPMoeBlock:
         y = ternary_expert_gemv(h, b.down.packed_weight, b.down.row_alpha, ids_all, plan=plan)
         self._mark("experts")
         if isinstance(self.ex, EPExchangeP2P):
-            out = self.ex.combine(y, idx, wt, residual)
+            out = self.ex.combine(y, plan, wt, residual)
         else:
             recv = self.ex.combine_exchange(y.reshape(-1, y.shape[-1]))
             out = ep_combine(recv, idx, wt, self.ex.n_experts, residual)
@@ -390,7 +391,7 @@ class EPDecoder:
 class EPDecodeGraph:
     """``EPDecoder.step`` captured in a CUDA graph (collectives included)."""
 
-    def __init__(self, decoder: EPDecoder, cache, rows: int, warmup: int = 3):
+    def __init__(self, decoder: EPDecoder, cache, rows: int, warmup: int = 3, keep_graph: bool = False):
         dev = decoder.model.device
         self.token_ids = torch.zeros(rows, 1, dtype=torch.long, device=dev)
         snap = (cache.seqlen.clone(), list(cache.seen))
@@ -401,7 +402,7 @@ class EPDecodeGraph:
                 decoder.step(self.token_ids, cache)
                 cache.seqlen.copy_(snap[0])
                 cache.seen = list(snap[1])
-            self.graph = torch.cuda.CUDAGraph()
+            self.graph = torch.cuda.CUDAGraph(keep_graph=keep_graph)
             with torch.cuda.graph(self.graph, stream=st):
                 self.next_id = decoder.step(self.token_ids, cache)
         torch.cuda.current_stream(dev).wait_stream(st)

@@ -109,10 +109,11 @@ class DecodeGraph:
     (the first ``width`` entries are this graph's inputs).  Only lengths are
     snapshotted around warm-up and capture: the steps write K/V at positions
     >= each row's length, which attention never reads before the real tokens
-    overwrite them, so the (possibly huge) cache is not copied."""
+    overwrite them, so the (possibly huge) cache is not copied.  ``keep_graph``
+    keeps the captured graph inspectable (``graph.raw_cuda_graph()``)."""
 
     def __init__(self, model, cache, *, width: int = 1, sample: tuple | None = None,
-                 tokens: torch.Tensor | None = None, uniform: torch.Tensor | None = None):
+                 tokens: torch.Tensor | None = None, uniform: torch.Tensor | None = None, keep_graph: bool = False):
         dev = model.device
         self.width = width
         self.sample = sample
@@ -126,7 +127,7 @@ class DecodeGraph:
                 for _ in range(_GRAPH_WARMUP):
                     self._step(model, cache)
                     _length_restore(cache, snap)
-                self.graph = torch.cuda.CUDAGraph()
+                self.graph = torch.cuda.CUDAGraph(keep_graph=keep_graph)
                 with torch.cuda.graph(self.graph, stream=stream):
                     self.logits, self.next_id = self._step(model, cache)
             torch.cuda.current_stream(dev).wait_stream(stream)

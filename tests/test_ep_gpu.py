@@ -1,5 +1,7 @@
-"""Expert-parallel batched decode on 2 GPUs (NCCL) vs single-GPU batched
-decode: identical greedy ids for every row (GPU; needs 2 GPUs)."""
+"""Expert-parallel batched decode on 2 GPUs vs single-GPU batched decode:
+identical greedy ids for every row, and one MoE block's output rows equal bit
+for bit, over NCCL and over the NVLink peer-memory exchange (GPU; needs 2
+GPUs)."""
 
 from __future__ import annotations
 
@@ -39,7 +41,26 @@ def _reference_ids(dev):
     return torch.stack(out, 1)
 
 
-def _worker(rank, world, port, q, transport):
+def _moe_inputs(cfg, dev):
+    g = torch.Generator(device="cpu").manual_seed(SEED + 11)
+    x = (torch.randn(B, cfg["hidden_size"], generator=g) * 0.5).to(torch.bfloat16).to(dev)
+    res = torch.randn(B, cfg["hidden_size"], generator=g).to(torch.bfloat16).to(dev)
+    return x, res
+
+
+def _reference_moe(dev):
+    """Layer 0's MoE block (+ residual) over all B rows on one GPU."""
+    from maple_flash_dgx_spark_b200.model import MapleForCausalLM
+    from maple_flash_dgx_spark_b200.synth import synthetic_weights
+
+    cfg = _cfg()
+    model = MapleForCausalLM.from_weight_dict(cfg, synthetic_weights(cfg, SEED, dev), device=dev)
+    x, res = _moe_inputs(cfg, dev)
+    with torch.inference_mode():
+        return model.layers[0].mlp(x, residual=res).cpu()
+
+
+def _worker(rank, world, port, q, transport, mode="decode"):
     import datetime
 
     import torch.distributed as dist
@@ -68,6 +89,15 @@ def _worker(rank, world, port, q, transport):
         fill_kv_cache(cache, SEED, CTX, row0=t0, total_rows=B)
         tok = synthetic_tokens(SEED, B, cfg["vocab_size"], dev)[t0:t0 + T].reshape(T, 1)
         dec = EPDecoder(model, ex)
+        if mode == "moe":
+            x, res = _moe_inputs(cfg, dev)
+            with torch.inference_mode():
+                out = model.layers[0].mlp(x[t0:t0 + T].contiguous(), residual=res[t0:t0 + T].contiguous())
+            torch.cuda.synchronize(dev)
+            if transport == "p2p":
+                ex.close()
+            q.put((rank, out.cpu()))
+            return
         ids = []
         with torch.inference_mode():
             for _ in range(STEPS // 2):
@@ -110,3 +140,28 @@ def test_ep_decode_equals_single_gpu(cuda, transport):
         p.join(timeout=60)
         assert p.exitcode == 0
     torch.testing.assert_close(torch.cat([got[0], got[1]]), ref, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("transport", ["nccl", "p2p"])
+def test_ep_moe_block_bit_exact(cuda, transport):
+    """One expert-parallel MoE block (dispatch, local experts, combine with the
+    residual) gives the single-GPU block's rows bit for bit."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ref = _reference_moe(cuda)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, transport, "moe")) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    out = torch.cat([got[0], got[1]])
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))

@@ -152,3 +152,44 @@ def test_model_decode_with_flash_head(cuda):
     b = run_generate(flash, prompt, max_tokens=12, temperature=0.0, log=None)
     assert a.token_ids == b.token_ids
     assert b.used_graph
+
+
+def test_flash_head_full_vocab_all_probes_exact(cuda):
+    """configs[4]'s head (151936 x 2048, RTN-4 group 128) in 4748 clusters of
+    32: with every cluster probed FlashHead returns the dense head's logits
+    bit for bit (reference tests/test_flash_head.py:89-112); at the default
+    512 probes the probed clusters' rows and the forced tokens equal the
+    dense logits, every other entry is -inf, and the top-20 recall is
+    printed."""
+    from maple_flash_dgx_spark_b200.flash_head import attach_flash_head
+    from maple_flash_dgx_spark_b200.model import MapleForCausalLM
+    from maple_flash_dgx_spark_b200.synth import synthetic_config, synthetic_weights
+
+    cfg = synthetic_config(num_layers=1)
+    assert cfg["vocab_size"] == 151936 and cfg["hidden_size"] == 2048
+    weights = synthetic_weights(cfg, 7, cuda)
+    force = [151643, 151645]
+    attach_flash_head(cfg, weights, n_clusters=4748, n_probes=4748, force_tokens=force)
+    full = MapleForCausalLM.from_weight_dict(cfg, dict(weights), device=cuda, use_flash_head=True)
+    cfg512 = dict(cfg)
+    cfg512["flash_head"] = dict(cfg["flash_head"], n_probes=512)
+    part = MapleForCausalLM.from_weight_dict(cfg512, dict(weights), device=cuda, use_flash_head=True)
+    g = torch.Generator(device="cpu").manual_seed(29)
+    recall = []
+    for _ in range(4):
+        h = torch.randn(1, 1, cfg["hidden_size"], generator=g).to(torch.bfloat16).to(cuda)
+        dense = full.lm_head(h.reshape(1, -1)).reshape(-1)
+        got = full.lm_head_flash(h).reshape(-1)
+        assert torch.equal(got.view(torch.int16), dense.view(torch.int16))
+        sub = part.lm_head_flash(h).reshape(-1)
+        fh = part.lm_head_flash
+        probed = fh.token_map[fh._cluster_ids.long()].reshape(-1).long()
+        keep = torch.zeros_like(sub, dtype=torch.bool)
+        keep[probed] = True
+        keep[torch.tensor(force, device=cuda)] = True
+        assert torch.equal(sub[keep].view(torch.int16), dense[keep].view(torch.int16))
+        assert bool(torch.isneginf(sub[~keep]).all())
+        top_d = set(torch.topk(dense.float(), 20).indices.tolist())
+        top_f = set(torch.topk(sub.float(), 20).indices.tolist())
+        recall.append(len(top_d & top_f) / 20)
+    print(f"FlashHead 4748x32, 512 probes: top-20 recall {sum(recall) / len(recall):.3f} on random hidden states")
