@@ -145,6 +145,37 @@ int maple_p2p_combine(void* const* peer_bases, int world, int rank, int64_t off_
                       int64_t tokens_per_rank, int64_t topk, int64_t n, const float* topk_weight,
                       const void* residual, void* out, unsigned* seq, unsigned* ticket, int* err, void* stream);
 
+/* Balanced spherical k-means of the lm_head rows for FlashHead (offline;
+ * reference flash_head.py:30-110, no C counterpart there).  Rows w [n][d]
+ * fp32 (d a multiple of 16, unit length), centroids cent [k][d] fp32.  Every
+ * similarity is one fp32 fmaf chain over d in order; ties go to the lowest
+ * cluster index.
+ * maple_km_assign: labels[r] = most similar centroid, best[r] = its
+ *   similarity (workspace: maple_km_assign_workspace_bytes).
+ * maple_km_dots: out[i][c] = similarity of row rows[i] with centroid c.
+ * maple_km_reassign: the evicted rows evict[] (in order) each take the most
+ *   similar cluster whose count (recount, at the start) is below
+ *   cluster_size, counting as they go; sims [n_evict][k] from maple_km_dots;
+ *   scratch: n_evict ints.
+ * maple_km_update: cent[j] = normalised mean of rows members[offsets[j] ..
+ *   offsets[j+1]) (ascending), summed in that order.
+ * maple_km_objective: per block of 1024 rows, the double sum of each row's
+ *   similarity to its centroid (maple_km_objective_blocks entries).
+ * maple_km_normalize: rows divided by (sqrt(R128 sum of squares) + 1e-8). */
+int64_t maple_km_assign_workspace_bytes(int64_t n, int64_t k);
+int maple_km_assign(const float* w, int64_t n, int64_t d, const float* cent, int64_t k, int32_t* labels, float* best,
+                    void* workspace, int64_t workspace_bytes, void* stream);
+int maple_km_dots(const float* w, const int32_t* rows, int64_t n_rows, int64_t d, const float* cent, int64_t k,
+                  float* out, void* stream);
+int maple_km_reassign(const float* sims, const int32_t* evict, int64_t n_evict, int64_t k, const int32_t* recount,
+                      int64_t cluster_size, int32_t* labels, int32_t* scratch, void* stream);
+int maple_km_update(const float* w, int64_t d, const int32_t* members, const int32_t* offsets, int64_t k, float* cent,
+                    void* stream);
+int64_t maple_km_objective_blocks(int64_t n);
+int maple_km_objective(const float* w, int64_t n, int64_t d, const int32_t* labels, const float* cent,
+                       double* partial, void* stream);
+int maple_km_normalize(float* v, int64_t rows, int64_t d, void* stream);
+
 /* Grouped expert GEMM on the tcgen05 tensor cores (accumulators in tensor
  * memory), for experts with many routed slots (prompt prefill, large batches):
  * the batched branch of kernels/ternary_gemv.py:156-258 and the expert kernels

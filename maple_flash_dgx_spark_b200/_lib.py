@@ -60,6 +60,14 @@ _SIGS: dict[str, tuple] = {
     "maple_p2p_dispatch": (i32, [vp, i32, i32, i64, vp, i32, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp, vp]),
     "maple_p2p_combine": (i32, [vp, i32, i32, i64, vp, i32, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp, vp, vp,
                                 vp]),
+    "maple_km_assign_workspace_bytes": (i64, [i64, i64]),
+    "maple_km_assign": (i32, [vp, i64, i64, vp, i64, vp, vp, vp, i64, vp]),
+    "maple_km_dots": (i32, [vp, vp, i64, i64, vp, i64, vp, vp]),
+    "maple_km_reassign": (i32, [vp, vp, i64, i64, vp, i64, vp, vp, vp]),
+    "maple_km_update": (i32, [vp, i64, vp, vp, i64, vp, vp]),
+    "maple_km_objective_blocks": (i64, [i64]),
+    "maple_km_objective": (i32, [vp, i64, i64, vp, vp, vp, vp]),
+    "maple_km_normalize": (i32, [vp, i64, i64, vp]),
     "maple_ternary_grouped_gemm": (i32, [vp, vp, i64, i64, vp, i64, i64, vp, i32, vp, vp, i64, i64, i32, i32, vp,
                                          i32, i64, vp, vp]),
     "maple_ternary_grouped_gemm_tc_workspace_bytes": (i64, [i64, i64]),

@@ -1,7 +1,8 @@
 """FlashHead: two-phase RTN-4 lm_head for batch-1 decode.
 
 Reference: flash_head.py:282-369 (``FlashHead``), :372-463
-(``build_flash_head``), :30-110 and :150-279 (clustering, offline).
+(``build_flash_head``), :30-110 and :150-279 (clustering, offline: the
+balanced spherical k-means runs on this package's CUDA kernels).
 
 Phase one scores the cluster centroids (``rtn4_gemv``), picks the
 ``n_probes`` best clusters on the device (``maple_topk_select``: radix select,
@@ -22,6 +23,7 @@ from maple_flash_dgx_spark_b200.kernels import rtn4_gemv, rtn4_indexed_gemv
 
 DEFAULT_N_CLUSTERS = 4748
 DEFAULT_N_PROBES = 512
+DEFAULT_KMEANS_ITERS = 60
 HEAD_GROUP_SIZE = 64
 
 
@@ -159,47 +161,108 @@ def build_flash_head(*, config: dict, lm_head, weights: dict, device, dtype) -> 
                      centroid_group_size=centroid_group)
 
 
-def cluster_head(w_dir: torch.Tensor, n_clusters: int, n_iter: int = 8, seed: int = 42):
-    """Balanced spherical k-means of L2-normalised head rows ``[V, D]`` (the
-    offline step of reference flash_head.py:30-110, simplified: assignment by
-    cosine, then equal-size rebalancing by sorting each row's score to its
-    nearest centroid).  Returns ``(centroids [C, D], token_map [C, V/C])``."""
-    V, D = w_dir.shape
-    cs = V // n_clusters
-    g = torch.Generator(device=w_dir.device)
-    g.manual_seed(int(seed))
-    C = w_dir[torch.randperm(V, generator=g, device=w_dir.device)[:n_clusters]].clone()
-    labels = None
-    for _ in range(n_iter):
-        sim = w_dir @ C.T
-        best, arg = sim.max(dim=1)
-        # capacity-limited greedy: rows in order of confidence take their best
-        # cluster while it has room; the rest fill the emptiest clusters
-        order = torch.argsort(best, descending=True)
-        lab = torch.full((V,), -1, dtype=torch.int64, device=w_dir.device)
-        counts = torch.zeros(n_clusters, dtype=torch.int64, device=w_dir.device)
-        a_sorted = arg[order]
-        rank = torch.zeros_like(a_sorted)
-        # rank of each row among rows preferring the same cluster
-        srt, perm = torch.sort(a_sorted, stable=True)
-        first = torch.searchsorted(srt, srt, right=False)
-        rank[perm] = torch.arange(V, device=w_dir.device) - first
-        keep = rank < cs
-        lab[order[keep]] = a_sorted[keep]
-        counts.scatter_add_(0, a_sorted[keep], torch.ones_like(a_sorted[keep]))
-        rest = order[~keep]
-        free = (cs - counts).clamp(min=0)
-        slots = torch.repeat_interleave(torch.arange(n_clusters, device=w_dir.device), free)
-        lab[rest] = slots[: rest.numel()]
-        labels = lab
-        C = torch.zeros_like(C).index_add_(0, labels, w_dir)
-        C = C / (C.norm(dim=1, keepdim=True) + 1e-8)
-    token_map = torch.argsort(labels, stable=True).reshape(n_clusters, cs).to(torch.int32)
-    return C, token_map
+def balanced_spherical_kmeans(w_dir: torch.Tensor, n_clusters: int, n_iter: int = DEFAULT_KMEANS_ITERS,
+                              seed: int = 42, init: torch.Tensor | None = None):
+    """Balanced spherical k-means over L2-normalised rows ``[N, D]`` into
+    equal-size clusters (reference flash_head.py:30-110, same steps and
+    tie rules), on this package's CUDA kernels (``maple_km_*``): per
+    iteration the assignment, the eviction of each over-full cluster's least
+    similar members, their sequential reassignment to the most similar open
+    cluster, the centroid update and the objective; the best iteration's
+    centroids and labels are returned.  ``init``: the initial centroid rows
+    (default: the reference's ``torch.randperm`` draw for ``seed`` on the
+    rows' device).  Returns ``(centroids [K, D] fp32, labels [N] int32)``."""
+    op = "balanced_spherical_kmeans"
+    _lib.require_cuda(op, w_dir)
+    w = w_dir.float().contiguous()
+    N, D = w.shape
+    K = int(n_clusters)
+    if K <= 0 or N % K:
+        raise ValueError(f"{K} clusters do not divide {N} rows.")
+    if D % 16:
+        raise ValueError(f"row length {D} must be a multiple of 16.")
+    cs = N // K
+    dev = w.device
+    L = lib()
+    st = stream_ptr(dev)
+    if init is None:
+        g = torch.Generator(device=dev)
+        g.manual_seed(int(seed))
+        init = torch.randperm(N, generator=g, device=dev)[:K]
+    cent = w.index_select(0, init.to(device=dev, dtype=torch.int64)).contiguous()
+    check(L.maple_km_normalize(ptr(cent), K, D, st), op)
+    labels = torch.empty(N, dtype=torch.int32, device=dev)
+    best = torch.empty(N, dtype=torch.float32, device=dev)
+    ws = torch.empty(L.maple_km_assign_workspace_bytes(N, K), dtype=torch.uint8, device=dev)
+    partial = torch.empty(L.maple_km_objective_blocks(N), dtype=torch.float64, device=dev)
+    rows = torch.arange(N, device=dev)
+    best_obj, best_c, best_l = -1.0, None, None
+    for _ in range(int(n_iter)):
+        check(L.maple_km_assign(ptr(w), N, D, ptr(cent), K, ptr(labels), ptr(best), ptr(ws), ws.numel(), st), op)
+        lab = labels.long()
+        over = torch.bincount(lab, minlength=K) > cs
+        if bool(over.any()):
+            # each over-full cluster keeps its cs most similar members (lower row on ties)
+            cand = rows[over[lab]]
+            cand = cand[torch.argsort(-best[cand], stable=True)]
+            cand = cand[torch.argsort(lab[cand], stable=True)]
+            cl = lab[cand]
+            rank = torch.arange(cand.numel(), device=dev) - torch.searchsorted(cl, cl)
+            dumped = cand[rank >= cs].sort().values
+            evict = dumped[torch.argsort(lab[dumped], stable=True)]  # by cluster, then row
+            lab[evict] = -1
+            recount = torch.bincount(lab[lab >= 0], minlength=K).to(torch.int32)
+            evict32 = evict.to(torch.int32).contiguous()
+            sims = torch.empty(evict32.numel(), K, dtype=torch.float32, device=dev)
+            check(L.maple_km_dots(ptr(w), ptr(evict32), evict32.numel(), D, ptr(cent), K, ptr(sims), st), op)
+            labels = lab.to(torch.int32).contiguous()
+            scratch = torch.empty(max(1, evict32.numel()), dtype=torch.int32, device=dev)
+            check(L.maple_km_reassign(ptr(sims), ptr(evict32), evict32.numel(), K, ptr(recount), cs, ptr(labels),
+                                      ptr(scratch), st), op)
+            del sims
+        members = torch.argsort(labels.long(), stable=True).to(torch.int32)
+        offsets = torch.zeros(K + 1, dtype=torch.int32, device=dev)
+        offsets[1:] = torch.cumsum(torch.bincount(labels.long(), minlength=K), 0)
+        check(L.maple_km_update(ptr(w), D, ptr(members), ptr(offsets), K, ptr(cent), st), op)
+        check(L.maple_km_objective(ptr(w), N, D, ptr(labels), ptr(cent), ptr(partial), st), op)
+        total = 0.0
+        for p_ in partial.cpu().tolist():  # block sums in order
+            total += p_
+        obj = total / N
+        if obj > best_obj:
+            best_obj, best_c, best_l = obj, cent.clone(), labels.clone()
+    return best_c, best_l
+
+
+def token_map_of(labels: torch.Tensor, n_clusters: int) -> torch.Tensor:
+    """``[K, N/K]`` rows of each cluster in ascending order (reference
+    flash_head.py:212-217; a short cluster repeats its first member)."""
+    K = int(n_clusters)
+    cs = labels.numel() // K
+    counts = torch.bincount(labels.long(), minlength=K)
+    order = torch.argsort(labels.long(), stable=True)
+    if bool((counts == cs).all()):
+        return order.reshape(K, cs).to(torch.int32)
+    lab = labels.cpu().numpy()
+    out = torch.zeros(K, cs, dtype=torch.int32)
+    for c in range(K):
+        members = [int(i) for i in (lab == c).nonzero()[0][:cs]]
+        while len(members) < cs:
+            members.append(members[0] if members else 0)
+        out[c] = torch.tensor(members, dtype=torch.int32)
+    return out.to(labels.device)
+
+
+def cluster_head(w_dir: torch.Tensor, n_clusters: int, n_iter: int = DEFAULT_KMEANS_ITERS, seed: int = 42):
+    """Cluster L2-normalised head rows ``[V, D]``: ``(centroids [C, D],
+    token_map [C, V/C])`` by the balanced spherical k-means."""
+    cent, labels = balanced_spherical_kmeans(w_dir, n_clusters, n_iter=n_iter, seed=seed)
+    return cent, token_map_of(labels, n_clusters)
 
 
 def attach_flash_head(config: dict, weights: dict, *, n_clusters: int = DEFAULT_N_CLUSTERS,
-                      n_probes: int = DEFAULT_N_PROBES, force_tokens=(), seed: int = 42, n_iter: int = 8) -> dict:
+                      n_probes: int = DEFAULT_N_PROBES, force_tokens=(), seed: int = 42,
+                      n_iter: int = DEFAULT_KMEANS_ITERS) -> dict:
     """Cluster the RTN-4 ``lm_head`` in ``weights`` and add the
     ``lm_head_flash.*`` tensors and ``flash_head`` metadata the way the
     reference converter does (flash_head.py:150-279): rows are dequantised and

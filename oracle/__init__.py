@@ -165,6 +165,10 @@ _SIGS = {
     "orc_argmax": (None, [_f32p, _i64, _i64, _i64p]),
     "orc_fused_sample": (None, [_f32p, _i64, _i64, _f32p, _flt, _flt, _i64, _i64p]),
     "orc_rtn4_embedding": (None, [_i64p, _i64, _u32p, _f32p, _vp, _i64, _i64, _i64, _int, _f32p]),
+    "orc_km_dots": (None, [_f32p, _i64, _f32p, _i64, _i64, _f32p]),
+    "orc_km_normalize": (None, [_f32p, _i64, _i64]),
+    "orc_km_update": (None, [_f32p, _i64, _i64, _i32p, _i64, _f32p]),
+    "orc_km_objective": (ctypes.c_double, [_f32p, _i64, _i64, _i32p, _f32p]),
 }
 
 

@@ -668,3 +668,70 @@ void orc_synth_tokens(uint64_t seed, uint64_t stream, int64_t n, int64_t vocab, 
   const uint64_t key = skey(seed, stream);
   for (int64_t i = 0; i < n; ++i) out[i] = (int64_t)(hat(key, (uint64_t)i) % (uint64_t)vocab);
 }
+
+/* ------------------------------------------------ balanced k-means ---- */
+/* Reference: src/maple_run/flash_head.py:30-110 (_balanced_spherical_kmeans),
+ * restated in the canonical arithmetic of the CUDA k-means
+ * (maple_flash_dgx_spark_b200/csrc/kmeans.cu): a similarity is the fp32 dot
+ * accumulated over k = 0..d-1 in order from 0.0f with fmaf; a centroid is the
+ * fp32 sum of its members' rows in ascending row order (plain adds), divided
+ * by the member count (at least 1), then divided by (sqrt(R128 sum of
+ * squares) + 1e-8); the objective is the mean of the members' similarities
+ * to their centroids, summed in double within blocks of 1024 rows in order
+ * and then over the blocks in order. */
+void orc_km_dots(const float* a, int64_t na, const float* b, int64_t nb, int64_t d, float* out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < na; ++i) {
+    const float* ar = a + i * d;
+    for (int64_t j = 0; j < nb; ++j) {
+      const float* br = b + j * d;
+      float acc = 0.0f;
+      for (int64_t k = 0; k < d; ++k) acc = fmaf(ar[k], br[k], acc);
+      out[i * nb + j] = acc;
+    }
+  }
+}
+
+void orc_km_normalize(float* v, int64_t rows, int64_t d) {
+  for (int64_t j = 0; j < rows; ++j) {
+    float* r = v + j * d;
+    const float nrm = sqrtf(orc_r128_sumsq(r, d)) + 1e-8f;
+    for (int64_t k = 0; k < d; ++k) r[k] = r[k] / nrm;
+  }
+}
+
+void orc_km_update(const float* w, int64_t n, int64_t d, const int32_t* labels, int64_t c, float* cent) {
+  int64_t* cnt = (int64_t*)calloc((size_t)c, sizeof(int64_t));
+  memset(cent, 0, (size_t)(c * d) * sizeof(float));
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t l = labels[i];
+    cnt[l] += 1;
+    float* cr = cent + l * d;
+    const float* wr = w + i * d;
+    for (int64_t k = 0; k < d; ++k) cr[k] = cr[k] + wr[k];
+  }
+  for (int64_t j = 0; j < c; ++j) {
+    const float cf = (float)(cnt[j] > 0 ? cnt[j] : 1);
+    float* cr = cent + j * d;
+    for (int64_t k = 0; k < d; ++k) cr[k] = cr[k] / cf;
+  }
+  orc_km_normalize(cent, c, d);
+  free(cnt);
+}
+
+double orc_km_objective(const float* w, int64_t n, int64_t d, const int32_t* labels, const float* cent) {
+  double total = 0.0;
+  for (int64_t b0 = 0; b0 < n; b0 += 1024) {
+    double part = 0.0;
+    const int64_t b1 = b0 + 1024 < n ? b0 + 1024 : n;
+    for (int64_t i = b0; i < b1; ++i) {
+      const float* wr = w + i * d;
+      const float* cr = cent + (int64_t)labels[i] * d;
+      float acc = 0.0f;
+      for (int64_t k = 0; k < d; ++k) acc = fmaf(wr[k], cr[k], acc);
+      part += (double)acc;
+    }
+    total += part;
+  }
+  return total / (double)n;
+}

@@ -103,6 +103,40 @@ def test_expert_down(cuda, K, mode, T, topk, E, N, k):
     np.testing.assert_array_equal(to_np(out), out_o)
 
 
+@pytest.mark.parametrize("skew", [False, True])
+def test_grouped_expert_gemms_decode_sizes(cuda, K, skew):
+    """configs[3]'s MoE at batch 64 (64 tokens x top-8 over 128 experts, ~4
+    slots per expert: the persistent streaming grouped kernels): SwiGLU
+    (K=2048, I=768) and down (K=768, N=2048) equal the oracle bit for bit.
+    The skewed routing sends many slots to a few experts (several digit
+    chunks per expert), leaves others empty, and has one out-of-range id (a
+    NaN row)."""
+    rs = rng(71 + skew)
+    T, topk, E, inter, k = 64, 8, 128, 768, 2048
+    x = randn_bf(rs, T, k)
+    up = tern_packed(rs, E, 2 * inter, k)
+    a_up = bf(alpha_bf(rs, E, 2 * inter) * 40)
+    down = tern_packed(rs, E, k, inter)
+    a_dn = alpha_bf(rs, E, k)
+    if skew:
+        hot = np.array([3, 17, 64, 127])
+        ids = np.stack([np.concatenate([hot, rs.permutation(np.setdiff1d(np.arange(40), hot))[:topk - 4]])
+                        for _ in range(T)]).astype(np.int32)
+        ids[5, 7] = -1
+    else:
+        ids = np.stack([rs.permutation(E)[:topk] for _ in range(T)]).astype(np.int32)
+    h = K.ternary_expert_swiglu(to_dev(x, cuda, torch.bfloat16), to_dev(up, cuda), to_dev(a_up, cuda, torch.bfloat16),
+                                to_dev(ids, cuda))
+    h_o = oracle.expert_swiglu(x, up, a_up, ids)
+    np.testing.assert_array_equal(to_np(h), h_o)
+    y = K.ternary_expert_gemv(to_dev(h_o, cuda, torch.bfloat16), to_dev(down, cuda), to_dev(a_dn, cuda, torch.bfloat16),
+                              to_dev(ids, cuda))
+    y_o = oracle.expert_gemv(h_o.reshape(-1, inter), down, a_dn, ids, x_rows_per_token=1)
+    np.testing.assert_array_equal(to_np(y).reshape(-1, k), y_o)
+    if skew:
+        assert np.isnan(y_o[5 * topk + 7]).all()
+
+
 def test_moe_reduce_add(cuda, K):
     rs = rng(9)
     x = randn_bf(rs, 3, 8, 2048)
