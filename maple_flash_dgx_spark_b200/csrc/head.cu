@@ -445,9 +445,7 @@ __global__ void embed_rtn4_kernel(const int64_t* ids, const uint32_t* codes, con
 
 }  // namespace mb
 
-using namespace mb;
-
-namespace {
+namespace mb {
 // ---------------------------------------------------- batched RTN-4 head --
 // For B > 1 rows the head is streamed once per chunk of up to 2*NP rows
 // instead of once per row: rtn4_encode_kernel FXA-encodes each row once (4-bit
@@ -690,7 +688,9 @@ int rtn4_checks(int x_dtype, int s_dtype, int64_t k, int64_t group) {
   if (k % group != 0 || k / group > 64) return kErrShape;
   return kOk;
 }
-}  // namespace
+}  // namespace mb
+
+using namespace mb;
 
 extern "C" int maple_rtn4_gemv(const void* x, int x_dtype, int64_t batch, int64_t k, int64_t x_row_stride,
                                const uint32_t* codes, int64_t n, const void* scales, const void* biases,

@@ -43,14 +43,15 @@ from maple_flash_dgx_spark_b200.kernels import (
     ternary_expert_swiglu,
 )
 
-PHASES = ("attention", "router", "dispatch", "experts", "combine", "head")
+PHASES = ("qkv", "attention", "o_norm", "router", "dispatch", "experts", "combine", "head")
 
 
 class PhaseMarks:
     """Timing events at the phase boundaries of one decode step, recorded as
     event nodes when the step is captured in a CUDA graph (``external``
-    events), so a replay can be split into its phases: attention (QKV,
-    attention, O, residual add + norm), router, dispatch, experts (SwiGLU +
+    events), so a replay can be split into its phases: qkv (input norm + QKV
+    projection), attention (QK-norm, RoPE, K/V store, attention), o_norm (O
+    projection, residual add + norm), router, dispatch, experts (SwiGLU +
     down), combine, and the sharded head (final norm, row gather, head GEMV,
     candidate gather).  Phase times are summed over the layers."""
 
@@ -358,6 +359,7 @@ class EPDecoder:
         self.marks = marks
         for layer in self.model.layers:
             layer.mlp.marks = marks
+            layer.self_attn.marks = marks
 
     def _mark(self, name: str) -> None:
         if self.marks is not None:
@@ -380,7 +382,7 @@ class EPDecoder:
                                    kv_final=True)
             post = layer.post_attention_layernorm
             hidden, mlp_in = add_rms_norm(hidden, attn, post.weight, post.eps)
-            self._mark("attention")
+            self._mark("o_norm")
             hidden = layer.mlp(mlp_in, residual=hidden)
         cache.advance(1, rows)
         ids = self.head.next_ids(m.norm(hidden))

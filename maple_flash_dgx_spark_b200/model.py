@@ -220,7 +220,15 @@ class KVCache:
 
 class MapleAttention:
     """Decode attention of one layer (reference model.py:320-414): fused
-    RMSNorm->QKV GEMV, QK-norm/RoPE/KV-store, split-K GQA, O GEMV."""
+    RMSNorm->QKV GEMV, QK-norm/RoPE/KV-store, split-K GQA, O GEMV.
+    ``marks`` (optional, an expert_parallel.PhaseMarks) records the phase
+    boundaries after the QKV projection and after the attention."""
+
+    marks = None
+
+    def _mark(self, name: str) -> None:
+        if self.marks is not None:
+            self.marks.mark(name)
 
     def __init__(self, qkv, o_proj, q_norm, k_norm, *, num_heads, num_kv_heads, head_dim, sliding_window,
                  use_qk_norm, use_rope, layer_idx):
@@ -241,6 +249,7 @@ class MapleAttention:
     def __call__(self, hidden, seqlen, row_map, rotary, cache, *, rms_weight, rms_eps, kv_final=False):
         rows = hidden.shape[0]
         qkv = self.qkv_proj(hidden, rms_weight=rms_weight, rms_eps=rms_eps)
+        self._mark("qkv")
         k_cache, v_cache = cache.k[self.layer_idx], cache.v[self.layer_idx]
         if row_map is None:
             k_cache, v_cache = k_cache[:rows], v_cache[:rows]
@@ -253,6 +262,7 @@ class MapleAttention:
                                       head_dim=self.head_dim, rotary_dim=rotary.rotary_dim, use_rope=self.use_rope,
                                       eps=self.q_norm.eps, scale=self.scale, window=self.sliding_window,
                                       split_len=cache.split_len)
+            self._mark("attention")
             return self.o_proj(attn.reshape(rows, -1))
         q = apply_qkv_decode(qkv, self.q_norm.weight, self.k_norm.weight, rotary.cos_table, rotary.sin_table,
                              k_cache, v_cache, seqlen, row_map=row_map, num_heads=self.num_heads,
@@ -262,6 +272,7 @@ class MapleAttention:
         attn = decode_gqa_attn(q, k_cache, v_cache, seqlen, row_map=row_map, scale=self.scale,
                                window=self.sliding_window, split_len=cache.split_len, kv_final=kv_final,
                                tensor_cores=getattr(cache, "attn_tc", False))
+        self._mark("attention")
         return self.o_proj(attn.reshape(rows, -1))
 
 
