@@ -48,15 +48,18 @@ def _args():
                     help="bs1 on one GPU: skip the batch-64 point measured after the batch-1 line")
     ap.add_argument("--breakdown", action="store_true",
                     help="also time each operator of the decode step in its own CUDA graph (48 layers)")
-    ap.add_argument("--workload", choices=["auto", "bs1", "bs64", "long", "attn", "prefill"], default="auto",
+    ap.add_argument("--workload", choices=["auto", "bs1", "bs64", "long", "attn", "prefill", "kmeans"],
+                    default="auto",
                     help="auto: bs64 under torchrun (expert-parallel scaling), else bs1; bs1: configs[2] batch-1 "
                          "decode; bs64: configs[3] batch-64 decode at 8192 cached positions per row; long: "
                          "configs[4] long-context sampling (FlashHead at batch 1); attn: the decode-attention "
                          "kernels alone (--batch rows x --context positions); prefill: the configs[2] 512-token "
-                         "prompt with and without the tcgen05 expert GEMM, and that GEMM alone")
+                         "prompt with and without the tcgen05 expert GEMM, and that GEMM alone; kmeans: the FlashHead "
+                         "balanced spherical k-means of --rows head rows")
     ap.add_argument("--context", type=int, default=None,
                     help="cached positions per row (bs64: 8192, long: 65536)")
     ap.add_argument("--batch", type=int, default=1, help="long: rows (1, 16 or 256)")
+    ap.add_argument("--rows", type=int, default=151936, help="kmeans: head rows (a multiple of 32)")
     return ap.parse_args()
 
 
@@ -244,6 +247,9 @@ def main():
         return
     if args.workload == "prefill":
         run_prefill(args)
+        return
+    if args.workload == "kmeans":
+        run_kmeans(args)
         return
     line = run_bs1(args)
     world, rank, _ = _dist()
@@ -944,6 +950,54 @@ def run_attn(args):
     out["peak_gbs"] = peak
     out["peak_kind"] = f"{peak_kind} hbm_gbs"
     print(json.dumps(out), flush=True)
+
+
+def run_kmeans(args):
+    """FlashHead clustering of the configs[4] head: the balanced spherical
+    k-means (CUDA) of ``--rows`` unit rows of the head's 2048 columns into
+    rows/32 clusters, ``--steps`` iterations from the reference's initial draw.
+    Reports the wall time per iteration (host bookkeeping included), the
+    assignment launch alone (CUDA events) against fp32 CUDA-core FMA
+    throughput, and the balance of the result."""
+    import torch
+
+    from maple_flash_dgx_spark_b200 import _lib
+    from maple_flash_dgx_spark_b200.flash_head import balanced_spherical_kmeans
+
+    dev = torch.device("cuda", 0)
+    n, d = int(args.rows), 2048
+    k = n // 32
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn(n, d, device=dev, generator=g)
+    w = (w / (w.norm(dim=1, keepdim=True) + 1e-8)).contiguous()
+    iters = max(int(args.steps), 1)
+    balanced_spherical_kmeans(w, k, n_iter=1)  # warm
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    cent, labels = balanced_spherical_kmeans(w, k, n_iter=iters)
+    torch.cuda.synchronize(dev)
+    wall = (time.perf_counter() - t0) / iters
+    L = _lib.lib()
+    lab = torch.empty(n, dtype=torch.int32, device=dev)
+    best = torch.empty(n, dtype=torch.float32, device=dev)
+    ws = torch.empty(L.maple_km_assign_workspace_bytes(n, k), dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+
+    def assign():
+        _lib.check(L.maple_km_assign(w.data_ptr(), n, d, cent.data_ptr(), k, lab.data_ptr(), best.data_ptr(),
+                                     ws.data_ptr(), ws.numel(), st), "km_assign")
+
+    ms = _event_ms(assign, 5)
+    flops = 2.0 * n * k * d
+    counts = torch.bincount(labels.long(), minlength=k)
+    fp32_nominal = 148 * 128 * 2 * 1.965e9 / 1e12  # TFLOP/s: 148 SMs x 128 FP32 lanes x FMA x 1965 MHz
+    print(json.dumps({
+        "workload": f"FlashHead balanced spherical k-means, {n} x {d} unit rows into {k} clusters of 32",
+        "iterations": iters, "s_per_iteration": wall,
+        "assign_ms": ms, "assign_tflops": flops / (ms * 1e-3) / 1e12,
+        "assign_frac_of_fp32_nominal": flops / (ms * 1e-3) / 1e12 / fp32_nominal,
+        "fp32_nominal_tflops": fp32_nominal,
+        "balanced": bool((counts == 32).all()), "device_errors": _lib.take_device_errors(dev)}), flush=True)
 
 
 def run_prefill(args):
