@@ -377,19 +377,20 @@ cudaError_t launch_tgemm(const TGemmParams& p, dim3 grid, cudaStream_t st) {
 inline int tgemm_wm(int iters) { return iters <= 8 ? 4 : 2; }
 inline int tile_rows(int mode, int iters) { return (mode == kGSwiglu ? 8 : 16) * tgemm_wm(iters); }
 
-// Single-buffer expert groups (decode-sized: a few routed slots per expert)
-// take 4 slots per chunk, so fewer MMAs and digit bytes go to empty slots
-// (measured at configs[3]: grouped SwiGLU 103 -> 93 us, down 86 -> 64 us).
-// Dense launches keep the larger chunks: the host sizes their grid by them.
+// Single-buffer expert groups (decode-sized: about 8 routed slots per expert
+// at configs[3]) take 8 slots per chunk also for K <= 1024, so fewer MMAs and
+// digit bytes go to empty slots (measured with the weights streaming from
+// HBM: grouped down GEMM 61.1 -> 55.4 us; 4-slot chunks: 57.9 us, and the
+// SwiGLU 98.8 -> 101.6 us).  Dense launches keep their chunks: the host sizes
+// their grid by them.
 template <int AT, int OT, int MODE, int NBUF>
 cudaError_t dispatch_tgemm_buf(const TGemmParams& p, dim3 grid, cudaStream_t st) {
   const bool small_groups = NBUF == 1 && p.offsets != nullptr;
   if (p.iters <= 4)  // K <= 1024
-    return small_groups ? launch_tgemm<AT, OT, MODE, 4, 2, 2, 4, NBUF>(p, grid, st)
+    return small_groups ? launch_tgemm<AT, OT, MODE, 4, 2, 2, 8, NBUF>(p, grid, st)
                         : launch_tgemm<AT, OT, MODE, 4, 2, 2, 16, NBUF>(p, grid, st);
   if (p.iters <= 8)  // K <= 2048
-    return small_groups ? launch_tgemm<AT, OT, MODE, 4, 2, 4, 4, NBUF>(p, grid, st)
-                        : launch_tgemm<AT, OT, MODE, 4, 2, 4, 8, NBUF>(p, grid, st);
+    return launch_tgemm<AT, OT, MODE, 4, 2, 4, 8, NBUF>(p, grid, st);
   if (p.iters <= 16) return launch_tgemm<AT, OT, MODE, 2, 4, 4, 4, NBUF>(p, grid, st);   // K <= 4096
   return cudaErrorInvalidValue;
 }

@@ -105,14 +105,14 @@ def test_expert_down(cuda, K, mode, T, topk, E, N, k):
 
 @pytest.mark.parametrize("skew", [False, True])
 def test_grouped_expert_gemms_decode_sizes(cuda, K, skew):
-    """configs[3]'s MoE at batch 64 (64 tokens x top-8 over 128 experts, ~4
-    slots per expert: the persistent streaming grouped kernels): SwiGLU
-    (K=2048, I=768) and down (K=768, N=2048) equal the oracle bit for bit.
-    The skewed routing sends many slots to a few experts (several digit
-    chunks per expert), leaves others empty, and has one out-of-range id (a
-    NaN row)."""
+    """configs[3]'s MoE at batch 64 (64 tokens x top-8 over 64 experts, ~8
+    slots per expert: the single-buffer grouped kernels): SwiGLU (K=2048,
+    I=1024) and down (K=1024, N=2048) equal the oracle bit for bit.  The
+    skewed routing sends many slots to a few experts (several digit chunks
+    per expert), leaves others empty, and has one out-of-range id (a NaN
+    row)."""
     rs = rng(71 + skew)
-    T, topk, E, inter, k = 64, 8, 128, 768, 2048
+    T, topk, E, inter, k = 64, 8, 64, 1024, 2048
     x = randn_bf(rs, T, k)
     up = tern_packed(rs, E, 2 * inter, k)
     a_up = bf(alpha_bf(rs, E, 2 * inter) * 40)
