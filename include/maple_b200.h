@@ -187,13 +187,17 @@ int maple_km_normalize(float* v, int64_t rows, int64_t d, void* stream);
  * maple_ternary_grouped_gemm and bit-identical results.  k % 128 == 0,
  * k <= 8192; workspace (256-byte aligned) of
  * maple_ternary_grouped_gemm_tc_workspace_bytes(n_slots, k) bytes.  A bounded
- * wait that gives up sets bit 1 of *err. */
+ * wait that gives up sets bit 1 of *err.  rms_w (optional, plain mode only,
+ * k elements): the fused input RMSNorm of maple_ternary_gemv (the digits
+ * encode x * rms_w and each output is scaled by the row's rstd), so a dense
+ * batched GEMM can run here as one "expert" whose plan lists every row. */
 int64_t maple_ternary_grouped_gemm_tc_workspace_bytes(int64_t n_slots, int64_t k);
 int maple_ternary_grouped_gemm_tc(const void* x, int x_dtype, int64_t in_rows, int64_t k, int64_t x_row_stride,
                                   const uint32_t* codes, int64_t n_experts, int64_t code_rows, const void* alpha,
                                   int alpha_dtype, const int32_t* offsets, const uint32_t* list, int64_t n_slots,
-                                  int64_t in_div, int swiglu, void* y, int y_dtype, int64_t y_row_stride,
-                                  void* workspace, int64_t workspace_bytes, int* err, void* stream);
+                                  int64_t in_div, int swiglu, const void* rms_w, int rms_dtype, float eps, void* y,
+                                  int y_dtype, int64_t y_row_stride, void* workspace, int64_t workspace_bytes,
+                                  int* err, void* stream);
 
 /* Grouped expert GEMM over a plan: slot s reads encoded row s / in_div
  * (in_div = top_k when rows are tokens, 1 when they are slots) and writes

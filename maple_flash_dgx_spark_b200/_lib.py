@@ -72,7 +72,7 @@ _SIGS: dict[str, tuple] = {
                                          i32, i64, vp, vp]),
     "maple_ternary_grouped_gemm_tc_workspace_bytes": (i64, [i64, i64]),
     "maple_ternary_grouped_gemm_tc": (i32, [vp, i32, i64, i64, i64, vp, i64, i64, vp, i32, vp, vp, i64, i64, i32,
-                                            vp, i32, i64, vp, i64, vp, vp]),
+                                            vp, i32, f32, vp, i32, i64, vp, i64, vp, vp]),
     "maple_ternary_expert_gemv_workspace_bytes": (i64, [i64, i64, i64]),
     "maple_ternary_expert_gemv": (i32, [vp, i32, i64, i64, vp, i64, i64, vp, i64, i64, vp, i32, vp, i64, vp,
                                         i64, vp]),

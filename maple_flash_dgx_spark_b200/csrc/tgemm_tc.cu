@@ -52,15 +52,17 @@ constexpr int kTcCodeBytes = kTcARows * 32;   // one K block of packed codes: 12
 // Position p (expert-sorted) encodes input row (list[p] & ~bad) / in_div;
 // positions past offsets[n_experts] (slots of other ranks' experts under
 // expert parallelism, not listed) are skipped.
-template <int XT>
-__global__ void __launch_bounds__(256) fxa_plain_kernel(const void* x, int64_t x_stride, int K,
-                                                        const int* offsets, int n_experts, const unsigned* list,
-                                                        int in_div, int8_t* digits, int* meta) {
+template <int XT, int RT, bool RMS>
+__global__ void __launch_bounds__(256) fxa_plain_kernel(const void* x, int64_t x_stride, const void* rms_w, float eps,
+                                                        int K, const int* offsets, int n_experts,
+                                                        const unsigned* list, int in_div, int8_t* digits,
+                                                        int* meta) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ FxaBlock fb;
   const int iters = (K + 255) / 256;
   uint2* frag = reinterpret_cast<uint2*>(smem);
   float* xsm = reinterpret_cast<float*>(smem + (size_t)iters * 256 * sizeof(uint2));
+  float* wsm = xsm + K;  // RMS: x * w, the encoded values
   const int p = blockIdx.x;
   pdl_wait();
   // the GEMM that follows is released only once these CTAs are done: its
@@ -73,14 +75,15 @@ __global__ void __launch_bounds__(256) fxa_plain_kernel(const void* x, int64_t x
   const int64_t row = (int64_t)(list[p] & ~kTcBadSlot) / in_div;
   const void* xr = static_cast<const char*>(x) + row * x_stride * (XT == kBF16 ? 2 : 4);
   // shift and digit totals exactly as the fragment encoders compute them
-  fxa_prologue<XT, kF32, false, 2, 256>(xr, nullptr, K, 0.0f, 0, iters, xsm, nullptr, frag, fb);
+  fxa_prologue<XT, RT, RMS, 2, 256>(xr, rms_w, K, eps, 0, iters, xsm, RMS ? wsm : nullptr, frag, fb);
   const int s = fb.s;
   const bool bad = (s == kFxaNonFinite);
+  const float* xh = RMS ? wsm : xsm;
   int8_t* d0 = digits + (int64_t)p * 4 * K;
   for (int k = 4 * threadIdx.x; k < K; k += 4 * 256) {
     uint32_t u[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) u[i] = static_cast<uint32_t>((bad ? 0 : fxa_enc(xsm[k + i], s)) + kFxaOffset);
+    for (int i = 0; i < 4; ++i) u[i] = static_cast<uint32_t>((bad ? 0 : fxa_enc(xh[k + i], s)) + kFxaOffset);
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       *reinterpret_cast<uint32_t*>(d0 + (int64_t)j * K + k) = signed_digits(raw_digits(u[0], u[1], u[2], u[3], j));
@@ -162,6 +165,7 @@ struct TcGemmParams {
   int* err;
   int64_t y_stride, expert_words, alpha_estride;
   int rows, n_out, K, nwords;
+  int use_rstd;           // multiply by the row's rstd (fused input RMSNorm, plain mode)
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -386,7 +390,9 @@ __global__ void __launch_bounds__(352, 1) tgemm_tc_kernel(TcGemmParams p, const 
             const unsigned slot = s_slot[idx];
             const int sh = ms[0];
             const bool nan_out = (sh == kFxaNonFinite) || (slot & kTcBadSlot);
-            const float v = __fmul_rn(nan_out ? __int_as_float(0x7fc00000) : fxa_value(S, sh), a_m);
+            float v = nan_out ? __int_as_float(0x7fc00000) : fxa_value(S, sh);
+            if (!SWIGLU && p.use_rstd) v = __fmul_rn(v, __int_as_float(ms[1]));
+            v = __fmul_rn(v, a_m);
             if constexpr (SWIGLU) {
               if (m >= 64) s_gate[idx * 64 + (m - 64)] = v;
               else s_gate[kTcSlots * 64 + idx * 64 + m] = v;  // up values after the gate block
@@ -451,9 +457,9 @@ extern "C" int maple_ternary_grouped_gemm_tc(const void* x, int x_dtype, int64_t
                                              int64_t x_row_stride, const uint32_t* codes, int64_t n_experts,
                                              int64_t code_rows, const void* alpha, int alpha_dtype,
                                              const int32_t* offsets, const uint32_t* list, int64_t n_slots,
-                                             int64_t in_div, int swiglu, void* y, int y_dtype,
-                                             int64_t y_row_stride, void* workspace, int64_t workspace_bytes,
-                                             int* err, void* stream) {
+                                             int64_t in_div, int swiglu, const void* rms_w, int rms_dtype,
+                                             float eps, void* y, int y_dtype, int64_t y_row_stride,
+                                             void* workspace, int64_t workspace_bytes, int* err, void* stream) {
   if (in_rows < 0 || n_slots < 0 || n_experts <= 0 || code_rows <= 0 || in_div <= 0) return kErrShape;
   if (k <= 0 || k % 128 != 0 || k > 8192) return kErrShape;
   if (n_slots == 0) return kOk;
@@ -462,6 +468,8 @@ extern "C" int maple_ternary_grouped_gemm_tc(const void* x, int x_dtype, int64_t
   if ((n_slots - 1) / in_div >= in_rows) return kErrBounds;
   if (x_dtype != kBF16 && x_dtype != kF32) return kErrDtype;
   if ((alpha_dtype != kBF16 && alpha_dtype != kF32) || (y_dtype != kBF16 && y_dtype != kF32)) return kErrDtype;
+  if (rms_w && rms_dtype != kBF16 && rms_dtype != kF32) return kErrDtype;
+  if (rms_w && swiglu) return kErrShape;  // the fused input norm is for plain (dense) GEMMs
   if (workspace_bytes < maple_ternary_grouped_gemm_tc_workspace_bytes(n_slots, k)) return kErrWorkspace;
   if ((reinterpret_cast<uintptr_t>(codes) | reinterpret_cast<uintptr_t>(workspace)) & 255) return kErrAlign;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || ((x_row_stride * (x_dtype == kBF16 ? 2 : 4)) & 15)) return kErrAlign;
@@ -470,14 +478,19 @@ extern "C" int maple_ternary_grouped_gemm_tc(const void* x, int x_dtype, int64_t
   int* meta = reinterpret_cast<int*>(static_cast<char*>(workspace) + (n_slots * 4 * k + 255) / 256 * 256);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int K = (int)k, iters = (K + 255) / 256;
-  const size_t esmem = (size_t)iters * 256 * sizeof(uint2) + (size_t)K * sizeof(float);
+  const size_t esmem = (size_t)iters * 256 * sizeof(uint2) + (size_t)(rms_w ? 2 : 1) * K * sizeof(float);
   cudaError_t e = cudaSuccess;
   {
-    auto kern = x_dtype == kBF16 ? fxa_plain_kernel<kBF16> : fxa_plain_kernel<kF32>;
+    void (*kern)(const void*, int64_t, const void*, float, int, const int*, int, const unsigned*, int, int8_t*,
+                 int*);
+    if (!rms_w) kern = x_dtype == kBF16 ? fxa_plain_kernel<kBF16, kF32, false> : fxa_plain_kernel<kF32, kF32, false>;
+    else if (rms_dtype == kBF16)
+      kern = x_dtype == kBF16 ? fxa_plain_kernel<kBF16, kBF16, true> : fxa_plain_kernel<kF32, kBF16, true>;
+    else kern = x_dtype == kBF16 ? fxa_plain_kernel<kBF16, kF32, true> : fxa_plain_kernel<kF32, kF32, true>;
     if (esmem > 32 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)esmem);
     if (e == cudaSuccess)
-      e = launch_k(kern, dim3((unsigned)n_slots), dim3(256), esmem, st, x, x_row_stride, K, offsets, (int)n_experts,
-                   list, (int)in_div, digits, meta);
+      e = launch_k(kern, dim3((unsigned)n_slots), dim3(256), esmem, st, x, x_row_stride, rms_w, eps, K, offsets,
+                   (int)n_experts, list, (int)in_div, digits, meta);
     if (e != cudaSuccess) return kErrCuda;
   }
   CUtensorMap tmb;
@@ -489,7 +502,7 @@ extern "C" int maple_ternary_grouped_gemm_tc(const void* x, int x_dtype, int64_t
   p.codes = codes; p.alpha = alpha; p.offsets = offsets; p.list = list; p.meta = meta; p.y = y; p.err = err;
   p.y_stride = y_row_stride; p.expert_words = code_rows * (k / 16); p.alpha_estride = code_rows;
   p.rows = (int)code_rows; p.n_out = swiglu ? (int)(code_rows / 2) : (int)code_rows;
-  p.K = K; p.nwords = (int)(k / 16);
+  p.K = K; p.nwords = (int)(k / 16); p.use_rstd = rms_w != nullptr;
   const int tiles = swiglu ? (p.n_out + 63) / 64 : (p.rows + kTcARows - 1) / kTcARows;
   const dim3 grid((unsigned)tiles, (unsigned)n_experts);
   const size_t gsmem = (size_t)kTcStages * kTcStage + 2 * (size_t)kTcSlots * 64 * sizeof(float) +

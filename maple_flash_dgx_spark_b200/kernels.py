@@ -71,6 +71,11 @@ def ternary_gemv(
             raise ValueError(f"rms_weight has {rms.numel()} elements, expected {k_in}.")
     y = out if out is not None else torch.empty(batch, n_out, device=x.device, dtype=x.dtype)
     L = lib()
+    if (use_tc_dense(batch, k_in, n_out) and packed_weight.data_ptr() % 256 == 0 and
+            (y.dim() == 1 or y.stride(-1) == 1)):
+        _grouped_tc(op, x_mat, 1, packed_weight.reshape(1, n_out, nwords), alpha.reshape(1, n_out),
+                    _dense_plan(batch, x.device), False, y.reshape(batch, n_out), rms=rms, rms_eps=rms_eps)
+        return y.reshape(*leading, n_out)
     if batch >= GEMM_MIN_ROWS and k_in <= 4096:
         frag, meta = fxa_encode(x_mat, rms, rms_eps)
         check(L.maple_ternary_gemm(ptr(frag), ptr(meta), batch, k_in, ptr(packed_weight), n_out, ptr(alpha),
@@ -208,7 +213,7 @@ def use_tc_grouped(plan: "MoePlan", k_in: int) -> bool:
             plan.n_slots >= TC_GEMM_MIN_SLOTS * max(plan.total_experts, 1))
 
 
-def _grouped_tc(op, x_rows, per, w, alpha, plan, swiglu, y):
+def _grouped_tc(op, x_rows, per, w, alpha, plan, swiglu, y, rms=None, rms_eps=1e-6):
     E, rows, nwords = w.shape
     k_in = nwords * _CODES_PER_WORD
     if x_rows.stride(-1) != 1 or (x_rows.stride(0) * x_rows.element_size()) % 16 or x_rows.data_ptr() % 16:
@@ -218,10 +223,40 @@ def _grouped_tc(op, x_rows, per, w, alpha, plan, swiglu, y):
                      device=x_rows.device)
     check(L.maple_ternary_grouped_gemm_tc(
         ptr(x_rows), dtype_code(x_rows, op), x_rows.shape[0], k_in, x_rows.stride(0), ptr(w), E, rows, ptr(alpha),
-        dtype_code(alpha, op), ptr(plan.offsets), ptr(plan.slots), plan.n_slots, per, int(swiglu), ptr(y),
-        dtype_code(y, op), y.stride(0), ptr(ws), ws.numel(), ptr(_err(x_rows.device)), stream_ptr(x_rows.device)),
-        op)
+        dtype_code(alpha, op), ptr(plan.offsets), ptr(plan.slots), plan.n_slots, per, int(swiglu), ptr(rms),
+        dtype_code(rms, op) if rms is not None else 0, float(rms_eps), ptr(y), dtype_code(y, op), y.stride(0),
+        ptr(ws), ws.numel(), ptr(_err(x_rows.device)), stream_ptr(x_rows.device)), op)
     return y
+
+
+# Dense batched GEMMs move to the tcgen05 kernel (as one expert whose plan
+# lists every row) where it measured faster than mma.sync: at least 64 rows
+# and at least 4096 output rows, so that its 128-row tiles cover the SMs
+# (QKV N=5120: 27.3 -> 20.0 us at 64 rows, 168 -> 125 us at 512; the O
+# projection, N=2048, stays on mma.sync: 23 vs 29 us at 64 rows, 159 vs 197
+# at 512).  Both paths give identical results.
+TC_DENSE_MIN_ROWS, TC_DENSE_MIN_OUT = 64, 4096
+_dense_plans: dict = {}
+
+
+def use_tc_dense(batch: int, k_in: int, n_out: int) -> bool:
+    import os
+
+    if os.environ.get("MAPLE_TC_DENSE", "1") == "0" or not _tc_gemm_enabled():
+        return False
+    if k_in % 128 or k_in > 8192:
+        return False
+    return batch >= TC_DENSE_MIN_ROWS and n_out >= TC_DENSE_MIN_OUT
+
+
+def _dense_plan(batch: int, device: torch.device) -> "MoePlan":
+    key = (batch, device.index)
+    plan = _dense_plans.get(key)
+    if plan is None:
+        offsets = torch.tensor([0, batch], dtype=torch.int32, device=device)
+        slots = torch.arange(batch, dtype=torch.int32, device=device)
+        plan = _dense_plans[key] = MoePlan(offsets, slots, 1, batch, total_experts=1)
+    return plan
 
 
 def _grouped(op, x_rows, per, w, alpha, plan, swiglu, out_rows, n_out, dtype, out=None, tc=None):

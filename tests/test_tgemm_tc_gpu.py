@@ -5,7 +5,8 @@ against the FXA digits of the activations) as the mma.sync grouped GEMM, so
 its outputs must equal that path's bit for bit -- SwiGLU (up|gate) and plain
 (down) modes, experts with no, few and several chunks of 64 routed slots, an
 out-of-range expert id (NaN row in both paths), a rank's local expert range,
-and a whole prefill through the model.
+a whole prefill through the model, and dense batched GEMMs (with the fused
+input RMSNorm) run as one expert.
 """
 
 from __future__ import annotations
@@ -129,6 +130,26 @@ def test_prefill_through_tc_gemm_equals_mma_sync(cuda, monkeypatch):
     torch.testing.assert_close(outs[1][0], outs[0][0], rtol=0, atol=0)
     for a, b in zip(outs[1][1].k + outs[1][1].v, outs[0][1].k + outs[0][1].v):
         torch.testing.assert_close(a, b, rtol=0, atol=0)
+    assert _errors(cuda) == 0
+
+
+@pytest.mark.parametrize("rows,k,n,rms", [(64, 2048, 5120, True), (512, 4096, 4096, False), (300, 2048, 5120, True),
+                                           (80, 1024, 4096, True)])
+def test_tc_dense_equals_mma_sync(cuda, K, monkeypatch, rows, k, n, rms):
+    """Dense batched GEMMs (QKV with its fused input RMSNorm, O) on the
+    tcgen05 kernel as one expert equal the mma.sync GEMM bit for bit."""
+    rs = rng(rows + n)
+    x = to_dev(randn_bf(rs, rows, k), cuda, torch.bfloat16)
+    w = to_dev(tern_packed(rs, n, k), cuda)
+    a = to_dev(alpha_bf(rs, n), cuda, torch.bfloat16)
+    rw = to_dev((1 + 0.05 * rs.standard_normal(k)).astype(np.float32), cuda) if rms else None
+    assert K.use_tc_dense(rows, k, n)
+    monkeypatch.setenv("MAPLE_TC_DENSE", "0")
+    want = K.ternary_gemv(x, w, a, rms_weight=rw)
+    monkeypatch.setenv("MAPLE_TC_DENSE", "1")
+    got = K.ternary_gemv(x, w, a, rms_weight=rw)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(got, want, rtol=0, atol=0)
     assert _errors(cuda) == 0
 
 
