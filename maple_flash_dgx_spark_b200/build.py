@@ -1,7 +1,10 @@
 """Build the sm_100a shared library ``libmaple_b200.so`` in-tree with nvcc.
 
 The library is a plain C ABI (``include/maple_b200.h``) loaded with ctypes,
-so it carries no torch or Python types and is built straight by nvcc:
+so it carries no torch or Python types and is built straight by nvcc.  Each
+``csrc/*.cu`` file is a self-contained translation unit (no device code is
+called across files), so the files compile to objects in parallel and are
+linked once:
 
     python -m maple_flash_dgx_spark_b200.build
 """
@@ -12,12 +15,14 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
 REPO = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libmaple_b200.so"
+OBJ = PKG / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -26,7 +31,6 @@ NVCC_FLAGS = [
     "-lineinfo",
     "--fmad=false",          # canonical numerics: no implicit mul+add contraction
     "-Xcompiler", "-fPIC",
-    "-shared",
     f"-I{REPO / 'include'}",
 ]
 
@@ -42,19 +46,43 @@ def sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu"))
 
 
+def _headers() -> list[Path]:
+    return sorted(CSRC.glob("*.cuh")) + [REPO / "include" / "maple_b200.h"]
+
+
 def needs_build() -> bool:
     if not LIB.exists():
         return True
     t = LIB.stat().st_mtime
-    deps = sources() + sorted(CSRC.glob("*.cuh")) + [REPO / "include" / "maple_b200.h"]
-    return any(p.stat().st_mtime > t for p in deps)
+    return any(p.stat().st_mtime > t for p in sources() + _headers())
+
+
+def _compile(src: Path, verbose: bool) -> Path:
+    obj = OBJ / (src.stem + ".o")
+    hdr_t = max(p.stat().st_mtime for p in _headers())
+    if obj.exists() and obj.stat().st_mtime > max(src.stat().st_mtime, hdr_t):
+        return obj
+    tmp = obj.with_suffix(".o.tmp")
+    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-c", str(src), "-o", str(tmp)]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, obj)
+    return obj
 
 
 def build(verbose: bool = False, force: bool = False) -> Path:
     if not force and not needs_build():
         return LIB
+    OBJ.mkdir(exist_ok=True)
+    if force:
+        for o in OBJ.glob("*.o"):
+            o.unlink()
+    srcs = sources()
+    with ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 4)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *map(str, sources()), "-o", str(tmp)]
+    cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(tmp)]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

@@ -339,6 +339,114 @@ __device__ __forceinline__ int fxa_warp_prologue2(const void* xr, int K, int ite
   return s;
 }
 
+// ----------------------------------------------------------- direct --
+// Direct prologue pieces: a thread owns whole 16-value blocks of the
+// activation row, loads them straight into registers (no shared-memory
+// staging), and once the row's shift is known writes the digit fragments of
+// its blocks into a COMPACT fragment array: 16 entries per (iteration, MMA),
+// entry 4j + t = digit j for lane (g = j, t).  Only lanes 0-15 (columns 0-3,
+// the four digits) read it; lanes 16-31 feed the zero columns 4-7 from a
+// register.  Block b (values 16b .. 16b+15) of iteration it = b / 16 is
+// exactly the pair of fragment entries (it, 2q, t) and (it, 2q+1, t) with
+// t = (b / 4) % 4 and q = b % 4, so the digits equal fxa_build's.
+template <int XT> struct XBlk { static constexpr int kChunks = XT == kBF16 ? 2 : 4; };
+
+// Load activation blocks tid, tid + NT, ... (b < K/16) into raw registers in
+// the 16-byte-vector layout widen_u4 expects.  Unaligned rows use element
+// loads packed into the same layout.
+template <int XT, int NT, int MAXB>
+__device__ __forceinline__ void xblk_issue(const void* src, int K, int tid, uint4 (&r)[MAXB][XBlk<XT>::kChunks]) {
+  constexpr int C = XBlk<XT>::kChunks;
+  const char* s8 = static_cast<const char*>(src);
+  const bool aligned = (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+#pragma unroll
+  for (int i = 0; i < MAXB; ++i) {
+    const int b = tid + i * NT;
+#pragma unroll
+    for (int c = 0; c < C; ++c) r[i][c] = make_uint4(0u, 0u, 0u, 0u);
+    if (b < (K >> 4)) {
+      if (aligned) {
+#pragma unroll
+        for (int c = 0; c < C; ++c) r[i][c] = ld_u4(s8 + (size_t)b * 16 * C + 16 * c);
+      } else {
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+          uint32_t w[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if constexpr (XT == kBF16) {
+              const uint16_t* h = reinterpret_cast<const uint16_t*>(s8) + (size_t)b * 16 + 8 * c + 2 * q;
+              w[q] = static_cast<uint32_t>(h[0]) | (static_cast<uint32_t>(h[1]) << 16);
+            } else {
+              w[q] = reinterpret_cast<const uint32_t*>(s8)[(size_t)b * 16 + 4 * c + q];
+            }
+          }
+          r[i][c] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+  }
+}
+
+// The 16 fp32 values of one raw block.
+template <int XT>
+__device__ __forceinline__ void xblk_values(const uint4 (&r)[XBlk<XT>::kChunks], float (&v)[16]) {
+  constexpr int C = XBlk<XT>::kChunks;
+#pragma unroll
+  for (int c = 0; c < C; ++c) widen_u4<XT>(r[c], v + c * (16 / C));
+}
+
+// Write the compact fragment entries of block b (values v, already scaled
+// like the contraction's input) at shift s; adds its plain digits to raws.
+__device__ __forceinline__ void fxa_block_encode(const float (&v)[16], int b, int s, bool bad, uint2* frag,
+                                                 int (&raws)[4]) {
+  const int it = b >> 4, t = (b >> 2) & 3, q = b & 3;
+  uint32_t u[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) u[e] = static_cast<uint32_t>((bad ? 0 : fxa_enc(v[e], s)) + kFxaOffset);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    // entry (it, 2q + h, t): values 2h + {0, 4, 8, 12} (low word), 2h + 1 + {0, 4, 8, 12} (high word)
+    uint2* dst = frag + (it * 8 + 2 * q + h) * 16 + t;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t w0 = raw_digits(u[2 * h], u[2 * h + 4], u[2 * h + 8], u[2 * h + 12], j);
+      const uint32_t w1 = raw_digits(u[2 * h + 1], u[2 * h + 5], u[2 * h + 9], u[2 * h + 13], j);
+      raws[j] = static_cast<int>(__dp4a(w0, 0x01010101u, static_cast<unsigned>(raws[j])));
+      raws[j] = static_cast<int>(__dp4a(w1, 0x01010101u, static_cast<unsigned>(raws[j])));
+      dst[4 * j] = make_uint2(signed_digits(w0), signed_digits(w1));
+    }
+  }
+}
+
+// contract_tile2 over a compact fragment array (16 entries per MMA).
+template <int NI>
+__device__ __forceinline__ void contract_tile2c(const uint4 (&wa)[NI], const uint4 (&wb)[NI], int iters,
+                                                const uint2* frag, int lane, int (&acc)[4]) {
+  int a2[4] = {0, 0, 0, 0};
+  const bool rd = lane < 16;
+#pragma unroll
+  for (int i = 0; i < NI; ++i) {
+    if (i < iters) {
+      const uint32_t ga[4] = {wa[i].x, wa[i].y, wa[i].z, wa[i].w};
+      const uint32_t gb[4] = {wb[i].x, wb[i].y, wb[i].z, wb[i].w};
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int q = m >> 1, sh = 4 * (m & 1);
+        const uint32_t a0 = (ga[q] >> sh) & 0x03030303u;
+        const uint32_t a2r = (ga[q] >> (sh + 2)) & 0x03030303u;
+        const uint32_t a1 = (gb[q] >> sh) & 0x03030303u;
+        const uint32_t a3 = (gb[q] >> (sh + 2)) & 0x03030303u;
+        const uint2 bf = rd ? frag[(i * 8 + m) * 16 + lane] : make_uint2(0u, 0u);
+        if (m & 1) mma_u8s8(a2, a0, a1, a2r, a3, bf.x, bf.y);
+        else mma_u8s8(acc, a0, a1, a2r, a3, bf.x, bf.y);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) acc[j] += a2[j];
+}
+
 // Contraction with two independent accumulator chains (even / odd MMAs),
 // summed at the end (exact integers).  Same tile semantics as contract_tile.
 template <int NI>

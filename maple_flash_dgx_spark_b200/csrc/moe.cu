@@ -274,9 +274,8 @@ __global__ void __launch_bounds__(256, NI == 4 ? 3 : 1) down_sum_kernel(DownPara
   const int g = lane >> 2, t = lane & 3;
   const int tok = blockIdx.y;
   const int row_g = blockIdx.x * 16 + g, row_h = row_g + 8;
-  const size_t per_warp = (size_t)p.iters * 256 * sizeof(uint2) + (size_t)p.K * sizeof(float);
-  uint2* frag = reinterpret_cast<uint2*>(smem + warp * per_warp);
-  float* xsm = reinterpret_cast<float*>(smem + warp * per_warp + (size_t)p.iters * 256 * sizeof(uint2));
+  // compact digit fragments of this warp's slot row (fxa.cuh, direct form)
+  uint2* frag = reinterpret_cast<uint2*>(smem + warp * ((size_t)p.iters * 128 * sizeof(uint2)));
 
   // Routing ids come from two launches back (complete once the previous
   // launch has passed its own wait), so the expert rows load before waiting.
@@ -314,10 +313,39 @@ __global__ void __launch_bounds__(256, NI == 4 ? 3 : 1) down_sum_kernel(DownPara
     }
     const void* hr = static_cast<const char*>(p.h) +
                      (tok * p.h_tok_stride + warp * p.h_slot_stride) * (XT == kBF16 ? 2 : 4);
-    int tot[4];
-    const int s = fxa_warp_prologue2<XT>(hr, p.K, p.iters, xsm, frag, tot);
+    // Direct FXA prologue on one warp: lane l owns the 16-value blocks l,
+    // l + 32, ... of the slot row in registers; the warp max gives the shift
+    // and each lane writes its blocks' digit fragments (same digits, shift and
+    // totals as fxa_warp_prologue2).
+    constexpr int MAXB = NI / 2;  // K <= NI * 256 values = NI * 16 blocks over 32 lanes
+    uint4 xb[MAXB][XBlk<XT>::kChunks];
+    xblk_issue<XT, 32, MAXB>(hr, p.K, lane, xb);
+    unsigned am = 0;
+#pragma unroll
+    for (int i = 0; i < MAXB; ++i) {
+      if (lane + 32 * i < (p.K >> 4)) {
+        float v[16];
+        xblk_values<XT>(xb[i], v);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) am = max(am, __float_as_uint(v[q]) & 0x7fffffffu);
+      }
+    }
+    const int s = fxa_shift(__reduce_max_sync(0xffffffffu, am));
+    int tot[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < MAXB; ++i) {
+      const int b = lane + 32 * i;
+      if (b < (p.K >> 4)) {
+        float v[16];
+        xblk_values<XT>(xb[i], v);
+        fxa_block_encode(v, b, s, s == kFxaNonFinite, frag, tot);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tot[j] = __reduce_add_sync(0xffffffffu, tot[j]) - 64 * p.K;
+    __syncwarp();
     int acc[4] = {0, 0, 0, 0};
-    contract_tile2<NI>(wa, wb, p.iters, frag, lane, acc);
+    contract_tile2c<NI>(wa, wb, p.iters, frag, lane, acc);
     long long Sg, Sh;
     combine_digits(acc, tot, t, Sg, Sh);
     if (t == 0) {
@@ -486,7 +514,7 @@ extern "C" int maple_add_norm_router_topk(const void* x, const void* y, int x_dt
 namespace {
 template <int XT, int AT, int MODE>
 cudaError_t launch_down(const DownParams& p, int T, cudaStream_t st) {
-  const size_t per_warp = (size_t)p.iters * 256 * sizeof(uint2) + (size_t)p.K * sizeof(float);
+  const size_t per_warp = (size_t)p.iters * 128 * sizeof(uint2);  // compact fragments
   const size_t smem = per_warp * kDownMaxTopk;
   auto kern = p.iters <= 4 ? down_sum_kernel<XT, AT, MODE, 4> : down_sum_kernel<XT, AT, MODE, kDownMaxIters>;
   if (smem > 32 * 1024) {

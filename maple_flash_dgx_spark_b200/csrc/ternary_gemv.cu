@@ -215,12 +215,23 @@ __global__ void __launch_bounds__(128) ternary_gemv_kernel(TGemvParams p) {
 // ---------------------------------------------------------------------------
 // v2: one CTA covers all of K.  8 warps = WM row tiles x WK K-slices; the
 // K-slices' exact int32 partials are summed in shared memory, so no
-// workspace is needed.  The FXA prologue is the fast one (fxa_prologue).
+// workspace is needed.
+//
+// Activation prologue (the direct form, fxa.cuh): each thread loads whole
+// 16-value blocks of the row into registers right after the dependency wait,
+// one block-wide max gives the FXA shift, and each thread writes the compact
+// digit fragments of its own blocks; a second barrier publishes them.  The
+// digits, shift, digit totals and the R128 sum of squares (fused RMSNorm) are
+// the same values fxa_prologue computes, so the results are bit-identical.
 template <int XT, int AT, int RT, bool RMS, int MODE, int WM, int WK, int NI>
 __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
-  constexpr int NT = 32 * WM * WK;
+  constexpr int NT = 32 * WM * WK, NW = NT / 32;
+  constexpr int MAXB = (8192 / 16 + NT - 1) / NT;  // activation blocks per thread (K <= 8192)
+  constexpr int C = XBlk<XT>::kChunks;
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ FxaBlock fb;
+  __shared__ unsigned s_amax[NW];
+  __shared__ int s_raw[NW][4];
+  __shared__ float s_part[RMS ? 128 : 1];
   __shared__ int red[WK > 1 ? WK - 1 : 1][WM][32][4];
   __shared__ float s_val[16 * WM];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -231,19 +242,18 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
   const int ipw = (iters_total + WK - 1) / WK;
   const int it0 = wk * ipw;
   const int my_iters = max(0, min(ipw, iters_total - it0));
-  uint2* frag = reinterpret_cast<uint2*>(smem);
-  float* xsm = reinterpret_cast<float*>(smem + (size_t)iters_total * 256 * sizeof(uint2));
-  float* wsm = xsm + p.K;
+  uint2* frag = reinterpret_cast<uint2*>(smem);  // compact: iters_total * 128 entries
+  float* wsm = reinterpret_cast<float*>(smem + (size_t)iters_total * 128 * sizeof(uint2));
 
   const bool dense = p.ids == nullptr;
   const void* xr = static_cast<const char*>(p.x) + (z / p.x_div) * p.x_stride * (XT == kBF16 ? 2 : 4);
-  uint4 x0 = make_uint4(0u, 0u, 0u, 0u);
+  uint4 xb[MAXB][C];
   if (!dense) {
     pdl_wait();
     pdl_trigger();
     // The activation row comes from the previous launch like the ids: its
     // loads go out before the expert rows', so they do not queue behind them.
-    x0 = stage_row_issue<XT, NT>(xr, p.K, tid);
+    xblk_issue<XT, NT, MAXB>(xr, p.K, tid, xb);
   }
   int e = 0;
   bool bad_id = false;
@@ -286,21 +296,73 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
     if (ok_h) al_h = load_f<AT>(alpha, row_h);
   }
   if constexpr (RMS) {
-    if (dense) stage_row<RT, NT, (8192 * 4 / 16 + NT - 1) / NT>(p.rms_w, p.K, wsm, tid);
+    stage_row<RT, NT, (8192 * 4 / 16 + NT - 1) / NT>(p.rms_w, p.K, wsm, tid);
+    __syncthreads();
   }
   if (dense) {
     pdl_wait();
     pdl_trigger();
-  } else {
-    stage_row_finish<XT, NT>(xr, p.K, xsm, tid, x0);
+    xblk_issue<XT, NT, MAXB>(xr, p.K, tid, xb);
   }
-  fxa_prologue<XT, RT, RMS, 2, NT>(xr, p.rms_w, p.K, p.eps, 0, iters_total, xsm, wsm, frag, fb, nullptr, 0, dense,
-                                   !dense);
-  const int s = fb.s;
-  const bool nan_out = (s == kFxaNonFinite) || bad_id;
+  // Fused RMSNorm: the R128 partial sums of squares of the raw row (thread
+  // tid < 128 sums k = tid, tid + 128, ... in order), loaded beside the blocks.
+  float ss = 0.0f;
+  if constexpr (RMS) {
+    if (tid < 128)
+      for (int k = tid; k < p.K; k += 128) {
+        const float xv = load_f<XT>(xr, k);
+        ss = __fmaf_rn(xv, xv, ss);
+      }
+  }
+  unsigned am = 0;
+#pragma unroll
+  for (int i = 0; i < MAXB; ++i) {
+    const int b = tid + i * NT;
+    if (b < (p.K >> 4)) {
+      float v[16];
+      xblk_values<XT>(xb[i], v);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        if constexpr (RMS) v[q] = __fmul_rn(v[q], wsm[16 * b + q]);
+        am = max(am, __float_as_uint(v[q]) & 0x7fffffffu);
+      }
+    }
+  }
+  am = __reduce_max_sync(0xffffffffu, am);
+  if (lane == 0) s_amax[warp] = am;
+  if constexpr (RMS) {
+    if (tid < 128) s_part[tid] = ss;
+  }
+  __syncthreads();
+  unsigned amax = 0;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) amax = max(amax, s_amax[w]);
+  const int s = fxa_shift(amax);
+  const bool bad = (s == kFxaNonFinite);
+  int raws[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int i = 0; i < MAXB; ++i) {
+    const int b = tid + i * NT;
+    if (b < (p.K >> 4)) {
+      float v[16];
+      xblk_values<XT>(xb[i], v);
+      if constexpr (RMS) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) v[q] = __fmul_rn(v[q], wsm[16 * b + q]);
+      }
+      fxa_block_encode(v, b, s, bad, frag, raws);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    raws[j] = __reduce_add_sync(0xffffffffu, raws[j]);
+    if (lane == 0) s_raw[warp][j] = raws[j];
+  }
+  __syncthreads();
+  const bool nan_out = bad || bad_id;
 
   int acc[4] = {0, 0, 0, 0};
-  contract_tile2<NI>(wa, wb, my_iters, frag + (size_t)it0 * 256, lane, acc);
+  contract_tile2c<NI>(wa, wb, my_iters, frag + (size_t)it0 * 128, lane, acc);
   if (wk > 0) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) red[wk - 1][wm][lane][j] = acc[j];
@@ -312,12 +374,22 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
     for (int w2 = 0; w2 < WK - 1; ++w2)
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[j] += red[w2][wm][lane][j];
+    int tot[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int r = 0;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) r += s_raw[w][j];
+      tot[j] = r - 64 * p.K;  // balanced digit sums over the row's K values
+    }
+    float rstd = 1.0f;
+    if constexpr (RMS) rstd = rstd_of(r128_smem_finish(s_part, lane), p.K, p.eps);
     long long Sg, Sh;
-    combine_digits(acc, fb.tot, t, Sg, Sh);
+    combine_digits(acc, tot, t, Sg, Sh);
     if (t == 0) {
       auto value = [&](float a, long long S) -> float {
         float v = nan_out ? __int_as_float(0x7fc00000) : fxa_value(S, s);
-        if constexpr (RMS) v = __fmul_rn(v, fb.rstd);
+        if constexpr (RMS) v = __fmul_rn(v, rstd);
         return __fmul_rn(v, a);
       };
       if constexpr (MODE == kSwiglu) {
@@ -395,7 +467,7 @@ cudaError_t dispatch(const TGemvParams& p, int x_dtype, int alpha_dtype, int rms
 template <int XT, int AT, int RT, bool RMS, int MODE, int WM, int WK, int NI>
 cudaError_t launch_v2(const TGemvParams& p, int Z, cudaStream_t st) {
   const int iters_total = (p.nwords + 15) / 16;
-  const size_t smem = (size_t)iters_total * 256 * sizeof(uint2) + 2 * (size_t)p.K * sizeof(float);
+  const size_t smem = (size_t)iters_total * 128 * sizeof(uint2) + (RMS ? (size_t)p.K * sizeof(float) : 0);
   const int per_cta = (MODE == kSwiglu) ? 8 * WM : 16 * WM;
   dim3 grid((p.n_out + per_cta - 1) / per_cta, 1, Z);
   auto kern = tgemv2_kernel<XT, AT, RT, RMS, MODE, WM, WK, NI>;
