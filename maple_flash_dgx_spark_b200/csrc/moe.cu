@@ -64,7 +64,6 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
   __shared__ float s_logit[kMaxE];  // CL: every expert's logit (rank 0's copy is filled)
   __shared__ int s_last;
   __shared__ float s_part[128];
-  __shared__ float s_rstd;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tok = blockIdx.y;
   const int e0 = blockIdx.x * kRouterWarps;
@@ -101,30 +100,40 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
   pdl_trigger();
   const int es = XT == kBF16 ? 2 : 4;
   const char* xr = static_cast<const char*>(p.x) + tok * p.x_stride * es;
-  stage_row<XT, 256, 2>(xr, p.K, xs, tid);
-  if constexpr (FUSE) stage_row<XT, 256, 2>(static_cast<const char*>(p.y) + tok * p.x_stride * es, p.K, ys, tid);
-  __syncthreads();
   if constexpr (FUSE) {
-    // v = x + y, sum of squares by 128 threads (thread j: elements j, j+128, ...), R128 finish
-    float ss = 0.0f;
+    // v = x + y straight from the two rows: thread j < 128 owns elements j,
+    // j + 128, ... (its R128 sum-of-squares partial, in order) and keeps v in
+    // xs; after one barrier every warp finishes the R128 sum itself.
+    (void)ys;
+    const char* yr = static_cast<const char*>(p.y) + tok * p.x_stride * es;
     if (tid < 128) {
-      for (int k = tid; k < p.K; k += 128) {
-        const float v = __fadd_rn(xs[k], ys[k]);
-        ss = __fmaf_rn(v, v, ss);
+      float ss = 0.0f;
+      for (int k0 = tid; k0 < p.K; k0 += 128 * 8) {
+        float xv[8], yv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int k = k0 + 128 * u;
+          xv[u] = k < p.K ? load_f<XT>(xr, k) : 0.0f;
+          yv[u] = k < p.K ? load_f<XT>(yr, k) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int k = k0 + 128 * u;
+          if (k < p.K) {
+            const float v = __fadd_rn(xv[u], yv[u]);
+            ss = __fmaf_rn(v, v, ss);
+            xs[k] = v;
+          }
+        }
       }
       s_part[tid] = ss;
     }
     __syncthreads();
-    if (tid < 32) {
-      const float tot = r128_smem_finish(s_part, tid);
-      if (tid == 0) s_rstd = rstd_of(tot, p.K, p.eps);
-    }
-    __syncthreads();
-    const float rstd = s_rstd;
+    const float rstd = rstd_of(r128_smem_finish(s_part, lane), p.K, p.eps);
     char* res = static_cast<char*>(p.residual_out) + tok * p.x_stride * es;
     char* nrm = static_cast<char*>(p.normed_out) + tok * p.x_stride * es;
     for (int k = tid; k < p.K; k += 256) {
-      const float v = __fadd_rn(xs[k], ys[k]);
+      const float v = xs[k];
       const float nv = __fmul_rn(__fmul_rn(v, rstd), ws[k]);
       float nq = nv;
       if constexpr (XT == kBF16) nq = bf16_to_f32(f32_to_bf16(nv));
@@ -134,6 +143,9 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
       }
       xs[k] = nq;  // the router reads the stored (rounded) normed row
     }
+    __syncthreads();
+  } else {
+    stage_row<XT, 256, 2>(xr, p.K, xs, tid);
     __syncthreads();
   }
   if constexpr (CL) cluster_wait_acquire();  // every CTA of the cluster has started

@@ -223,19 +223,24 @@ __global__ void __launch_bounds__(32 * WM * WK, NBUF == 1 ? 2 : 1) tgemm_kernel(
     mbar_init(&bar[1], 1);
   }
   __syncthreads();
-  // Stage chunk c into buffer c & 1 (thread 0).
+  // Stage chunk c into buffer c % NBUF (thread 0).  The chunk's slot ids are
+  // loaded together (one L2 round trip, not one per slot) before the copies
+  // that depend on them are issued.
   auto issue = [&](int c) {
     const int b = c % NBUF;
     const int n = min(RC, count - c * RC);
-    unsigned bytes = 0;
-    for (int i = 0; i < n; ++i) {
-      s_slot[b][i] = grouped ? p.list[first + c * RC + i] : static_cast<unsigned>(first + c * RC + i);
-      bytes += (unsigned)(rowu2 * sizeof(uint2)) + kMetaInts * 4;
-    }
-    for (int i = n; i < RC; ++i) s_slot[b][i] = 0xffffffffu;
-    mbar_expect_tx(&bar[b], bytes);
-    for (int i = 0; i < n; ++i) {
-      const unsigned slot = s_slot[b][i];
+    unsigned sl[RC];
+#pragma unroll
+    for (int i = 0; i < RC; ++i)
+      sl[i] = i < n ? (grouped ? p.list[first + c * RC + i] : static_cast<unsigned>(first + c * RC + i))
+                    : 0xffffffffu;
+#pragma unroll
+    for (int i = 0; i < RC; ++i) s_slot[b][i] = sl[i];
+    mbar_expect_tx(&bar[b], (unsigned)n * ((unsigned)(rowu2 * sizeof(uint2)) + kMetaInts * 4));
+#pragma unroll
+    for (int i = 0; i < RC; ++i) {
+      if (i >= n) break;
+      const unsigned slot = sl[i];
       const int64_t in_row = grouped ? (int64_t)(slot & ~kBadSlot) / p.in_div : (int64_t)slot;
       bulk_g2s(buf0 + ((size_t)b * RC + i) * rowu2, p.frag + in_row * rowu2, (unsigned)(rowu2 * sizeof(uint2)),
                &bar[b]);
