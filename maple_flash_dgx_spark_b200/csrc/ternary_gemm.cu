@@ -274,23 +274,29 @@ __global__ void __launch_bounds__(32 * WM * WK, NBUF == 1 ? 2 : 1) tgemm_kernel(
 #pragma unroll
     for (int q = 0; q < NP; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0;
     const int half = lane >> 4, l16 = lane & 15;
+    // One code word of each row (q4) per pass: with two CTAs per SM (NBUF 1,
+    // 128 registers) a fully unrolled pass hoists every fragment load and
+    // spills; a rolled q4 loop keeps 8 fragment registers live.
 #pragma unroll
     for (int i = 0; i < NI; ++i) {
       if (i < my_iters) {
-        const uint32_t ga[4] = {wa[i].x, wa[i].y, wa[i].z, wa[i].w};
-        const uint32_t gb[4] = {wb[i].x, wb[i].y, wb[i].z, wb[i].w};
+#pragma unroll(NBUF == 1 ? 1 : 4)
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const uint32_t wga = q4 == 0 ? wa[i].x : q4 == 1 ? wa[i].y : q4 == 2 ? wa[i].z : wa[i].w;
+          const uint32_t wgb = q4 == 0 ? wb[i].x : q4 == 1 ? wb[i].y : q4 == 2 ? wb[i].z : wb[i].w;
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          const int q4 = m >> 1, sh = 4 * (m & 1);
-          const uint32_t a0 = (ga[q4] >> sh) & 0x03030303u;
-          const uint32_t a2 = (ga[q4] >> (sh + 2)) & 0x03030303u;
-          const uint32_t a1 = (gb[q4] >> sh) & 0x03030303u;
-          const uint32_t a3 = (gb[q4] >> (sh + 2)) & 0x03030303u;
-          const int ent = ((it0 + i) * 8 + m) * 16 + l16;
+          for (int hm = 0; hm < 2; ++hm) {
+            const int sh = 4 * hm;
+            const uint32_t a0 = (wga >> sh) & 0x03030303u;
+            const uint32_t a2 = (wga >> (sh + 2)) & 0x03030303u;
+            const uint32_t a1 = (wgb >> sh) & 0x03030303u;
+            const uint32_t a3 = (wgb >> (sh + 2)) & 0x03030303u;
+            const int ent = ((it0 + i) * 8 + 2 * q4 + hm) * 16 + l16;
 #pragma unroll
-          for (int q = 0; q < NP; ++q) {
-            const uint2 bv = fr[(size_t)(2 * q + half) * rowu2 + ent];
-            mma_u8s8(acc[q], a0, a1, a2, a3, bv.x, bv.y);
+            for (int q = 0; q < NP; ++q) {
+              const uint2 bv = fr[(size_t)(2 * q + half) * rowu2 + ent];
+              mma_u8s8(acc[q], a0, a1, a2, a3, bv.x, bv.y);
+            }
           }
         }
       }
