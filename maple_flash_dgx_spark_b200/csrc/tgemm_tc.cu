@@ -192,8 +192,9 @@ __device__ __forceinline__ bool sync_expanders_and(bool v) {
 // warp halves); warp 10 lane 0 streams the packed code tiles from HBM by TMA
 // into a ring of 8 K blocks (32 KB in flight per SM hides the DRAM latency);
 // warp 8 lane 0 loads the digit tiles; warp 9 lane 0 issues the MMAs.  Per
-// code slot: cfull (TMA bytes), cempty (256 expander arrivals); per MMA stage:
-// full (TMA bytes), afull (256 expander arrivals), empty (tcgen05.commit); per
+// code slot: cfull (TMA bytes), cempty (8 expander-warp arrivals); per MMA
+// stage: full (TMA bytes), afull (8 expander-warp arrivals), empty
+// (tcgen05.commit); per
 // chunk of 64 slots: accfull (commit after its last MMA), accempty (256
 // epilogue arrivals).  N = 64 x the digit boxes the chunk needs, so decode-
 // sized groups (a few slots per expert) run narrow MMAs.  The dependent launch
@@ -226,14 +227,14 @@ __global__ void __launch_bounds__(352, 1) tgemm_tc_kernel(TcGemmParams p, const 
   if (tid == 0) {
     for (int i = 0; i < kTcStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&afull[i], kTcExp);
+      mbar_init(&afull[i], kTcExp / 32);  // one arrival per expander warp
       mbar_init(&empty[i], 1);
     }
     mbar_init(&accfull, 1);
     mbar_init(&accempty, kTcExp);
     for (int i = 0; i < kTcCodeSlots; ++i) {
       mbar_init(&cfull[i], 1);
-      mbar_init(&cempty[i], kTcExp);
+      mbar_init(&cempty[i], kTcExp / 32);
     }
     s_fail = 0;
   }
@@ -359,7 +360,6 @@ __global__ void __launch_bounds__(352, 1) tgemm_tc_kernel(TcGemmParams p, const 
         }
         const uint4 wa = aok ? *reinterpret_cast<const uint4*>(codes_s + cs * kTcCodeBytes + m * 32 + hh * 16)
                              : make_uint4(0, 0, 0, 0);
-        mbar_arrive(&cempty[cs]);
         unsigned char* arow_s = smem + st * kTcStage + (m >> 3) * 1024 + (m & 7) * 128;
         const uint32_t ws[4] = {wa.x, wa.y, wa.z, wa.w};
 #pragma unroll
@@ -368,7 +368,14 @@ __global__ void __launch_bounds__(352, 1) tgemm_tc_kernel(TcGemmParams p, const 
           *reinterpret_cast<uint4*>(arow_s + ((u ^ (m & 7)) << 4)) = expand_codes16(ws[i]);
         }
         fence_proxy_async_smem();  // the tensor core reads these bytes through the async proxy
-        mbar_arrive(&afull[st]);
+        // One arrival per warp (not per thread) on each barrier: the warp's
+        // code reads were consumed by the expansion above and its stores are
+        // ordered before lane 0's release by the warp barrier.
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&cempty[cs]);
+          mbar_arrive(&afull[st]);
+        }
       }
       if (!ok || !sync_expanders_and(mbar_wait_bounded(&accfull, (unsigned)(c & 1)))) {
         ok = false;

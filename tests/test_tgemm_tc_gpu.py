@@ -52,6 +52,7 @@ def _both(K, monkeypatch, fn):
 @pytest.mark.parametrize("tokens,topk,E,inter,H,skew", [
     (100, 4, 8, 256, 2048, True),
     (64, 8, 64, 1024, 2048, False),
+    (64, 8, 64, 512, 1024, True),   # decode-sized, skewed: some experts need several 16-slot chunks
     (300, 2, 4, 128, 256, True),
 ])
 def test_tc_swiglu_equals_mma_sync(cuda, K, monkeypatch, tokens, topk, E, inter, H, skew):
@@ -73,7 +74,8 @@ def test_tc_swiglu_equals_mma_sync(cuda, K, monkeypatch, tokens, topk, E, inter,
     assert K.lib() is not None and _errors(cuda) == 0
 
 
-@pytest.mark.parametrize("tokens,topk,E,inter,H", [(96, 4, 8, 1024, 2048), (40, 8, 16, 256, 512)])
+@pytest.mark.parametrize("tokens,topk,E,inter,H", [(96, 4, 8, 1024, 2048), (40, 8, 16, 256, 512),
+                                                   (64, 8, 64, 1024, 2048)])
 def test_tc_down_equals_mma_sync(cuda, K, monkeypatch, tokens, topk, E, inter, H):
     rs = rng(7 * tokens + E)
     h = to_dev(randn_bf(rs, tokens, topk, inter, scale=0.5), cuda, torch.bfloat16)
