@@ -226,12 +226,15 @@ int maple_ternary_expert_gemv(const void* x, int x_dtype, int64_t x_row_stride, 
  * ternary_expert_swiglu and linear.py:55 PackedTernaryExperts.swiglu.
  * codes [n_experts, 2*inter, k/16] (rows [0, inter) up, [inter, 2*inter) gate),
  * expert_ids [tokens, topk]; y [tokens*topk, inter]:
- *   y = clamp(up, -7, 7) * min(gate, 7) * sigmoid(min(gate, 7)). */
+ *   y = clamp(up, -7, 7) * min(gate, 7) * sigmoid(min(gate, 7)).
+ * err: the device error word (bit 0 = a bounded wait on the bulk-staged
+ * expert rows ran out); nullptr keeps per-thread row loads. */
 int64_t maple_ternary_expert_swiglu_workspace_bytes(int64_t slots, int64_t inter, int64_t k);
 int maple_ternary_expert_swiglu(const void* x, int x_dtype, int64_t x_row_stride, const int32_t* expert_ids,
                                 int64_t tokens, int64_t topk, int64_t k, const uint32_t* codes,
                                 int64_t n_experts, int64_t inter, const void* alpha, int alpha_dtype, void* y,
-                                int64_t y_row_stride, void* workspace, int64_t workspace_bytes, void* stream);
+                                int64_t y_row_stride, void* workspace, int64_t workspace_bytes, int* err,
+                                void* stream);
 
 /* Down projection of every top-k slot fused with the weighted combine and the
  * residual add.  maple_ternary_expert_down_reduce has the reference model's

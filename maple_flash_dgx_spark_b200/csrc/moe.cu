@@ -108,16 +108,16 @@ __global__ void __launch_bounds__(256) router_kernel(RouterParams p) {
     const char* yr = static_cast<const char*>(p.y) + tok * p.x_stride * es;
     if (tid < 128) {
       float ss = 0.0f;
-      for (int k0 = tid; k0 < p.K; k0 += 128 * 8) {
-        float xv[8], yv[8];
+      for (int k0 = tid; k0 < p.K; k0 += 128 * 16) {  // one memory round trip for K <= 2048
+        float xv[16], yv[16];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 16; ++u) {
           const int k = k0 + 128 * u;
           xv[u] = k < p.K ? load_f<XT>(xr, k) : 0.0f;
           yv[u] = k < p.K ? load_f<XT>(yr, k) : 0.0f;
         }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 16; ++u) {
           const int k = k0 + 128 * u;
           if (k < p.K) {
             const float v = __fadd_rn(xv[u], yv[u]);

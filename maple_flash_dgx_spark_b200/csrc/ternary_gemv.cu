@@ -21,6 +21,7 @@
 // warps 2-3 the gate rows I+n.  grid.y splits K only when K > 2048; split
 // partials are exact int32 and the last CTA of a row group (atomic ticket)
 // finishes the rows.  grid.z = activation row (token, or token x top-k slot).
+#include "bulk.cuh"
 #include "fxa.cuh"
 #include "launch.cuh"
 
@@ -48,6 +49,8 @@ struct TGemvParams {
   int n_experts;
   int K, nwords, ks, iters;
   float eps;
+  int* err;                 // device error word (bounded waits), or nullptr
+  int bulk_w;               // SwiGLU expert rows staged by bulk copies (K <= 2048, WM = 4)
 };
 
 template <int XT, int AT, int RT, bool RMS, int MODE>
@@ -234,6 +237,7 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
   __shared__ float s_part[RMS ? 128 : 1];
   __shared__ int red[WK > 1 ? WK - 1 : 1][WM][32][4];
   __shared__ float s_val[16 * WM];
+  __shared__ uint64_t wbar;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int wm = warp % WM, wk = warp / WM;
   const int g = lane >> 2, t = lane & 3;
@@ -244,6 +248,14 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
   const int my_iters = max(0, min(ipw, iters_total - it0));
   uint2* frag = reinterpret_cast<uint2*>(smem);  // compact: iters_total * 128 entries
   float* wsm = reinterpret_cast<float*>(smem + (size_t)iters_total * 128 * sizeof(uint2));
+  // Bulk-staged expert rows (SwiGLU, bulk_w): the CTA's 8*WM up rows, then its
+  // 8*WM gate rows, each row nwords words.  The rows depend on the routing ids
+  // of the previous launch, so they are fetched after the dependency wait; two
+  // bulk copies put the whole 32 KB tile in flight at once, where per-thread
+  // 16-byte loads stall at issue once the SM's outstanding requests fill up.
+  unsigned char* wtile = smem + (size_t)iters_total * 128 * sizeof(uint2) + (RMS ? (size_t)p.K * sizeof(float) : 0);
+  const bool bulkw = MODE == kSwiglu && p.bulk_w != 0;
+  const unsigned rowb = (unsigned)p.nwords * 4u;
 
   const bool dense = p.ids == nullptr;
   const void* xr = static_cast<const char*>(p.x) + (z / p.x_div) * p.x_stride * (XT == kBF16 ? 2 : 4);
@@ -274,12 +286,20 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
   const int lim = (MODE == kSwiglu) ? base + p.n_out : p.rows;
   const bool ok_g = row_g < lim, ok_h = row_h < lim;
 
+  if (bulkw && tid == 0) {
+    const int n0 = blockIdx.x * (8 * WM), nrows = min(8 * WM, p.n_out - n0);
+    mbar_init(&wbar, 1);
+    mbar_expect_tx(&wbar, 2u * (unsigned)nrows * rowb);
+    bulk_g2s(wtile, codes + (int64_t)n0 * p.nwords, (unsigned)nrows * rowb, &wbar);
+    bulk_g2s(wtile + (size_t)(8 * WM) * rowb, codes + (int64_t)((p.rows >> 1) + n0) * p.nwords,
+             (unsigned)nrows * rowb, &wbar);
+  }
   uint4 wa[NI], wb[NI];
 #pragma unroll
   for (int i = 0; i < NI; ++i) {
     wa[i] = make_uint4(0, 0, 0, 0);
     wb[i] = make_uint4(0, 0, 0, 0);
-    if (i < my_iters) {
+    if (i < my_iters && !bulkw) {
       const int word = (it0 + i) * 16 + 4 * t;
       if (word < p.nwords) {
         if (ok_g) wa[i] = ld_stream_u4(codes + (int64_t)row_g * p.nwords + word);
@@ -360,6 +380,27 @@ __global__ void __launch_bounds__(32 * WM * WK) tgemv2_kernel(TGemvParams p) {
   }
   __syncthreads();
   const bool nan_out = bad || bad_id;
+  if (bulkw) {
+    // the staged rows: a wait that runs out is reported, lets the copies
+    // land (bounded) and ends the CTA before anything is read
+    const bool ready = mbar_wait_bounded(&wbar, 0);
+    if (__syncthreads_or(!ready)) {
+      if (tid == 0 && p.err != nullptr) atomicOr(p.err, kErrFlagTimeout);
+      mbar_wait_bounded(&wbar, 0);
+      return;
+    }
+    const int lr = (wm < WM / 2 ? 0 : 8 * WM) + 16 * (wm % (WM / 2)) + g;  // local row of row_g
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      if (i < my_iters) {
+        const int word = (it0 + i) * 16 + 4 * t;
+        if (word < p.nwords) {
+          if (ok_g) wa[i] = *reinterpret_cast<const uint4*>(wtile + (size_t)lr * rowb + 4 * word);
+          if (ok_h) wb[i] = *reinterpret_cast<const uint4*>(wtile + (size_t)(lr + 8) * rowb + 4 * word);
+        }
+      }
+    }
+  }
 
   int acc[4] = {0, 0, 0, 0};
   contract_tile2c<NI>(wa, wb, my_iters, frag + (size_t)it0 * 128, lane, acc);
@@ -467,7 +508,8 @@ cudaError_t dispatch(const TGemvParams& p, int x_dtype, int alpha_dtype, int rms
 template <int XT, int AT, int RT, bool RMS, int MODE, int WM, int WK, int NI>
 cudaError_t launch_v2(const TGemvParams& p, int Z, cudaStream_t st) {
   const int iters_total = (p.nwords + 15) / 16;
-  const size_t smem = (size_t)iters_total * 128 * sizeof(uint2) + (RMS ? (size_t)p.K * sizeof(float) : 0);
+  const size_t smem = (size_t)iters_total * 128 * sizeof(uint2) + (RMS ? (size_t)p.K * sizeof(float) : 0) +
+                      (p.bulk_w ? (size_t)(16 * WM) * p.nwords * 4 : 0);
   const int per_cta = (MODE == kSwiglu) ? 8 * WM : 16 * WM;
   dim3 grid((p.n_out + per_cta - 1) / per_cta, 1, Z);
   auto kern = tgemv2_kernel<XT, AT, RT, RMS, MODE, WM, WK, NI>;
@@ -486,7 +528,12 @@ cudaError_t launch_v2(const TGemvParams& p, int Z, cudaStream_t st) {
 template <int XT, int AT, int RT, bool RMS, int MODE>
 cudaError_t pick_v2(const TGemvParams& p, int Z, cudaStream_t st) {
   const int iters_total = (p.nwords + 15) / 16;
-  if (iters_total <= 8) return launch_v2<XT, AT, RT, RMS, MODE, 4, 2, 4>(p, Z, st);
+  if (iters_total <= 8) {
+    // SwiGLU expert rows by bulk copies when the error word is there for the wait
+    TGemvParams q = p;
+    q.bulk_w = (MODE == kSwiglu && p.ids != nullptr && p.err != nullptr) ? 1 : 0;
+    return launch_v2<XT, AT, RT, RMS, MODE, 4, 2, 4>(q, Z, st);
+  }
   if (iters_total <= 16) return launch_v2<XT, AT, RT, RMS, MODE, 2, 4, 4>(p, Z, st);
   return launch_v2<XT, AT, RT, RMS, MODE, 2, 4, 8>(p, Z, st);
 }
@@ -586,7 +633,7 @@ extern "C" int maple_ternary_expert_swiglu(const void* x, int x_dtype, int64_t x
                                            int64_t k, const uint32_t* codes, int64_t n_experts,
                                            int64_t inter, const void* alpha, int alpha_dtype,
                                            void* y, int64_t y_row_stride, void* workspace,
-                                           int64_t workspace_bytes, void* stream) {
+                                           int64_t workspace_bytes, int* err, void* stream) {
   if (tokens < 0 || topk <= 0 || k < 0 || inter < 0 || n_experts <= 0) return kErrShape;
   if (tokens == 0 || inter == 0) return kOk;
   if (int rc = common_checks(x_dtype, alpha_dtype, nullptr, 0, k)) return rc;
@@ -599,7 +646,7 @@ extern "C" int maple_ternary_expert_swiglu(const void* x, int x_dtype, int64_t x
   p.x_stride = x_row_stride; p.y_stride = y_row_stride; p.x_div = (int)topk;
   p.rows = (int)(2 * inter); p.n_out = (int)inter; p.n_experts = (int)n_experts;
   p.expert_words = 2 * inter * (k / 16); p.alpha_estride = 2 * inter;
-  p.K = (int)k; p.nwords = (int)(k / 16);
+  p.K = (int)k; p.nwords = (int)(k / 16); p.err = err;
   (void)workspace; (void)workspace_bytes;
   const cudaError_t e = dispatch2<kSwiglu>(p, x_dtype, alpha_dtype, 0, (int)slots,
                                            static_cast<cudaStream_t>(stream));

@@ -361,7 +361,7 @@ def ternary_expert_swiglu(x, packed_weight, row_alpha, expert_ids, *, packed_kn:
     check(L.maple_ternary_expert_swiglu(
         ptr(xm), dtype_code(x, op), xm.stride(0), ptr(ids), tokens, topk, k_in, ptr(w), E, inter, ptr(alpha),
         dtype_code(alpha, op), ptr(y), inter, ptr(ws), ws.numel() if ws is not None else 0,
-        stream_ptr(x.device)), op)
+        ptr(_err(x.device)), stream_ptr(x.device)), op)
     return y.reshape(*id_shape, inter)
 
 
