@@ -244,17 +244,19 @@ int maple_ternary_expert_swiglu(const void* x, int x_dtype, int64_t x_row_stride
  * ternary_expert_down_sum and linear.py:59 PackedTernaryExperts.down_sum.
  * h: [tokens, topk, k] (strides h_tok_stride, h_slot_stride); ids/wt
  * [tokens, topk]; codes [n_experts, n, k/16]; residual [tokens, n] or NULL;
- * out [tokens, n].  topk <= 8, k <= 2048. */
+ * out [tokens, n].  topk <= 8, k <= 2048.  err: the device error word (bit 0 =
+ * a bounded wait on the bulk-staged expert rows ran out; that slot's rows are
+ * NaN); nullptr keeps per-thread row loads. */
 int maple_ternary_expert_down_reduce(const void* h, int h_dtype, int64_t h_tok_stride, int64_t h_slot_stride,
                                      const int32_t* ids, const float* wt, int64_t tokens, int64_t topk,
                                      int64_t k, const uint32_t* codes, int64_t n_experts, int64_t n,
                                      const void* alpha, int alpha_dtype, const void* residual,
-                                     int64_t res_stride, void* out, int64_t out_stride, void* stream);
+                                     int64_t res_stride, void* out, int64_t out_stride, int* err, void* stream);
 int maple_ternary_expert_down_sum(const void* h, int h_dtype, int64_t h_tok_stride, int64_t h_slot_stride,
                                   const int32_t* ids, const float* wt, int64_t tokens, int64_t topk, int64_t k,
                                   const uint32_t* codes, int64_t n_experts, int64_t n, const void* alpha,
                                   int alpha_dtype, const void* residual, int64_t res_stride, void* out,
-                                  int64_t out_stride, void* stream);
+                                  int64_t out_stride, int* err, void* stream);
 
 /* y = sum_s w[t,s] * x[t,s,:] (+ residual).  Replaces kernels/fused_norm.py:164
  * moe_reduce_add. */

@@ -80,9 +80,9 @@ _SIGS: dict[str, tuple] = {
     "maple_ternary_expert_swiglu": (i32, [vp, i32, i64, vp, i64, i64, i64, vp, i64, i64, vp, i32, vp, i64, vp,
                                           i64, vp, vp]),
     "maple_ternary_expert_down_reduce": (i32, [vp, i32, i64, i64, vp, vp, i64, i64, i64, vp, i64, i64, vp, i32,
-                                               vp, i64, vp, i64, vp]),
+                                               vp, i64, vp, i64, vp, vp]),
     "maple_ternary_expert_down_sum": (i32, [vp, i32, i64, i64, vp, vp, i64, i64, i64, vp, i64, i64, vp, i32,
-                                            vp, i64, vp, i64, vp]),
+                                            vp, i64, vp, i64, vp, vp]),
     "maple_moe_reduce_add": (i32, [vp, i32, i64, i64, vp, i64, i64, i64, vp, i64, vp, i64, vp]),
     "maple_router_topk_workspace_bytes": (i64, [i64, i64]),
     "maple_router_topk": (i32, [vp, i32, i64, i64, i64, vp, i32, i64, i64, vp, vp, vp, i64, vp]),

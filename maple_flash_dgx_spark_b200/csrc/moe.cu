@@ -7,6 +7,7 @@
 // moe_reduce_add   reference kernels/fused_norm.py:164-202
 #include <cooperative_groups.h>
 
+#include "bulk.cuh"
 #include "fxa.cuh"
 #include "launch.cuh"
 
@@ -266,6 +267,7 @@ struct DownParams {
   void* out;              // [T, N]
   int64_t h_tok_stride, h_slot_stride, res_stride, out_stride;
   int E, N, K, nwords, topk, iters;
+  int* err;               // device error word; non-null: expert rows staged by bulk copies
 };
 
 constexpr int kDownMaxIters = 8;
@@ -286,8 +288,17 @@ __global__ void __launch_bounds__(256, NI == 4 ? 3 : 1) down_sum_kernel(DownPara
   const int g = lane >> 2, t = lane & 3;
   const int tok = blockIdx.y;
   const int row_g = blockIdx.x * 16 + g, row_h = row_g + 8;
-  // compact digit fragments of this warp's slot row (fxa.cuh, direct form)
-  uint2* frag = reinterpret_cast<uint2*>(smem + warp * ((size_t)p.iters * 128 * sizeof(uint2)));
+  // Per warp: the compact digit fragments of its slot row (fxa.cuh, direct
+  // form), then (bulk) its expert's 16 code rows of this tile.  The rows are
+  // one contiguous 16 x K/4-byte block that one bulk copy brings in whole:
+  // per-thread 16-byte loads of them stall at issue while the SwiGLU launch
+  // this one overlaps still holds the SM's outstanding requests.
+  __shared__ uint64_t wbar[kDownMaxTopk];
+  const bool bulk = p.err != nullptr;
+  const unsigned rowb = (unsigned)p.nwords * 4u;
+  const size_t per_warp = (size_t)p.iters * 128 * sizeof(uint2) + (bulk ? (size_t)16 * rowb : 0);
+  uint2* frag = reinterpret_cast<uint2*>(smem + warp * per_warp);
+  unsigned char* wtile = smem + warp * per_warp + (size_t)p.iters * 128 * sizeof(uint2);
 
   // Routing ids come from two launches back (complete once the previous
   // launch has passed its own wait), so the expert rows load before waiting.
@@ -296,13 +307,22 @@ __global__ void __launch_bounds__(256, NI == 4 ? 3 : 1) down_sum_kernel(DownPara
     const bool bad = (e < 0 || e >= p.E);
     if (bad) e = 0;
     const uint32_t* codes = p.codes + (int64_t)e * p.N * p.nwords;
+    const int row0 = blockIdx.x * 16, nrows = min(16, p.N - row0);
+    if (bulk) {
+      if (lane == 0) {
+        mbar_init(&wbar[warp], 1);
+        mbar_expect_tx(&wbar[warp], (unsigned)nrows * rowb);
+        bulk_g2s(wtile, codes + (int64_t)row0 * p.nwords, (unsigned)nrows * rowb, &wbar[warp]);
+      }
+      __syncwarp();
+    }
     uint4 wa[NI], wb[NI];
 #pragma unroll
     for (int i = 0; i < NI; ++i) {
       wa[i] = make_uint4(0, 0, 0, 0);
       wb[i] = make_uint4(0, 0, 0, 0);
       const int word = i * 16 + 4 * t;
-      if (i < p.iters && word < p.nwords) {
+      if (!bulk && i < p.iters && word < p.nwords) {
         if (row_g < p.N) wa[i] = ld_stream_u4(codes + (int64_t)row_g * p.nwords + word);
         if (row_h < p.N) wb[i] = ld_stream_u4(codes + (int64_t)row_h * p.nwords + word);
       }
@@ -355,13 +375,31 @@ __global__ void __launch_bounds__(256, NI == 4 ? 3 : 1) down_sum_kernel(DownPara
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) tot[j] = __reduce_add_sync(0xffffffffu, tot[j]) - 64 * p.K;
+    bool lost = false;  // bulk rows that never landed: reported, the slot's rows become NaN
+    if (bulk) {
+      const bool ready = mbar_wait_bounded(&wbar[warp], 0);
+      if (!ready) {
+        lost = true;
+        if (lane == 0) atomicOr(p.err, kErrFlagTimeout);
+        mbar_wait_bounded(&wbar[warp], 0);  // let the copy land before the CTA can exit
+      } else {
+#pragma unroll
+        for (int i = 0; i < NI; ++i) {
+          const int word = i * 16 + 4 * t;
+          if (i < p.iters && word < p.nwords) {
+            if (g < nrows) wa[i] = *reinterpret_cast<const uint4*>(wtile + (size_t)g * rowb + 4 * word);
+            if (g + 8 < nrows) wb[i] = *reinterpret_cast<const uint4*>(wtile + (size_t)(g + 8) * rowb + 4 * word);
+          }
+        }
+      }
+    }
     __syncwarp();
     int acc[4] = {0, 0, 0, 0};
     contract_tile2c<NI>(wa, wb, p.iters, frag, lane, acc);
     long long Sg, Sh;
     combine_digits(acc, tot, t, Sg, Sh);
     if (t == 0) {
-      const bool nan_out = bad || s == kFxaNonFinite;
+      const bool nan_out = bad || lost || s == kFxaNonFinite;
       const float nanv = __int_as_float(0x7fc00000);
       const float vg = nan_out ? nanv : fxa_value(Sg, s);
       const float vh = nan_out ? nanv : fxa_value(Sh, s);
@@ -526,7 +564,8 @@ extern "C" int maple_add_norm_router_topk(const void* x, const void* y, int x_dt
 namespace {
 template <int XT, int AT, int MODE>
 cudaError_t launch_down(const DownParams& p, int T, cudaStream_t st) {
-  const size_t per_warp = (size_t)p.iters * 128 * sizeof(uint2);  // compact fragments
+  // compact fragments (+ the bulk-staged code rows)
+  const size_t per_warp = (size_t)p.iters * 128 * sizeof(uint2) + (p.err ? (size_t)16 * p.nwords * 4 : 0);
   const size_t smem = per_warp * kDownMaxTopk;
   auto kern = p.iters <= 4 ? down_sum_kernel<XT, AT, MODE, 4> : down_sum_kernel<XT, AT, MODE, kDownMaxIters>;
   if (smem > 32 * 1024) {
@@ -547,7 +586,7 @@ int down_entry(const void* h, int h_dtype, int64_t h_tok_stride, int64_t h_slot_
                const int32_t* ids, const float* wt, int64_t tokens, int64_t topk, int64_t k,
                const uint32_t* codes, int64_t n_experts, int64_t n, const void* alpha,
                int alpha_dtype, const void* residual, int64_t res_stride, void* out,
-               int64_t out_stride, void* stream) {
+               int64_t out_stride, int* err, void* stream) {
   if (tokens < 0 || topk <= 0 || k <= 0 || n < 0 || n_experts <= 0) return kErrShape;
   if (tokens == 0 || n == 0) return kOk;
   if (topk > kDownMaxTopk || k % 64 != 0 || k > kDownMaxIters * 256 || tokens > 65535) return kErrShape;
@@ -558,7 +597,7 @@ int down_entry(const void* h, int h_dtype, int64_t h_tok_stride, int64_t h_slot_
   p.h = h; p.ids = ids; p.wt = wt; p.codes = codes; p.alpha = alpha; p.residual = residual; p.out = out;
   p.h_tok_stride = h_tok_stride; p.h_slot_stride = h_slot_stride; p.res_stride = res_stride;
   p.out_stride = out_stride; p.E = (int)n_experts; p.N = (int)n; p.K = (int)k; p.nwords = (int)(k / 16);
-  p.topk = (int)topk; p.iters = (int)((k + 255) / 256);
+  p.topk = (int)topk; p.iters = (int)((k + 255) / 256); p.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (h_dtype == kBF16)
@@ -577,9 +616,9 @@ extern "C" int maple_ternary_expert_down_reduce(const void* h, int h_dtype, int6
                                                 int64_t k, const uint32_t* codes, int64_t n_experts,
                                                 int64_t n, const void* alpha, int alpha_dtype,
                                                 const void* residual, int64_t res_stride, void* out,
-                                                int64_t out_stride, void* stream) {
+                                                int64_t out_stride, int* err, void* stream) {
   return down_entry<0>(h, h_dtype, h_tok_stride, h_slot_stride, ids, wt, tokens, topk, k, codes,
-                       n_experts, n, alpha, alpha_dtype, residual, res_stride, out, out_stride, stream);
+                       n_experts, n, alpha, alpha_dtype, residual, res_stride, out, out_stride, err, stream);
 }
 
 extern "C" int maple_ternary_expert_down_sum(const void* h, int h_dtype, int64_t h_tok_stride,
@@ -588,9 +627,9 @@ extern "C" int maple_ternary_expert_down_sum(const void* h, int h_dtype, int64_t
                                              int64_t k, const uint32_t* codes, int64_t n_experts,
                                              int64_t n, const void* alpha, int alpha_dtype,
                                              const void* residual, int64_t res_stride, void* out,
-                                             int64_t out_stride, void* stream) {
+                                             int64_t out_stride, int* err, void* stream) {
   return down_entry<1>(h, h_dtype, h_tok_stride, h_slot_stride, ids, wt, tokens, topk, k, codes,
-                       n_experts, n, alpha, alpha_dtype, residual, res_stride, out, out_stride, stream);
+                       n_experts, n, alpha, alpha_dtype, residual, res_stride, out, out_stride, err, stream);
 }
 
 extern "C" int maple_moe_reduce_add(const void* x, int x_dtype, int64_t x_tok_stride,

@@ -388,7 +388,8 @@ def _down(x, packed_weight, row_alpha, expert_ids, topk_weight, residual, packed
         res = residual.reshape(tokens, N).contiguous()
     y = torch.empty(tokens, N, device=x.device, dtype=x.dtype)
     check(fn(ptr(xm), dtype_code(x, op), topk * k_in, k_in, ptr(ids), ptr(wts), tokens, topk, k_in, ptr(w), E, N,
-             ptr(alpha), dtype_code(alpha, op), ptr(res), N, ptr(y), N, stream_ptr(x.device)), op)
+             ptr(alpha), dtype_code(alpha, op), ptr(res), N, ptr(y), N, ptr(_err(x.device)), stream_ptr(x.device)),
+          op)
     return y.reshape(*expert_ids.shape[:-1], N)
 
 
